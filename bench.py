@@ -1,0 +1,307 @@
+"""Benchmark: bs1 greedy decode of the Qwen3-8B-architecture W8A16 model.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+One step = one decode token through embed -> 36 W8A16 decoder layers
+(RMSNorm + fused QKV GEMV + q/k-norm + RoPE + paged split-KV attention +
+o_proj + fused gate/up SwiGLU + down) -> ln_f -> bf16 lm_head -> argmax.
+Weights are seeded random-init N(0, 0.02) bf16 quantized to int8 at load
+(8.2 GB streamed per token, far larger than L2); the context starts from a
+128-token prompt (seed 1) prefilled before timing.
+
+``value`` is tok/s of the device-resident decode loop (CUDA-graph replays,
+CUDA events on the engine stream).  ``e2e`` is the same metric through the
+public C ABI call dial_b200_decode_step with host token buffers (H2D of the
+token/session/position, D2H of the next token + status inside the timed
+region).  ``roofline`` reports the dominant kernel (the fused gate/up W8A16
+GEMV) timed live with CUDA events on the engine stream.  With --gpus N > 1
+(torchrun) the 36 layers are split into N pipeline stages that hand the
+hidden state to the next GPU with NCCL send/recv.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "dial-27b_b200"))
+
+PROMPT_LEN = 128
+WORKLOAD = "qwen3-8b-w8a16-bs1-decode"
+
+
+def load_peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": d["hbm_gbs"], "source": "measured"}
+    return {"hbm_gbs": 6650.0, "source": "fallback"}
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self._t = threading.Thread(target=self._read, daemon=True)
+            self._t.start()
+        except FileNotFoundError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for name, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ----------------------------------------------------------------- CPU leg
+def cpu_decode_sample(budget_s: float = 20.0) -> dict:
+    """Time the CPU oracle on a bounded sample of the same decode step: whole
+    decoder layers of Qwen3-8B shape (W8A16, one token at context 128) plus
+    one lm_head, scaled to a full 36-layer token."""
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import numpy as np
+
+    import dial_oracle as O
+
+    cfg = O.ModelConfig(layers=1)
+    table = O.normal_table(0.02)
+    H, I, D = cfg.hidden, cfg.inter, cfg.head_dim
+    rng = np.random.default_rng(0)
+
+    def qw(n, k, stream):
+        return O.quantize_w8a16_rows(O.synth_normal(0, stream, n * k, table).reshape(n, k))
+
+    qkv = qw(cfg.heads * D + 2 * cfg.kv_heads * D, H, 0x100)
+    o = qw(H, H, 0x103)
+    gu = qw(2 * I, H, 0x104)
+    dn = qw(H, I, 0x106)
+    one = lambda n: np.ones(n, np.float32)  # noqa: E731
+    lw = O.LayerWeights(*qkv, *o, *gu, *dn, one(H), one(H), one(D), one(D))
+    cos, sin = O.rope_tables(D, 512, cfg.rope_theta)
+    cache = O.Cache(1, 512)
+    ctx = PROMPT_LEN
+    kv = O.bf16_round(rng.standard_normal((1, cfg.kv_heads, ctx, D)).astype(np.float32))
+    cache.process_kv(0, 0, kv, kv.copy())
+    x = O.bf16_round(rng.standard_normal((1, H)).astype(np.float32))
+    lm = O.synth_normal(0, 0xE0002, 8192 * H, table).reshape(8192, H)
+    t_layer, n_layer = 0.0, 0
+    t0 = time.perf_counter()
+    while time.perf_counter() - t0 < budget_s or n_layer < 2:
+        a = time.perf_counter()
+        O.layer_forward(x, lw, cfg, ctx + n_layer, 0, cache, cos, sin)
+        t_layer += time.perf_counter() - a
+        n_layer += 1
+        if n_layer >= 64:
+            break
+    a = time.perf_counter()
+    O.dense_linear(x, lm)
+    t_head = (time.perf_counter() - a) * (cfg.vocab / 8192)
+    per_token = 36 * t_layer / n_layer + t_head
+    cores = len(os.sched_getaffinity(0))
+    return {"value": 1.0 / per_token, "unit": "tok/s", "cores": cores, "kind": "port",
+            "sample": f"{n_layer} single-token W8A16 decoder layers of Qwen3-8B shape at context "
+                      f"{PROMPT_LEN} + an 8192-row slice of the bf16 lm_head, numpy oracle "
+                      f"(dial_oracle.py), scaled to 36 layers + full vocab"}
+
+
+def run_reference(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    budget = max(2.0, 60.0 / max(1, args.steps + args.warmup))
+    vals = []
+    for i in range(args.warmup + args.steps):
+        r = cpu_decode_sample(budget_s=budget)
+        if i >= args.warmup:
+            vals.append(r["value"])
+    v = statistics.median(vals)
+    line = {"impl": "reference", "metric": "decode tok/s (bs1, Qwen3-8B W8A16)", "value": v,
+            "unit": "tok/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": 1000.0 / v, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": WORKLOAD, "prompt_len": PROMPT_LEN, "batch": 1},
+            "cpu_baseline": {**r, "value": v},
+            "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------------- GPU leg
+def run_single(args) -> dict:
+    import numpy as np
+    import torch
+
+    import dial_b200
+    from dial_b200.synth import STREAM_TOKENS  # noqa: F401
+
+    dev = 0
+    torch.cuda.set_device(dev)
+    cfg = dial_b200.Config(max_seq_len=4096, max_sessions=1, max_tokens=PROMPT_LEN)
+    eng = dial_b200.Engine(cfg, device=dev)
+    eng.load_synthetic(seed=0)
+    sys.path.insert(0, str(ROOT / "oracle"))
+    prompt = _prompt_tokens(cfg.vocab_size)
+    first, ttft, _ = eng.generate(prompt, 1)
+    stream = eng.stream
+    pos = PROMPT_LEN
+    tok = int(first[0])
+
+    # ---- e2e through the public C ABI (host buffers, synchronous per step)
+    for _ in range(args.warmup):
+        tok = int(eng.decode_step([tok], [0], [pos])[0])
+        pos += 1
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        tok = int(eng.decode_step([tok], [0], [pos])[0])
+        pos += 1
+    e2e_s = time.perf_counter() - t0
+
+    # ---- device-resident loop (graph replays, tokens fed back on device)
+    eng.loop_prepare([tok], [0], [pos])
+    eng.loop_run(1, args.warmup)
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(dev) as clk:
+        time.sleep(0.3)
+        ev0.record(stream)
+        eng.loop_run(1, args.steps)
+        ev1.record(stream)
+        ev1.synchronize()
+    step_ms = ev0.elapsed_time(ev1) / args.steps
+    toks, positions = eng.loop_state(1)
+
+    # ---- dominant kernel live: fused gate/up GEMV, same launch config
+    iters = 50
+    eng.linear_replay(0, 2, 1, 5)
+    torch.cuda.synchronize()
+    ev0.record(stream)
+    eng.linear_replay(0, 2, 1, iters)
+    ev1.record(stream)
+    ev1.synchronize()
+    k_us = ev0.elapsed_time(ev1) * 1000.0 / iters
+    k_bytes = eng.linear_bytes(0, 2, 1)
+    step_bytes = sum(eng.linear_bytes(0, w, 1) for w in range(4)) * cfg.num_hidden_layers + \
+        eng.linear_bytes(0, 4, 1) + 36 * 2 * 8 * 128 * 2 * (pos + args.steps)
+    peaks = load_peaks()
+    achieved = k_bytes / (k_us * 1e-6) / 1e9
+    status = dial_b200.device_status()
+    return {
+        "value": 1000.0 / step_ms, "ms_per_step": step_ms, "e2e_tok_s": args.steps / e2e_s,
+        "ttft_s": ttft, "clocks": clk.summary(), "status": status,
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": achieved / peaks["hbm_gbs"], "traffic": None,
+                     "kernel": "gemv_kernel<bf16,W8A16,SwiGLU,norm> (fused gate/up, N=24576 K=4096 M=1)",
+                     "launch_us": k_us, "bytes_per_launch": k_bytes, "peak_source": peaks["source"],
+                     "step_bytes": step_bytes,
+                     "step_frac": step_bytes / (step_ms * 1e-3) / 1e9 / peaks["hbm_gbs"]},
+        "gpu_launches": (eng.step_kernel_count(1) + 1) * args.steps,
+        "final_token": int(toks[0]), "final_pos": int(positions[0]),
+    }
+
+
+def _prompt_tokens(vocab: int):
+    import numpy as np
+
+    from dial_b200.synth import STREAM_TOKENS
+
+    # seed-1 uniform ids; same hash as the device generator (layout.cu)
+    def mix64(z):
+        z = (z ^ (z >> np.uint64(30))) * np.uint64(0xBF58476D1CE4E5B9)
+        z = (z ^ (z >> np.uint64(27))) * np.uint64(0x94D049BB133111EB)
+        return z ^ (z >> np.uint64(31))
+
+    seed = 1
+    base = np.uint64(((seed * 0x9E3779B97F4A7C15) ^ (STREAM_TOKENS * 0xD1B54A32D192ED03)) & ((1 << 64) - 1))
+    with np.errstate(over="ignore"):
+        h = mix64(np.arange(PROMPT_LEN, dtype=np.uint64) + base)
+    return (h % np.uint64(vocab)).astype(np.int32)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=64)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+        return
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if world > 1 or args.gpus > 1:
+        import bench_pipeline
+
+        bench_pipeline.run(args, WORKLOAD, PROMPT_LEN, load_peaks, ClockSampler, cpu_decode_sample)
+        return
+    r = run_single(args)
+    cpu = None if args.no_cpu_baseline else cpu_decode_sample()
+    line = {
+        "metric": "decode tok/s (bs1, Qwen3-8B W8A16)", "value": r["value"], "unit": "tok/s",
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": r["ms_per_step"],
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic",
+        "config": {"workload": WORKLOAD, "prompt_len": PROMPT_LEN, "batch": 1,
+                   "layers": 36, "hidden": 4096, "linear": "W8A16 row int8 + f32 scale",
+                   "lm_head": "bf16 dense", "parallelism": "single GPU",
+                   "l2": "inputs larger than L2 (8.2 GB weights streamed per step)"},
+        "e2e": {"value": r["e2e_tok_s"], "unit": "tok/s", "h2d_bytes_per_step": 12,
+                "d2h_bytes_per_step": 8},
+        "roofline": r["roofline"], "cpu_baseline": cpu, "clocks": r["clocks"],
+        "gpu_launches": r["gpu_launches"], "ttft_s": r["ttft_s"], "device_status": r["status"],
+    }
+    print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,75 @@
+// Host interface of the attention kernels (attention.cu).
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace dialb200 {
+
+constexpr int kPageTokens = 16;  // tokens per paged-KV block
+
+// Paged KV pool of one layer: [num_blocks][kv_heads][16][head_dim] (act dtype).
+struct KvLayer {
+  void* k;
+  void* v;
+};
+
+struct AttnShape {
+  int q_heads, kv_heads, head_dim;
+  int max_blocks;      // block-table row length
+  int max_pos;         // rows of the cos/sin tables
+  float eps;
+};
+
+// Decode: M rows, each one new token of session sid[m] at position pos[m].
+struct AttnDecodeArgs {
+  AttnShape sh;
+  const void* qkv;           // [M][qkv_ld]: q | k | v (pre-norm, pre-RoPE)
+  int qkv_ld;
+  const void* q_norm_w;      // [head_dim]
+  const void* k_norm_w;      // [head_dim]
+  const void* cos;           // [max_pos][head_dim/2]
+  const void* sin;
+  KvLayer kv;
+  const int32_t* block_table;// [num_sessions][max_blocks]
+  const int32_t* sid;        // [M]
+  const int32_t* pos;        // [M]
+  void* out;                 // [M][q_heads*head_dim]
+  int out_ld;
+  int M;
+  int splits;                // KV splits per (row, kv head); 1 = no scratch use.
+                             // Each row's context is cut into `splits` equal
+                             // 16-token-aligned spans at run time.
+  float* part_o;             // [M][q_heads][splits][head_dim]
+  float* part_ml;            // [M][q_heads][splits][2]
+  int* counters;             // [M][kv_heads], zero on entry, left zero on exit
+  int* status;
+};
+
+// Scratch bytes needed for (M, splits).
+size_t attn_decode_scratch_bytes(const AttnShape& sh, int M, int splits);
+
+cudaError_t attn_decode_launch(const AttnDecodeArgs& a, int act, cudaStream_t s, bool pdl);
+
+// Prefill of one session: M tokens at positions p0 .. p0+M-1.
+struct AttnPrefillArgs {
+  AttnShape sh;
+  const void* qkv;
+  int qkv_ld;
+  const void* q_norm_w;
+  const void* k_norm_w;
+  const void* cos;
+  const void* sin;
+  KvLayer kv;
+  const int32_t* block_table;  // this session's row [max_blocks]
+  int p0;
+  int M;
+  int32_t* rows_scratch;       // [2*M] int32 scratch (per-row positions, sessions)
+  void* out;                   // [M][q_heads*head_dim]
+  int out_ld;
+  int* status;
+};
+
+cudaError_t attn_prefill_launch(const AttnPrefillArgs& a, int act, cudaStream_t s, bool pdl);
+
+}  // namespace dialb200

@@ -1,0 +1,551 @@
+// Decode-path linear (M <= 8 tokens per launch): a memory-bound, dequant-fused
+// GEMV for the weight formats of DIAL's worker linears.
+//
+// Reference kernels this replaces (all in lisa301/DIAL-27B):
+//   dial_w8a16_decode_f16   dial-core/src/models/qwen3_vl/worker_w8a16.rs:146-184
+//   dial_fp8_decode_f16     dial-core/src/models/qwen3_8/cuda_quant.rs:102-133
+//   dial_nvfp4_decode_f16   dial-core/src/models/qwen3_8/cuda_quant.rs:67-100
+// plus the dense candle Linear used for the lm_head (qwen3_vl.rs:1325-1335).
+//
+// Design (one CTA per SM, 8 consumer warps + 1 producer warp):
+//  * The producer streams the CTA's contiguous range of 16-row weight tiles
+//    through a shared-memory ring with 1-D bulk async copies (TMA engine),
+//    16 chunks (16-18 KB) per stage, completion tracked on mbarriers.  It
+//    starts before griddepcontrol.wait, so weight streaming overlaps the tail
+//    of the previous kernel (programmatic dependent launch).
+//  * Activations are staged once per CTA in shared memory as f16 (with a
+//    power-of-two pre-scale that keeps bf16 values exact and in range); the
+//    RMSNorm that precedes the QKV and gate/up projections is computed here.
+//  * Each lane converts its own weight bytes into m16n8k16 A fragments in
+//    registers (int8: PRMT+HSUB2, e4m3/e2m1: hardware cvt) and issues
+//    register-fed MMAs with f32 accumulation; the K order inside a chunk is
+//    permuted identically for weights and activations.
+//  * Per-tile partial sums of the 8 warps are reduced in shared memory and
+//    the epilogue applies the row scale and one of: store, residual add
+//    (o_proj/down), or SiLU(gate)*up (fused gate/up projection).
+#include "common.cuh"
+#include "gemv.h"
+
+namespace dialb200 {
+namespace {
+
+constexpr int kNW = 8;                      // consumer warps
+constexpr int kThreads = (kNW + 1) * 32;    // + producer warp
+constexpr int kStageChunks = 16;
+constexpr int kMaxSlots = 16;
+constexpr int kMaxM = 8;
+constexpr int kSmemBudget = 232448;         // 227 KB opt-in per CTA
+
+struct SmemPlan {
+  int ring_off, x_off, red_off, misc_off, bsc_off, bar_off, total;
+  int slots, xs_stride, bsc_rows_lo, bsc_rows_hi;
+};
+
+// Block-scale row ranges a CTA needs for tiles [t0, t1).
+__host__ __device__ inline void bsc_rows(const DevQLinear& w, int t0, int t1, int& lo0, int& nlo,
+                                         int& hi0, int& nhi) {
+  if (t1 <= t0) { lo0 = nlo = hi0 = nhi = 0; return; }
+  if (w.swiglu) {
+    const int I = w.N / 2;
+    lo0 = (8 * t0) / 128;
+    nlo = (8 * (t1 - 1)) / 128 - lo0 + 1;
+    hi0 = (I + 8 * t0) / 128;
+    nhi = (I + 8 * (t1 - 1)) / 128 - hi0 + 1;
+  } else {
+    lo0 = (16 * t0) / 128;
+    nlo = (16 * (t1 - 1) + 15) / 128 - lo0 + 1;
+    hi0 = 0;
+    nhi = 0;
+  }
+}
+
+__host__ inline SmemPlan make_plan(const DevQLinear& w, int M, int grid, int slots_req) {
+  SmemPlan p{};
+  const int stage = kStageChunks * fmt_chunk_bytes(w.fmt);
+  p.xs_stride = w.K_pad + 8;
+  const int x_bytes = ((M * p.xs_stride * 2) + 127) / 128 * 128;
+  const int red_bytes = 2 * kNW * 32 * 4 * 4;
+  const int misc_bytes = 256;
+  int bsc_bytes = 0;
+  if (w.fmt == kFmtFp8Block128) {
+    // worst case over CTAs: tiles per CTA <= ceil(T/grid)
+    const int tpc = (w.T + grid - 1) / grid;
+    const int rows_lo = w.swiglu ? (8 * tpc + 127) / 128 + 1 : (16 * tpc + 127) / 128 + 1;
+    const int rows_hi = w.swiglu ? rows_lo : 0;
+    p.bsc_rows_lo = rows_lo;
+    p.bsc_rows_hi = rows_hi;
+    bsc_bytes = (rows_lo + rows_hi) * w.blk_ld * 4;
+    bsc_bytes = (bsc_bytes + 127) / 128 * 128;
+  }
+  const int bar_bytes = (2 * kMaxSlots + 2) * 8;
+  const int fixed = x_bytes + red_bytes + misc_bytes + bsc_bytes + bar_bytes + 1024;
+  int slots = (kSmemBudget - fixed) / stage;
+  if (slots > kMaxSlots) slots = kMaxSlots;
+  if (slots_req > 0 && slots_req < slots) slots = slots_req;
+  p.slots = slots;
+  p.ring_off = 0;
+  p.x_off = slots * stage;
+  p.red_off = p.x_off + x_bytes;
+  p.misc_off = p.red_off + red_bytes;
+  p.bsc_off = p.misc_off + misc_bytes;
+  p.bar_off = p.bsc_off + bsc_bytes;
+  p.total = p.bar_off + bar_bytes;
+  return p;
+}
+
+template <int FMT>
+struct XType { using T = __half; };
+
+// --------------------------------------------------------------- x staging
+template <typename Act, typename XT, bool NORM, bool SCALE>
+__device__ void stage_x(const GemvArgs& a, XT* xs, int xs_stride, int* xexp, float* scratch) {
+  using AT = ActTraits<Act>;
+  const int tid = threadIdx.x;
+  constexpr int NT = kNW * 32;
+  const int K = a.w.K, Kp = a.w.K_pad;
+  const Act* nw = reinterpret_cast<const Act*>(a.norm_w);
+  const int warp = tid >> 5, lane = tid & 31;
+
+  float wmax = 1.f;
+  if (NORM && SCALE) {
+    float m = 0.f;
+    for (int k = tid; k < K; k += NT) m = fmaxf(m, fabsf(AT::to_f(nw[k])));
+    m = warp_max(m);
+    if (lane == 0) scratch[warp] = m;
+    named_bar_sync(1, NT);
+    m = 0.f;
+#pragma unroll
+    for (int i = 0; i < kNW; ++i) m = fmaxf(m, scratch[i]);
+    wmax = m;
+    named_bar_sync(1, NT);
+  }
+  for (int r = 0; r < a.M; ++r) {
+    const Act* xr = reinterpret_cast<const Act*>(a.x) + static_cast<size_t>(r) * a.x_ld;
+    float ss = 0.f, am = 0.f;
+    for (int k = tid; k < K; k += NT) {
+      const float v = AT::to_f(xr[k]);
+      ss = fmaf(v, v, ss);
+      am = fmaxf(am, fabsf(v));
+    }
+    ss = warp_sum(ss);
+    am = warp_max(am);
+    if (lane == 0) {
+      scratch[warp] = ss;
+      scratch[kNW + warp] = am;
+    }
+    named_bar_sync(1, NT);
+    ss = 0.f;
+    am = 0.f;
+#pragma unroll
+    for (int i = 0; i < kNW; ++i) {
+      ss += scratch[i];
+      am = fmaxf(am, scratch[kNW + i]);
+    }
+    named_bar_sync(1, NT);
+    float rms = 1.f;
+    if (NORM) rms = AT::round(__fsqrt_rn(__fdiv_rn(ss, static_cast<float>(K)) + a.eps));
+    int e = 0;
+    if (SCALE) {
+      const float bound = NORM ? __fdiv_rn(am, rms) * wmax * 1.02f : am;
+      if (bound >= 16384.f) e = ilogbf(bound) - 13;
+    }
+    const float sc = exp2i(-e);
+    XT* xrow = xs + static_cast<size_t>(r) * xs_stride;
+    for (int k = tid; k < Kp; k += NT) {
+      float v = 0.f;
+      if (k < K) {
+        v = AT::to_f(xr[k]);
+        if (NORM) {
+          v = AT::round(__fdiv_rn(v, rms));
+          v = AT::round(v * AT::to_f(nw[k]));
+        }
+      }
+      if constexpr (sizeof(XT) == 2 && std::is_same<XT, __half>::value) {
+        xrow[k] = __float2half_rn(v * sc);
+      } else {
+        xrow[k] = ActTraits<XT>::from_f(v);
+      }
+    }
+    if (tid == 0) xexp[r] = e;
+  }
+}
+
+// ---------------------------------------------------------- chunk compute
+// acc: 16 rows x 8 tokens C fragment.  xrow: this lane's token row in smem.
+template <int FMT, typename XT>
+__device__ __forceinline__ void chunk_mma(const uint8_t* st, int kc, const XT* xrow, int lane,
+                                          float (&acc)[4]) {
+  const int c = lane & 3;
+  if constexpr (FMT == kFmtW8A16Row || FMT == kFmtFp8Row || FMT == kFmtFp8Block128) {
+    const uint4 w0 = *reinterpret_cast<const uint4*>(st + lane * 16);
+    const uint4 w1 = *reinterpret_cast<const uint4*>(st + 512 + lane * 16);
+    const XT* xp = xrow + kc * 64 + c * 16;
+    const uint4 xa = *reinterpret_cast<const uint4*>(xp);
+    const uint4 xb = *reinterpret_cast<const uint4*>(xp + 8);
+    const uint32_t xw[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
+    const uint32_t wa[4] = {w0.x, w0.y, w0.z, w0.w};
+    const uint32_t wb[4] = {w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+    for (int s = 0; s < 4; ++s) {
+      uint32_t A[4];
+      if constexpr (FMT == kFmtW8A16Row) {
+        A[0] = i8_lo_pair(wa[s]);
+        A[1] = i8_lo_pair(wb[s]);
+        A[2] = i8_hi_pair(wa[s]);
+        A[3] = i8_hi_pair(wb[s]);
+      } else {
+        A[0] = e4m3x2_to_f16x2(static_cast<uint16_t>(wa[s] & 0xffffu));
+        A[1] = e4m3x2_to_f16x2(static_cast<uint16_t>(wb[s] & 0xffffu));
+        A[2] = e4m3x2_to_f16x2(static_cast<uint16_t>(wa[s] >> 16));
+        A[3] = e4m3x2_to_f16x2(static_cast<uint16_t>(wb[s] >> 16));
+      }
+      mma_f16(acc, A, xw[2 * s], xw[2 * s + 1]);
+    }
+  } else if constexpr (FMT == kFmtNvfp4G16) {
+    const uint4 w0 = *reinterpret_cast<const uint4*>(st + lane * 16);
+    const uint4 w1 = *reinterpret_cast<const uint4*>(st + 512 + lane * 16);
+    const uint16_t s0 = *reinterpret_cast<const uint16_t*>(st + 1024 + lane * 2);
+    const uint16_t s1 = *reinterpret_cast<const uint16_t*>(st + 1024 + 64 + lane * 2);
+    const uint32_t sg0 = e4m3x2_to_f16x2(s0);  // row g   : groups (2c, 2c+1)
+    const uint32_t sg1 = e4m3x2_to_f16x2(s1);  // row g+8
+    const __half2 sc0[2] = {__low2half2(*reinterpret_cast<const __half2*>(&sg0)),
+                            __high2half2(*reinterpret_cast<const __half2*>(&sg0))};
+    const __half2 sc1[2] = {__low2half2(*reinterpret_cast<const __half2*>(&sg1)),
+                            __high2half2(*reinterpret_cast<const __half2*>(&sg1))};
+    const uint32_t wa[4] = {w0.x, w0.y, w0.z, w0.w};
+    const uint32_t wb[4] = {w1.x, w1.y, w1.z, w1.w};
+    const XT* xp = xrow + kc * 128 + c * 32;
+#pragma unroll
+    for (int s = 0; s < 4; ++s) {
+      uint32_t oa[4], ob[4];
+      e2m1x8_to_f16x2x4(wa[s], oa);
+      e2m1x8_to_f16x2x4(wb[s], ob);
+      const int gj = s >> 1;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        __half2 ha = __hmul2(*reinterpret_cast<__half2*>(&oa[q]), sc0[gj]);
+        __half2 hb = __hmul2(*reinterpret_cast<__half2*>(&ob[q]), sc1[gj]);
+        oa[q] = *reinterpret_cast<uint32_t*>(&ha);
+        ob[q] = *reinterpret_cast<uint32_t*>(&hb);
+      }
+      const uint4 xv = *reinterpret_cast<const uint4*>(xp + 8 * s);
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const uint32_t A[4] = {oa[2 * h], ob[2 * h], oa[2 * h + 1], ob[2 * h + 1]};
+        const uint32_t b0 = h ? xv.z : xv.x;
+        const uint32_t b1 = h ? xv.w : xv.y;
+        mma_f16(acc, A, b0, b1);
+      }
+    }
+  } else {  // dense act-dtype weights
+    const uint4 w0 = *reinterpret_cast<const uint4*>(st + lane * 16);
+    const uint4 w1 = *reinterpret_cast<const uint4*>(st + 512 + lane * 16);
+    const XT* xp = xrow + kc * 32 + c * 8;
+    const uint4 xv = *reinterpret_cast<const uint4*>(xp);
+    const uint32_t A0[4] = {w0.x, w1.x, w0.y, w1.y};
+    const uint32_t A1[4] = {w0.z, w1.z, w0.w, w1.w};
+    if constexpr (std::is_same<XT, __nv_bfloat16>::value) {
+      mma_bf16(acc, A0, xv.x, xv.y);
+      mma_bf16(acc, A1, xv.z, xv.w);
+    } else {
+      mma_f16(acc, A0, xv.x, xv.y);
+      mma_f16(acc, A1, xv.z, xv.w);
+    }
+  }
+}
+
+template <typename Act>
+__device__ __forceinline__ float silu_mul_ref(float g, float u) {
+  using AT = ActTraits<Act>;
+  // act(act(g / act(1 + act(exp(-g)))) * u)  (text.rs:816-820 via candle silu)
+  const float e = AT::round(expf(-g));
+  const float d = AT::round(1.f + e);
+  const float s = AT::round(__fdiv_rn(g, d));
+  return s * u;
+}
+
+// ------------------------------------------------------------------ kernel
+template <typename Act, int FMT, int EPI, bool NORM>
+__global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const GemvArgs a, const SmemPlan p) {
+  using AT = ActTraits<Act>;
+  using XT = typename std::conditional<FMT == kFmtDense, Act, __half>::type;
+  constexpr bool kScaleX = (FMT != kFmtDense) && std::is_same<Act, __nv_bfloat16>::value;
+  constexpr int CB = fmt_chunk_bytes(FMT);
+  constexpr int kStageBytes = kStageChunks * CB;
+
+  extern __shared__ __align__(1024) uint8_t smem[];
+  uint8_t* ring = smem + p.ring_off;
+  XT* xs = reinterpret_cast<XT*>(smem + p.x_off);
+  float* red = reinterpret_cast<float*>(smem + p.red_off);
+  int* xexp = reinterpret_cast<int*>(smem + p.misc_off);
+  float* scratch = reinterpret_cast<float*>(smem + p.misc_off + 64);
+  float* bsc = reinterpret_cast<float*>(smem + p.bsc_off);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + p.bar_off);
+  uint64_t* empty = full + kMaxSlots;
+  uint64_t* sbar = empty + kMaxSlots;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int T = a.w.T, C = a.w.C;
+  const int t0 = static_cast<int>(static_cast<long long>(T) * blockIdx.x / gridDim.x);
+  const int t1 = static_cast<int>(static_cast<long long>(T) * (blockIdx.x + 1) / gridDim.x);
+  const int spt = (C + kStageChunks - 1) / kStageChunks;
+  const int NS = p.slots;
+
+  int lo0 = 0, nlo = 0, hi0 = 0, nhi = 0;
+  if constexpr (FMT == kFmtFp8Block128) bsc_rows(a.w, t0, t1, lo0, nlo, hi0, nhi);
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < NS; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], kNW);
+    }
+    mbar_init(sbar, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  pdl_launch_dependents();
+
+  if (warp == kNW) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      if constexpr (FMT == kFmtFp8Block128) {
+        const uint32_t row_bytes = static_cast<uint32_t>(a.w.blk_ld) * 4u;
+        mbar_arrive_expect_tx(sbar, row_bytes * static_cast<uint32_t>(nlo + nhi));
+        if (nlo) bulk_g2s(bsc, a.w.blk_scale + static_cast<size_t>(lo0) * a.w.blk_ld,
+                          row_bytes * nlo, sbar);
+        if (nhi) bulk_g2s(bsc + static_cast<size_t>(nlo) * a.w.blk_ld,
+                          a.w.blk_scale + static_cast<size_t>(hi0) * a.w.blk_ld, row_bytes * nhi,
+                          sbar);
+      }
+      long long it = 0;
+      bool ok = true;
+      for (int t = t0; t < t1 && ok; ++t) {
+        const uint8_t* src = a.w.tiles + static_cast<size_t>(t) * C * CB;
+        for (int s = 0; s < spt; ++s, ++it) {
+          const int slot = static_cast<int>(it % NS);
+          const uint32_t round = static_cast<uint32_t>(it / NS);
+          if (round > 0 && !mbar_wait(&empty[slot], (round - 1) & 1u, a.status,
+                                      kStatusEmptyWaitTimeout)) {
+            ok = false;
+            break;
+          }
+          const int nch = min(kStageChunks, C - s * kStageChunks);
+          const uint32_t bytes = static_cast<uint32_t>(nch * CB);
+          mbar_arrive_expect_tx(&full[slot], bytes);
+          bulk_g2s(ring + static_cast<size_t>(slot) * kStageBytes,
+                   src + static_cast<size_t>(s) * kStageChunks * CB, bytes, &full[slot]);
+        }
+      }
+      // Drain: the most recent NS stages must have landed before the CTA may
+      // retire, whether or not the consumers waited for them.
+      const long long first = it > NS ? it - NS : 0;
+      for (long long j = first; j < it; ++j) {
+        const int slot = static_cast<int>(j % NS);
+        if (!mbar_wait(&full[slot], static_cast<uint32_t>(j / NS) & 1u, a.status,
+                       kStatusDrainTimeout))
+          break;
+      }
+      if constexpr (FMT == kFmtFp8Block128) mbar_wait(sbar, 0, a.status, kStatusDrainTimeout);
+    }
+    return;
+  }
+
+  // -------------------------------------------------------------- consumers
+  pdl_wait();
+  stage_x<Act, XT, NORM, kScaleX>(a, xs, p.xs_stride, xexp, scratch);
+  named_bar_sync(1, kNW * 32);
+  if constexpr (FMT == kFmtFp8Block128) mbar_wait(sbar, 0, a.status, kStatusFullWaitTimeout);
+
+  const int g = lane >> 2;
+  const int tok = min(g, a.M - 1);
+  const XT* xrow = xs + static_cast<size_t>(tok) * p.xs_stride;
+  const int I = a.w.N / 2;
+
+  long long it = 0;
+  bool ok = true;
+  int tile_i = 0;
+  for (int t = t0; t < t1; ++t, ++tile_i) {
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    float acc2[4] = {0.f, 0.f, 0.f, 0.f};
+    int rb_lo = 0, rb_hi = 0;
+    if constexpr (FMT == kFmtFp8Block128) {
+      if (a.w.swiglu) {
+        rb_lo = (8 * t) / 128 - lo0;
+        rb_hi = nlo + (I + 8 * t) / 128 - hi0;
+      } else {
+        rb_lo = rb_hi = (16 * t) / 128 - lo0;
+      }
+    }
+    for (int s = 0; s < spt; ++s, ++it) {
+      const int slot = static_cast<int>(it % NS);
+      if (ok && !mbar_wait(&full[slot], static_cast<uint32_t>(it / NS) & 1u, a.status,
+                           kStatusFullWaitTimeout))
+        ok = false;
+      const int nch = min(kStageChunks, C - s * kStageChunks);
+      const uint8_t* st = ring + static_cast<size_t>(slot) * kStageBytes;
+      if (ok) {
+        if constexpr (FMT == kFmtFp8Block128) {
+          float tmp[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+            const int ch = warp * 2 + j;
+            if (ch < nch) chunk_mma<FMT, XT>(st + ch * CB, s * kStageChunks + ch, xrow, lane, tmp);
+          }
+          const int kb = (s * kStageChunks + warp * 2) / 2;
+          const float slo = bsc[rb_lo * a.w.blk_ld + kb];
+          const float shi = bsc[rb_hi * a.w.blk_ld + kb];
+          acc[0] = fmaf(tmp[0], slo, acc[0]);
+          acc[1] = fmaf(tmp[1], slo, acc[1]);
+          acc[2] = fmaf(tmp[2], shi, acc[2]);
+          acc[3] = fmaf(tmp[3], shi, acc[3]);
+        } else {
+          const int ch0 = warp * 2, ch1 = warp * 2 + 1;
+          if (ch0 < nch) chunk_mma<FMT, XT>(st + ch0 * CB, s * kStageChunks + ch0, xrow, lane, acc);
+          if (ch1 < nch) chunk_mma<FMT, XT>(st + ch1 * CB, s * kStageChunks + ch1, xrow, lane, acc2);
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[slot]);
+    }
+    // ---- cross-warp reduction (double-buffered by tile parity)
+    float* rb = red + (tile_i & 1) * (kNW * 128);
+    *reinterpret_cast<float4*>(rb + (warp * 32 + lane) * 4) =
+        make_float4(acc[0] + acc2[0], acc[1] + acc2[1], acc[2] + acc2[2], acc[3] + acc2[3]);
+    named_bar_sync(1, kNW * 32);
+    const int i = threadIdx.x;
+    auto gather = [&](int rr, int tt) {
+      const int src_lane = (rr & 7) * 4 + (tt >> 1);
+      const int reg = ((rr >> 3) << 1) | (tt & 1);
+      float v = 0.f;
+#pragma unroll
+      for (int w = 0; w < kNW; ++w) v += rb[(w * 32 + src_lane) * 4 + reg];
+      return v;
+    };
+    if constexpr (EPI == kEpiSwiglu) {
+      if (i < 64) {
+        const int rr = i >> 3, tt = i & 7;
+        const int j = t * 8 + rr;
+        if (tt < a.M && j < I) {
+          float vg = gather(rr, tt), vu = gather(rr + 8, tt);
+          float mul = exp2i(xexp[tt]);
+          if constexpr (FMT == kFmtNvfp4G16) mul *= a.w.global_scale;
+          float sg = mul, su = mul;
+          if (a.w.row_scale) {
+            sg *= a.w.row_scale[t * 16 + rr];
+            su *= a.w.row_scale[t * 16 + 8 + rr];
+          }
+          const float gq = AT::round(vg * sg), uq = AT::round(vu * su);
+          Act* out = reinterpret_cast<Act*>(a.out) + static_cast<size_t>(tt) * a.out_ld + j;
+          *out = AT::from_f(silu_mul_ref<Act>(gq, uq));
+        }
+      }
+    } else {
+      if (i < 128) {
+        const int rr = i >> 3, tt = i & 7;
+        const int n = t * 16 + rr;
+        if (tt < a.M && n < a.w.N) {
+          float v = gather(rr, tt);
+          float mul = exp2i(xexp[tt]);
+          if constexpr (FMT == kFmtNvfp4G16) mul *= a.w.global_scale;
+          if (a.w.row_scale) mul *= a.w.row_scale[t * 16 + rr];
+          const float y = AT::round(v * mul);
+          Act* out = reinterpret_cast<Act*>(a.out) + static_cast<size_t>(tt) * a.out_ld + n;
+          if constexpr (EPI == kEpiResidual) {
+            *out = AT::from_f(y + AT::to_f(*out));
+          } else {
+            *out = AT::from_f(y);
+          }
+        }
+      }
+    }
+  }
+}
+
+template <typename Act, int FMT, int EPI, bool NORM>
+cudaError_t launch_one(const GemvArgs& a, int slots_req, int grid_req, cudaStream_t stream,
+                       bool pdl) {
+  int dev = 0, sms = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  int grid = grid_req > 0 ? grid_req : sms;
+  if (grid > a.w.T) grid = a.w.T;
+  const SmemPlan p = make_plan(a.w, a.M, grid, slots_req);
+  if (p.slots < 2) return cudaErrorInvalidConfiguration;
+  auto kern = gemv_kernel<Act, FMT, EPI, NORM>;
+  cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         kSmemBudget);
+  if (err != cudaSuccess) return err;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = p.total;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, a, p);
+}
+
+template <typename Act, int FMT>
+cudaError_t dispatch_epi(const GemvArgs& a, int epi, bool norm, int slots, int grid,
+                         cudaStream_t s, bool pdl) {
+  if (epi == kEpiStore)
+    return norm ? launch_one<Act, FMT, kEpiStore, true>(a, slots, grid, s, pdl)
+                : launch_one<Act, FMT, kEpiStore, false>(a, slots, grid, s, pdl);
+  if (epi == kEpiResidual)
+    return norm ? launch_one<Act, FMT, kEpiResidual, true>(a, slots, grid, s, pdl)
+                : launch_one<Act, FMT, kEpiResidual, false>(a, slots, grid, s, pdl);
+  if (epi == kEpiSwiglu)
+    return norm ? launch_one<Act, FMT, kEpiSwiglu, true>(a, slots, grid, s, pdl)
+                : launch_one<Act, FMT, kEpiSwiglu, false>(a, slots, grid, s, pdl);
+  return cudaErrorInvalidValue;
+}
+
+template <typename Act>
+cudaError_t dispatch_fmt(const GemvArgs& a, int epi, bool norm, int slots, int grid,
+                         cudaStream_t s, bool pdl) {
+  switch (a.w.fmt) {
+    case kFmtW8A16Row: return dispatch_epi<Act, kFmtW8A16Row>(a, epi, norm, slots, grid, s, pdl);
+    case kFmtFp8Block128:
+      return dispatch_epi<Act, kFmtFp8Block128>(a, epi, norm, slots, grid, s, pdl);
+    case kFmtFp8Row: return dispatch_epi<Act, kFmtFp8Row>(a, epi, norm, slots, grid, s, pdl);
+    case kFmtNvfp4G16: return dispatch_epi<Act, kFmtNvfp4G16>(a, epi, norm, slots, grid, s, pdl);
+    case kFmtDense: return dispatch_epi<Act, kFmtDense>(a, epi, norm, slots, grid, s, pdl);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+}  // namespace
+
+cudaError_t gemv_launch(const GemvArgs& args, int act, int epi, bool norm, cudaStream_t stream,
+                        const GemvTuning& tune) {
+  if (args.M < 1 || args.w.T < 1 || args.w.C < 1) return cudaErrorInvalidValue;
+  if (epi == kEpiSwiglu && !args.w.swiglu) return cudaErrorInvalidValue;
+  GemvArgs a = args;
+  const size_t esz = 2;
+  // Rows per launch: up to kMaxM, fewer when the staged activations would
+  // leave the weight ring under 4 stages.  Each group re-streams W.
+  const int pgrid = std::max(1, std::min(args.w.T, 148));
+  int group = kMaxM;
+  while (group > 1 && make_plan(args.w, group, pgrid, 0).slots < 4) group >>= 1;
+  if (make_plan(args.w, group, pgrid, 0).slots < 2) return cudaErrorInvalidConfiguration;
+  for (int r0 = 0; r0 < args.M; r0 += group) {
+    a.M = std::min(group, args.M - r0);
+    a.x = static_cast<const char*>(args.x) + static_cast<size_t>(r0) * args.x_ld * esz;
+    a.out = static_cast<char*>(args.out) + static_cast<size_t>(r0) * args.out_ld * esz;
+    cudaError_t e = act == 0 ? dispatch_fmt<__nv_bfloat16>(a, epi, norm, tune.slots, tune.grid,
+                                                           stream, tune.pdl)
+                             : dispatch_fmt<__half>(a, epi, norm, tune.slots, tune.grid, stream,
+                                                    tune.pdl);
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
+}
+
+int gemv_smem_bytes(const DevQLinear& w, int M, int grid, int slots) {
+  return make_plan(w, std::min(M, kMaxM), grid, slots).total;
+}
+
+}  // namespace dialb200

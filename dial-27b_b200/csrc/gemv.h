@@ -1,0 +1,41 @@
+// Host interface of the decode GEMV (gemv.cu).
+#pragma once
+
+#include <algorithm>
+#include <cuda_runtime.h>
+#include <type_traits>
+
+#include "qlinear.h"
+
+namespace dialb200 {
+
+enum GemvEpilogue : int {
+  kEpiStore = 0,     // out = act(acc * scale)
+  kEpiResidual = 1,  // out = act(out + act(acc * scale))      (in-place residual)
+  kEpiSwiglu = 2,    // out[:, j] = act(silu(gate_j) * up_j)   (fused gate/up rows)
+};
+
+struct GemvArgs {
+  DevQLinear w;
+  const void* x;       // [M][x_ld] activations (bf16 or f16)
+  int x_ld;
+  const void* norm_w;  // RMSNorm weight [K] when the prologue normalizes x
+  float eps;
+  void* out;           // [M][out_ld]
+  int out_ld;
+  int M;
+  int* status;         // device status word (first error code wins)
+};
+
+struct GemvTuning {
+  int slots = 0;   // ring stages (0 = as many as fit)
+  int grid = 0;    // CTAs (0 = one per SM)
+  bool pdl = true; // programmatic dependent launch
+};
+
+// act: 0 = bf16, 1 = f16.  Launches ceil(M/8) kernels on `stream`.
+cudaError_t gemv_launch(const GemvArgs& args, int act, int epi, bool norm, cudaStream_t stream,
+                        const GemvTuning& tune);
+int gemv_smem_bytes(const DevQLinear& w, int M, int grid, int slots);
+
+}  // namespace dialb200

@@ -1,0 +1,240 @@
+/*
+ * dial_b200.h -- C ABI of the B200-native DIAL decoder-layer path.
+ *
+ * The entry points replace, one for one, the two boundaries of the reference
+ * (lisa301/DIAL-27B) on this path:
+ *
+ *   1. the linear custom op: candle `CustomOp1::cuda_fwd` implemented by
+ *      `CudaW8A16Linear` (dial-core/src/models/qwen3_vl/worker_w8a16.rs:295-476)
+ *      and `CudaQuantLinear` (dial-core/src/models/qwen3_8/cuda_quant.rs:256-500);
+ *   2. the layer API: the `Forwarder` trait (dial-core/src/spm/mod.rs:230-287)
+ *      as used by the Worker loop (dial-core/src/spm/worker.rs:740-796) and the
+ *      Master (dial-core/src/models/qwen3_vl/qwen3_vl.rs:2018-2177), plus the
+ *      per-connection KV `Cache` (dial-core/src/models/llama3/cache.rs).
+ *
+ * Conventions follow the reference's own C ABI (backends/qwen38_ggml/adapter.h):
+ * opaque handles, an int status (0 = OK), and a caller-provided error buffer
+ * that receives a NUL-terminated message.  No C++ exception crosses the ABI.
+ * Device pointers are plain CUDA device addresses; `stream` is a cudaStream_t
+ * (NULL = the legacy default stream).  Launches are asynchronous unless an
+ * entry point says it synchronizes.  A handle is not thread-safe: serialize
+ * calls per handle, as the reference serializes calls per GGML engine.
+ */
+#ifndef DIAL_B200_H
+#define DIAL_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define DIAL_B200_ABI_VERSION 1u
+
+/* status codes */
+#define DIAL_OK 0
+#define DIAL_ERR_INVALID 1 /* bad argument or shape (reference: candle_core::Error::Msg) */
+#define DIAL_ERR_CUDA 2    /* CUDA runtime error */
+#define DIAL_ERR_DEVICE 3  /* a kernel recorded a device status (bounded wait expired, bad index) */
+
+/* weight formats */
+#define DIAL_FMT_W8A16_ROW 0    /* int8 [out,in] + f32 scale [out]      (worker_w8a16.rs:295-366) */
+#define DIAL_FMT_FP8_BLOCK128 1 /* e4m3 [out,in] + f32 [ceil(out/128)][ceil(in/128)] */
+#define DIAL_FMT_FP8_ROW 2      /* e4m3 [out,in] + f32 [out] or [1]     (cuda_quant.rs:58-65, 305-334) */
+#define DIAL_FMT_NVFP4_G16 3    /* e2m1 packed [out,in/2] + e4m3 [out,in/16] + f32 global (cuda_quant.rs:43-56) */
+#define DIAL_FMT_DENSE 4        /* activation-dtype dense [out,in] (candle Linear, lm_head) */
+
+/* activation / tensor dtypes */
+#define DIAL_ACT_BF16 0
+#define DIAL_ACT_F16 1
+#define DIAL_ACT_F32 2 /* source weights only */
+
+/* Library version; replaces nothing (the reference links statically). */
+uint32_t dial_b200_abi_version(void);
+
+/* Read (and optionally clear) the device status word of the current device.
+ * A non-zero value names the first bounded wait that expired or the first
+ * out-of-range index a kernel saw since the last clear. */
+int dial_b200_device_status(int* status_out, int clear, char* err, size_t err_size);
+
+/* ------------------------------------------------------------------------ */
+/* Linear op: CudaW8A16Linear / CudaQuantLinear                             */
+/* ------------------------------------------------------------------------ */
+
+typedef struct dial_b200_qlinear dial_b200_qlinear;
+
+/* a1: row-wise symmetric int8 quantization of a dense [out_dim, in_dim]
+ * weight, bit-identical to CudaW8A16Linear::from_linear
+ * (worker_w8a16.rs:330-341).  `weight` is a host pointer; results go to the
+ * host arrays q[out_dim*in_dim] and scale[out_dim]. */
+int dial_b200_w8a16_quantize(const void* weight, int weight_dtype, int64_t out_dim, int64_t in_dim,
+                             int8_t* q, float* scale, char* err, size_t err_size);
+
+/* CudaW8A16Linear::from_linear (worker_w8a16.rs:302-366): quantize a dense
+ * host weight [out_dim, in_dim] and keep it device resident.  `act` is the
+ * activation dtype forward() accepts. */
+int dial_b200_w8a16_from_dense(const void* weight, int weight_dtype, int64_t out_dim,
+                               int64_t in_dim, int act, dial_b200_qlinear** out, char* err,
+                               size_t err_size);
+
+/* CudaQuantLinear::nvfp4 / ::fp8 (cuda_quant.rs:270-371) and the W8A16 /
+ * dense formats from pre-quantized host arrays (see DIAL_FMT_* for layouts;
+ * scales of NVFP4 are e4m3 codes, `global_scale` its f32 multiplier). */
+int dial_b200_qlinear_create(int fmt, int act, const void* codes, const void* scales,
+                             float global_scale, int64_t in_dim, int64_t out_dim,
+                             dial_b200_qlinear** out, char* err, size_t err_size);
+
+void dial_b200_qlinear_destroy(dial_b200_qlinear* lin);
+
+/* CustomOp1::cuda_fwd (worker_w8a16.rs:402-475, cuda_quant.rs:406-499):
+ * y[rows, out_dim] = x[rows, in_dim] . dequant(W)^T, both contiguous device
+ * arrays of the activation dtype; y is caller-owned. */
+int dial_b200_qlinear_forward(dial_b200_qlinear* lin, const void* x, void* y, int64_t rows,
+                              void* stream, char* err, size_t err_size);
+
+int64_t dial_b200_qlinear_in_dim(const dial_b200_qlinear* lin);
+int64_t dial_b200_qlinear_out_dim(const dial_b200_qlinear* lin);
+/* CudaQuantLinear::resident_bytes (cuda_quant.rs:345-356) */
+int64_t dial_b200_qlinear_resident_bytes(const dial_b200_qlinear* lin);
+
+/* ------------------------------------------------------------------------ */
+/* Decoder layers: Forwarder + per-session KV cache + Worker                */
+/* ------------------------------------------------------------------------ */
+
+typedef struct dial_b200_engine dial_b200_engine;
+
+/* Shape contract of llama3::Config (dial-core/src/models/llama3/config.rs:68-85)
+ * plus the engine's capacities. */
+typedef struct {
+  int32_t hidden_size;
+  int32_t intermediate_size;
+  int32_t vocab_size;
+  int32_t num_hidden_layers;
+  int32_t num_attention_heads;
+  int32_t num_key_value_heads;
+  float rms_norm_eps;
+  float rope_theta;
+  int32_t max_seq_len;  /* per-session KV capacity in tokens (--kv-cache-max-len) */
+  int32_t max_sessions; /* concurrent sessions (one reference TCP connection each) */
+  int32_t max_tokens;   /* rows per forward call (decode batch or prefill chunk) */
+  int32_t act;          /* DIAL_ACT_BF16 or DIAL_ACT_F16 */
+  int32_t linear_fmt;   /* DIAL_FMT_* of the layer linears */
+  int32_t first_layer;  /* layer range owned by this engine (a topology node / stage) */
+  int32_t num_layers;
+  int32_t has_embed;    /* owns the token embedding (first stage) */
+  int32_t has_head;     /* owns ln_f + lm_head + greedy argmax (last stage) */
+} dial_b200_model_config;
+
+/* Worker::new (spm/worker.rs:469-523): allocate weights, paged KV and work
+ * buffers for the owned layers on `device`. */
+int dial_b200_engine_create(const dial_b200_model_config* cfg, int device,
+                            dial_b200_engine** out, char* err, size_t err_size);
+void dial_b200_engine_destroy(dial_b200_engine* eng);
+
+/* Seeded random-init weights generated on the device:
+ * bf16 N(0, std) via `normal_table_bits` (65536 bf16 quantiles, host array),
+ * norm weights 1.0, linears quantized to the engine's format at load. */
+int dial_b200_engine_load_synthetic(dial_b200_engine* eng, uint64_t seed,
+                                    const uint16_t* normal_table_bits, char* err, size_t err_size);
+
+/* Explicit weights (host arrays).  which: 0 qkv (fused q|k|v rows),
+ * 1 o_proj, 2 gate_up (fused gate|up rows), 3 down_proj, 4 lm_head. */
+int dial_b200_engine_set_linear(dial_b200_engine* eng, int layer, int which, int fmt,
+                                const void* codes, const void* scales, float global_scale,
+                                int64_t out_dim, int64_t in_dim, char* err, size_t err_size);
+/* which: 0 input_layernorm, 1 post_attention_layernorm, 2 q_norm, 3 k_norm,
+ * 4 final norm (ln_f), 5 embedding [vocab, hidden]. */
+int dial_b200_engine_set_tensor(dial_b200_engine* eng, int layer, int which, const void* host,
+                                int64_t numel, char* err, size_t err_size);
+
+/* Forwarder::forward (spm/mod.rs:236-242, text.rs:1636-1688): one session,
+ * `seq_len` tokens starting at `index_pos`; hidden [seq_len, hidden] device
+ * array updated in place.  index_pos == 0 starts the session over
+ * (Cache::process_kv replace semantics, cache.rs:133-136). */
+int dial_b200_layer_forward(dial_b200_engine* eng, int layer, void* hidden, int64_t seq_len,
+                            int32_t session, int64_t index_pos, void* stream, char* err,
+                            size_t err_size);
+
+/* Forwarder::forward_local_batch (spm/mod.rs:268-277): a contiguous layer
+ * range in one call; validates the whole range before touching the cache. */
+int dial_b200_range_forward(dial_b200_engine* eng, int first_layer, int count, void* hidden,
+                            int64_t seq_len, int32_t session, int64_t index_pos, void* stream,
+                            char* err, size_t err_size);
+
+/* Ragged multi-session decode: row m is one new token of session sids[m] at
+ * positions[m] (host arrays); hidden [rows, hidden] device, in place. */
+int dial_b200_batch_decode_forward(dial_b200_engine* eng, int first_layer, int count,
+                                   void* hidden, int64_t rows, const int32_t* sids,
+                                   const int32_t* positions, void* stream, char* err,
+                                   size_t err_size);
+
+/* Cache::clear / as_new for one session (cache.rs:240-265). */
+int dial_b200_session_reset(dial_b200_engine* eng, int32_t session, char* err, size_t err_size);
+
+/* Embedding::forward (qwen3_vl.rs:3302): tokens_dev [rows] -> hidden [rows, H]. */
+int dial_b200_embed(dial_b200_engine* eng, const int32_t* tokens_dev, int64_t rows, void* hidden,
+                    void* stream, char* err, size_t err_size);
+
+/* ln_f + lm_head + greedy argmax (qwen3_vl.rs:2462-2487, 138-143) on `rows`
+ * hidden rows; logits_dev [rows, vocab] may be NULL (an internal buffer is
+ * used); tokens_dev [rows] receives the argmax ids. */
+int dial_b200_head(dial_b200_engine* eng, const void* hidden, int64_t rows, void* logits_dev,
+                   int32_t* tokens_dev, void* stream, char* err, size_t err_size);
+
+/* One greedy decode step end to end, host buffers (synchronizes): tokens ->
+ * embed -> owned layers -> head -> next tokens.  Engine must own the whole
+ * model (has_embed && has_head && all layers).  Replays a CUDA graph per
+ * distinct `rows`. */
+int dial_b200_decode_step(dial_b200_engine* eng, int64_t rows, const int32_t* tokens_host,
+                          const int32_t* sids_host, const int32_t* positions_host,
+                          int32_t* next_tokens_host, char* err, size_t err_size);
+
+/* Greedy generation for one session (Master::generate, spm/master.rs:56-103):
+ * prefill of `n_prompt` tokens then `n_gen` decode steps; out_tokens[n_gen]
+ * (host).  ttft_s / decode_s receive wall times (may be NULL). */
+int dial_b200_generate(dial_b200_engine* eng, int32_t session, const int32_t* prompt,
+                       int64_t n_prompt, int64_t n_gen, int32_t* out_tokens, double* ttft_s,
+                       double* decode_s, char* err, size_t err_size);
+
+/* Device-resident decode loop for measurement: `n_steps` replays of the
+ * step graph with the sampled tokens fed back on the device; rows of state
+ * are seeded by dial_b200_decode_loop_prepare.  Asynchronous on the engine
+ * stream. */
+int dial_b200_decode_loop_prepare(dial_b200_engine* eng, int64_t rows, const int32_t* tokens_host,
+                                  const int32_t* sids_host, const int32_t* positions_host,
+                                  char* err, size_t err_size);
+int dial_b200_decode_loop_run(dial_b200_engine* eng, int64_t rows, int64_t n_steps, char* err,
+                              size_t err_size);
+/* Copy the loop's current tokens/positions back to host (synchronizes). */
+int dial_b200_decode_loop_state(dial_b200_engine* eng, int64_t rows, int32_t* tokens_host,
+                                int32_t* positions_host, char* err, size_t err_size);
+
+/* The engine's CUDA stream (cudaStream_t) for event timing by the caller. */
+void* dial_b200_engine_stream(dial_b200_engine* eng);
+
+/* Fill a session's KV pages [0, length) with seeded N(0,1) bf16 values for
+ * every owned layer (ragged multi-session benchmarks start from such a
+ * cache); uses the normal table of load_synthetic scaled by `std`. */
+int dial_b200_session_fill_random(dial_b200_engine* eng, int32_t session, int64_t length,
+                                  uint64_t seed, const uint16_t* normal_table_bits, char* err,
+                                  size_t err_size);
+
+/* Number of kernels one decode step launches for `rows` rows. */
+int64_t dial_b200_step_kernel_count(dial_b200_engine* eng, int64_t rows);
+
+/* Measurement hook: launch one owned layer's linear (`which` as in
+ * set_linear, with the epilogue the decode step uses) `iters` times back to
+ * back on the engine stream over the engine's work buffers.  Asynchronous. */
+int dial_b200_engine_linear_replay(dial_b200_engine* eng, int layer, int which, int64_t rows,
+                                   int64_t iters, char* err, size_t err_size);
+
+/* Algorithmic bytes one launch of that linear moves (weights + scales +
+ * activations in + out), the roofline numerator. */
+int64_t dial_b200_engine_linear_bytes(dial_b200_engine* eng, int layer, int which, int64_t rows);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DIAL_B200_H */

@@ -1,0 +1,208 @@
+"""Decoder-layer and model parity on the GPU through the C ABI (Forwarder /
+Worker / Master counterparts) against the CPU oracle, at sizes the oracle
+finishes in seconds."""
+
+import numpy as np
+import pytest
+import torch
+
+import dial_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+
+def small_cfg(**kw):
+    base = dict(hidden=256, inter=512, vocab=1000, layers=2, heads=2, kv_heads=1, eps=1e-6,
+                rope_theta=1e6, max_seq_len=512)
+    base.update(kw)
+    return O.ModelConfig(**base)
+
+
+def engine_for(ocfg, dial_b200, max_sessions=1, max_tokens=256, **kw):
+    cfg = dial_b200.Config(hidden_size=ocfg.hidden, intermediate_size=ocfg.inter,
+                           vocab_size=ocfg.vocab, num_hidden_layers=ocfg.layers,
+                           num_attention_heads=ocfg.heads, num_key_value_heads=ocfg.kv_heads,
+                           rms_norm_eps=ocfg.eps, rope_theta=ocfg.rope_theta,
+                           max_seq_len=ocfg.max_seq_len, max_sessions=max_sessions,
+                           max_tokens=max_tokens)
+    return dial_b200.Engine(cfg, **kw)
+
+
+def random_layer(cfg, seed):
+    rng = np.random.default_rng(seed)
+    H, I, D = cfg.hidden, cfg.inter, cfg.head_dim
+    qkv = (cfg.heads + 2 * cfg.kv_heads) * D
+    w = lambda n, k: O.bf16_round(rng.standard_normal((n, k)).astype(np.float32) * 0.05)  # noqa: E731
+    nw = lambda n: O.bf16_round(1.0 + 0.1 * rng.standard_normal(n).astype(np.float32))  # noqa: E731
+    return O.LayerWeights(*O.quantize_w8a16_rows(w(qkv, H)), *O.quantize_w8a16_rows(w(H, cfg.heads * D)),
+                          *O.quantize_w8a16_rows(w(2 * I, H)), *O.quantize_w8a16_rows(w(H, I)),
+                          nw(H), nw(H), nw(D), nw(D))
+
+
+def assert_hidden_close(got, ref, rel=2 ** -5, mean_rel=2 ** -7, ulps=4, frac=0.99):
+    """bf16 hidden-state tolerance against the reference-semantics oracle:
+    max |d| <= 2^-5 max|ref|, mean |d| <= 2^-7 rms(ref), and 99% of elements
+    within 4 bf16 ulps of max(|ref_i|, rms) (elements near zero after the
+    residual add carry the rounding error of their operands).  The GPU keeps
+    softmax probabilities in f32 and accumulates in f32 in another order; an
+    oracle run with those two choices lands at mean |d| ~ 2^-8.3 rms."""
+    got = np.asarray(got, np.float32)
+    ref = np.asarray(ref, np.float32)
+    d = np.abs(got - ref)
+    scale = float(np.max(np.abs(ref)))
+    rms = float(np.sqrt(np.mean(ref.astype(np.float64) ** 2)))
+    assert float(d.max()) <= rel * scale + 1e-3, f"max |d| {d.max()} vs scale {scale}"
+    assert float(d.mean()) <= mean_rel * rms, f"mean |d| {d.mean()} vs rms {rms}"
+    mag = np.maximum(np.abs(ref), rms)
+    ulp = np.exp2(np.floor(np.log2(mag)) - 7)
+    assert np.mean(d <= ulps * ulp) >= frac, f"{np.mean(d <= ulps * ulp):.4f} within {ulps} ulp"
+
+
+@pytest.mark.parametrize("heads,kv", [(4, 1), (8, 2), (10, 2), (2, 2)])
+def test_layer_prefill_then_decode(cuda, heads, kv):
+    import dial_b200
+
+    cfg = small_cfg(heads=heads, kv_heads=kv, hidden=128 * heads, layers=1)
+    lw = random_layer(cfg, 1)
+    eng = engine_for(cfg, dial_b200)
+    eng.set_layer_w8a16(0, lw)
+    cos, sin = O.rope_tables(cfg.head_dim, cfg.max_seq_len, cfg.rope_theta)
+    cache = O.Cache(1, cfg.max_seq_len)
+    rng = np.random.default_rng(7)
+    S = 21
+    x = O.bf16_round(rng.standard_normal((S, cfg.hidden)).astype(np.float32))
+    ref = O.layer_forward(x, lw, cfg, 0, 0, cache, cos, sin)
+    tight = O.layer_forward(x, lw, cfg, 0, 0, O.Cache(1, cfg.max_seq_len), cos, sin,
+                            round_probs=False)
+    xt = torch.from_numpy(x).to(cuda).to(torch.bfloat16)
+    eng.forward(xt, 0, 0)
+    torch.cuda.synchronize()
+    got = xt.float().cpu().numpy()
+    assert_hidden_close(got, ref)
+    # same rounding choices as the kernels: only summation order differs
+    assert_hidden_close(got, tight, mean_rel=2 ** -10, ulps=2, frac=0.995)
+    for step in range(4):
+        x1 = O.bf16_round(rng.standard_normal((1, cfg.hidden)).astype(np.float32))
+        ref1 = O.layer_forward(x1, lw, cfg, S + step, 0, cache, cos, sin)
+        t1 = torch.from_numpy(x1).to(cuda).to(torch.bfloat16)
+        eng.forward(t1, S + step, 0)
+        torch.cuda.synchronize()
+        assert_hidden_close(t1.float().cpu().numpy(), ref1)
+    assert dial_b200.device_status() == 0
+
+
+def test_long_context_split_kv(cuda):
+    """Decode attention over ~700 cached positions uses several KV splits."""
+    import dial_b200
+
+    cfg = small_cfg(layers=1, max_seq_len=1024)
+    lw = random_layer(cfg, 2)
+    eng = engine_for(cfg, dial_b200, max_tokens=800)
+    eng.set_layer_w8a16(0, lw)
+    cos, sin = O.rope_tables(cfg.head_dim, cfg.max_seq_len, cfg.rope_theta)
+    cache = O.Cache(1, cfg.max_seq_len)
+    rng = np.random.default_rng(8)
+    S = 700
+    x = O.bf16_round(rng.standard_normal((S, cfg.hidden)).astype(np.float32))
+    O.layer_forward(x, lw, cfg, 0, 0, cache, cos, sin)
+    eng.forward(torch.from_numpy(x).to(cuda).to(torch.bfloat16), 0, 0)
+    x1 = O.bf16_round(rng.standard_normal((1, cfg.hidden)).astype(np.float32))
+    ref = O.layer_forward(x1, lw, cfg, S, 0, cache, cos, sin)
+    t1 = torch.from_numpy(x1).to(cuda).to(torch.bfloat16)
+    eng.forward(t1, S, 0)
+    torch.cuda.synchronize()
+    assert_hidden_close(t1.float().cpu().numpy(), ref)
+
+
+def test_ragged_multi_session_decode(cuda):
+    """Rows of different sessions at different positions in one call."""
+    import dial_b200
+
+    cfg = small_cfg(layers=2)
+    lws = [random_layer(cfg, 10 + l) for l in range(cfg.layers)]
+    n_sess = 5
+    eng = engine_for(cfg, dial_b200, max_sessions=n_sess)
+    for l, lw in enumerate(lws):
+        eng.set_layer_w8a16(l, lw)
+    cos, sin = O.rope_tables(cfg.head_dim, cfg.max_seq_len, cfg.rope_theta)
+    rng = np.random.default_rng(9)
+    lens = [3, 17, 40, 1, 64]
+    prefills = [O.bf16_round(rng.standard_normal((L, cfg.hidden)).astype(np.float32)) for L in lens]
+    caches = []
+    for s, x in enumerate(prefills):
+        c = O.Cache(cfg.layers, cfg.max_seq_len)
+        for l, lw in enumerate(lws):
+            x = O.layer_forward(x, lw, cfg, 0, l, c, cos, sin)
+        caches.append(c)
+        xt = torch.from_numpy(prefills[s]).to(cuda).to(torch.bfloat16)
+        eng.forward_local_batch(xt, [(f"l{l}", 0, l) for l in range(cfg.layers)], session=s)
+    rows = O.bf16_round(rng.standard_normal((n_sess, cfg.hidden)).astype(np.float32))
+    ref = []
+    for s, L in enumerate(lens):
+        x = rows[s:s + 1]
+        for l, lw in enumerate(lws):
+            x = O.layer_forward(x, lw, cfg, L, l, caches[s], cos, sin)
+        ref.append(x[0])
+    xt = torch.from_numpy(rows).to(cuda).to(torch.bfloat16)
+    eng.batch_decode(xt, list(range(n_sess)), lens)
+    torch.cuda.synchronize()
+    assert_hidden_close(xt.float().cpu().numpy(), np.stack(ref))
+
+
+def test_synthetic_model_greedy_tokens(cuda):
+    """Device-generated random-init weights equal the oracle's generator, and
+    greedy decoding agrees token for token (teacher-forced per step)."""
+    import dial_b200
+
+    cfg = small_cfg(layers=3, vocab=2048, hidden=512, heads=4, kv_heads=1, inter=1024)
+    model = O.synth_model(cfg, seed=0)
+    eng = engine_for(cfg, dial_b200)
+    eng.load_synthetic(seed=0)
+    prompt = O.synth_tokens(1, 12, cfg.vocab).tolist()
+    toks, _, _ = eng.generate(prompt, 10)
+    ref_toks, ref_logits = O.greedy_generate(model, prompt, 10, forced=toks)
+    agree = 0
+    for i, (a, b) in enumerate(zip(toks.tolist(), ref_toks)):
+        lg = ref_logits[i]
+        if a == b:
+            agree += 1
+        else:  # a disagreement must be a near tie under the oracle
+            assert lg[b] - lg[a] <= 2 * 2.0 ** (np.floor(np.log2(abs(lg[b]))) - 7) + 1e-6
+    assert agree >= 9
+    assert dial_b200.device_status() == 0
+
+
+def test_decode_step_graph_matches_eager(cuda):
+    import dial_b200
+
+    cfg = small_cfg(layers=2, vocab=1024)
+    eng = engine_for(cfg, dial_b200, max_sessions=3)
+    eng.load_synthetic(seed=3)
+    prompt = [5, 9, 200, 31]
+    out, _, _ = eng.generate(prompt, 6, session=0)
+    # same prompt in session 1 driven step by step through decode_step
+    out2, _, _ = eng.generate(prompt, 1, session=1)
+    toks = [int(out2[0])]
+    for i in range(5):
+        nxt = eng.decode_step([toks[-1]], [1], [len(prompt) + i])
+        toks.append(int(nxt[0]))
+    assert toks == out.tolist()
+
+
+def test_layer_forward_rejects_bad_requests(cuda):
+    import dial_b200
+
+    cfg = small_cfg(layers=1, max_seq_len=64)
+    eng = engine_for(cfg, dial_b200, max_tokens=32)
+    x = torch.zeros(4, cfg.hidden, dtype=torch.bfloat16, device=cuda)
+    with pytest.raises(dial_b200.DialError, match="no weights"):
+        eng.forward(x, 0, 0)
+    eng.set_layer_w8a16(0, random_layer(cfg, 0))
+    with pytest.raises(dial_b200.DialError, match="not owned"):
+        eng.forward(x, 0, 1)
+    with pytest.raises(dial_b200.DialError, match="KV capacity"):
+        eng.forward(x, 62, 0)
+    with pytest.raises(dial_b200.DialError, match="seq_len"):
+        eng.forward(torch.zeros(40, cfg.hidden, dtype=torch.bfloat16, device=cuda), 0, 0)
+    with pytest.raises(dial_b200.DialError, match="contiguous layer range"):
+        eng.forward_local_batch(x, [("a", 0, 0), ("b", 0, 2)])
