@@ -17,254 +17,21 @@
 #include <cmath>
 
 #include "attention.h"
+#include "attn_dev.cuh"
 #include "common.cuh"
 
 namespace dialb200 {
 namespace {
 
-constexpr int kD = 128;  // head_dim supported by these kernels
-
-template <typename Act>
-__device__ __forceinline__ void load4(const Act* p, float (&v)[4]) {
-  const uint2 raw = *reinterpret_cast<const uint2*>(p);
-  const Act* h = reinterpret_cast<const Act*>(&raw);
-#pragma unroll
-  for (int e = 0; e < 4; ++e) v[e] = ActTraits<Act>::to_f(h[e]);
-}
-
-template <typename Act>
-__device__ __forceinline__ void store4(Act* p, const float (&v)[4]) {
-  uint2 raw;
-  Act* h = reinterpret_cast<Act*>(&raw);
-#pragma unroll
-  for (int e = 0; e < 4; ++e) h[e] = ActTraits<Act>::from_f(v[e]);
-  *reinterpret_cast<uint2*>(p) = raw;
-}
-
-// Per-head RMSNorm + RoPE of one 128-wide head held 4 dims per lane
-// (lane l: dims 4l..4l+3); values are activation-rounded floats.
-template <typename Act, bool NORM, bool ROPE>
-__device__ __forceinline__ void norm_rope(float (&x)[4], const Act* norm_w, float eps,
-                                          const Act* cos_row, const Act* sin_row, int lane) {
-  using AT = ActTraits<Act>;
-  if constexpr (NORM) {
-    float ss = 0.f;
-#pragma unroll
-    for (int e = 0; e < 4; ++e) ss = fmaf(x[e], x[e], ss);
-    ss = warp_sum(ss);
-    const float m = AT::round(__fsqrt_rn(__fdiv_rn(ss, static_cast<float>(kD)) + eps));
-    float w[4];
-    load4(norm_w + lane * 4, w);
-#pragma unroll
-    for (int e = 0; e < 4; ++e) x[e] = AT::round(AT::round(__fdiv_rn(x[e], m)) * w[e]);
-  }
-  if constexpr (ROPE) {
-    float partner[4];
-#pragma unroll
-    for (int e = 0; e < 4; ++e) partner[e] = __shfl_xor_sync(0xffffffffu, x[e], 16);
-    const int i0 = (lane & 15) * 4;
-    float c[4], s[4];
-    load4(cos_row + i0, c);
-    load4(sin_row + i0, s);
-    const bool first = lane < 16;
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const float x1 = first ? x[e] : partner[e];
-      const float x2 = first ? partner[e] : x[e];
-      x[e] = first ? AT::round(AT::round(x1 * c[e]) - AT::round(x2 * s[e]))
-                   : AT::round(AT::round(x1 * s[e]) + AT::round(x2 * c[e]));
-    }
-  }
-}
-
-__device__ __forceinline__ int lane_of_token(int t) {
-  return (((t >> 3) & 1) << 4) | (((t >> 2) & 1) << 3) | (((t >> 1) & 1) << 2) | ((t & 1) << 1);
-}
+constexpr int kD = kHeadDim;
 
 template <typename Act, int NREP>
 __global__ void __launch_bounds__(NREP * 32) attn_decode_kernel(const AttnDecodeArgs a) {
-  using AT = ActTraits<Act>;
-  const int kvh = blockIdx.x, split = blockIdx.y, m = blockIdx.z;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int QH = a.sh.q_heads, KVH = a.sh.kv_heads;
-  const int h = kvh * NREP + warp;
-
   pdl_launch_dependents();
   pdl_wait();
-
-  __shared__ float kn_s[kD], vn_s[kD];
-  __shared__ int last_flag;
-
-  const int sid = a.sid[m];
-  int pos = a.pos[m];
-  const bool bad = pos < 0 || pos >= a.sh.max_pos || pos / kPageTokens >= a.sh.max_blocks;
-  if (bad) {
-    set_status(a.status, kStatusBadArgs);
-    pos = 0;
-  }
-  const int ctx = pos + 1;
-  const int32_t* bt = a.block_table + static_cast<size_t>(sid) * a.sh.max_blocks;
-  const int span = ((ctx + a.splits - 1) / a.splits + kPageTokens - 1) / kPageTokens * kPageTokens;
-  const int tok0 = split * span;
-  const int tok1 = min(ctx, tok0 + span);
-  const bool owner = tok0 <= pos && pos < tok1;
-
-  const Act* qkv = reinterpret_cast<const Act*>(a.qkv) + static_cast<size_t>(m) * a.qkv_ld;
-  const Act* cos_row = reinterpret_cast<const Act*>(a.cos) + static_cast<size_t>(pos) * (kD / 2);
-  const Act* sin_row = reinterpret_cast<const Act*>(a.sin) + static_cast<size_t>(pos) * (kD / 2);
-  Act* kpool = reinterpret_cast<Act*>(a.kv.k);
-  Act* vpool = reinterpret_cast<Act*>(a.kv.v);
-
-  float q[4];
-  load4(qkv + h * kD + lane * 4, q);
-  norm_rope<Act, true, true>(q, reinterpret_cast<const Act*>(a.q_norm_w), a.sh.eps, cos_row,
-                             sin_row, lane);
-
-  if (owner && warp == 0 && !bad) {
-    float k[4], v[4];
-    load4(qkv + (QH + kvh) * kD + lane * 4, k);
-    load4(qkv + (QH + KVH + kvh) * kD + lane * 4, v);
-    norm_rope<Act, true, true>(k, reinterpret_cast<const Act*>(a.k_norm_w), a.sh.eps, cos_row,
-                               sin_row, lane);
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      kn_s[lane * 4 + e] = k[e];
-      vn_s[lane * 4 + e] = v[e];
-    }
-    const int blk = bt[pos / kPageTokens];
-    const size_t off =
-        ((static_cast<size_t>(blk) * KVH + kvh) * kPageTokens + (pos % kPageTokens)) * kD + lane * 4;
-    store4(kpool + off, k);
-    store4(vpool + off, v);
-  }
-  __syncthreads();
-
-  const float scale = AT::round(1.0f / sqrtf(static_cast<float>(kD)));
-  float mrun = -INFINITY, lrun = 0.f, acc[4] = {0.f, 0.f, 0.f, 0.f};
-  const int my_tok = ((lane >> 4) & 1) * 8 + ((lane >> 3) & 1) * 4 + ((lane >> 2) & 1) * 2 +
-                     ((lane >> 1) & 1);
-
-  for (int b0 = tok0; b0 < tok1; b0 += kPageTokens) {
-    const int blk = bt[b0 / kPageTokens];
-    const size_t base = (static_cast<size_t>(blk) * KVH + kvh) * kPageTokens * kD + lane * 4;
-    uint2 kr[kPageTokens], vr[kPageTokens];
-#pragma unroll
-    for (int j = 0; j < kPageTokens; ++j) {
-      kr[j] = *reinterpret_cast<const uint2*>(kpool + base + j * kD);
-      vr[j] = *reinterpret_cast<const uint2*>(vpool + base + j * kD);
-    }
-    float v16[kPageTokens];
-#pragma unroll
-    for (int j = 0; j < kPageTokens; ++j) {
-      const Act* kh = reinterpret_cast<const Act*>(&kr[j]);
-      float d = 0.f;
-      if (owner && b0 + j == pos) {
-#pragma unroll
-        for (int e = 0; e < 4; ++e) d = fmaf(q[e], kn_s[lane * 4 + e], d);
-      } else {
-#pragma unroll
-        for (int e = 0; e < 4; ++e) d = fmaf(q[e], AT::to_f(kh[e]), d);
-      }
-      v16[j] = d;
-    }
-    // reduce-scatter: afterwards lane holds the full dot of token my_tok
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const float send = (lane & 16) ? v16[i] : v16[i + 8];
-      const float keep = (lane & 16) ? v16[i + 8] : v16[i];
-      v16[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
-    }
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float send = (lane & 8) ? v16[i] : v16[i + 4];
-      const float keep = (lane & 8) ? v16[i + 4] : v16[i];
-      v16[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
-    }
-#pragma unroll
-    for (int i = 0; i < 2; ++i) {
-      const float send = (lane & 4) ? v16[i] : v16[i + 2];
-      const float keep = (lane & 4) ? v16[i + 2] : v16[i];
-      v16[i] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
-    }
-    {
-      const float send = (lane & 2) ? v16[0] : v16[1];
-      const float keep = (lane & 2) ? v16[1] : v16[0];
-      v16[0] = keep + __shfl_xor_sync(0xffffffffu, send, 2);
-    }
-    float s = v16[0] + __shfl_xor_sync(0xffffffffu, v16[0], 1);
-    const bool valid = b0 + my_tok < tok1;
-    s = valid ? AT::round(AT::round(s) * scale) : -INFINITY;
-    const float bm = warp_max(s);
-    const float mnew = fmaxf(mrun, bm);
-    const float p = valid ? expf(s - mnew) : 0.f;
-    const float alpha = expf(mrun - mnew);
-    const float lsum = warp_sum((lane & 1) ? 0.f : p);
-    lrun = lrun * alpha + lsum;
-#pragma unroll
-    for (int e = 0; e < 4; ++e) acc[e] *= alpha;
-#pragma unroll
-    for (int j = 0; j < kPageTokens; ++j) {
-      const float pj = __shfl_sync(0xffffffffu, p, lane_of_token(j));
-      const Act* vh = reinterpret_cast<const Act*>(&vr[j]);
-      if (owner && b0 + j == pos) {
-#pragma unroll
-        for (int e = 0; e < 4; ++e) acc[e] = fmaf(pj, vn_s[lane * 4 + e], acc[e]);
-      } else {
-#pragma unroll
-        for (int e = 0; e < 4; ++e) acc[e] = fmaf(pj, AT::to_f(vh[e]), acc[e]);
-      }
-    }
-    mrun = mnew;
-  }
-
-  Act* out = reinterpret_cast<Act*>(a.out) + static_cast<size_t>(m) * a.out_ld + h * kD + lane * 4;
-  if (a.splits == 1) {
-    float o[4];
-    const float inv = lrun > 0.f ? 1.f / lrun : 0.f;
-#pragma unroll
-    for (int e = 0; e < 4; ++e) o[e] = acc[e] * inv;
-    store4(out, o);
-    return;
-  }
-
-  const int S = a.splits;
-  const size_t prow = (static_cast<size_t>(m) * QH + h) * S;
-  *reinterpret_cast<float4*>(a.part_o + (prow + split) * kD + lane * 4) =
-      make_float4(acc[0], acc[1], acc[2], acc[3]);
-  if (lane == 0) {
-    a.part_ml[(prow + split) * 2] = mrun;
-    a.part_ml[(prow + split) * 2 + 1] = lrun;
-  }
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    __threadfence();
-    const int old = atomicAdd(a.counters + m * KVH + kvh, 1);
-    last_flag = (old == S - 1);
-  }
-  __syncthreads();
-  if (!last_flag) return;
-  __threadfence();
-  float M = -INFINITY;
-  for (int s2 = lane; s2 < S; s2 += 32) M = fmaxf(M, __ldcg(a.part_ml + (prow + s2) * 2));
-  M = warp_max(M);
-  float L = 0.f, o[4] = {0.f, 0.f, 0.f, 0.f};
-  for (int s2 = 0; s2 < S; ++s2) {
-    const float ms = __ldcg(a.part_ml + (prow + s2) * 2);
-    const float ls = __ldcg(a.part_ml + (prow + s2) * 2 + 1);
-    const float w = ms == -INFINITY ? 0.f : expf(ms - M);
-    L = fmaf(w, ls, L);
-    const float4 po = __ldcg(reinterpret_cast<const float4*>(a.part_o + (prow + s2) * kD + lane * 4));
-    o[0] = fmaf(w, po.x, o[0]);
-    o[1] = fmaf(w, po.y, o[1]);
-    o[2] = fmaf(w, po.z, o[2]);
-    o[3] = fmaf(w, po.w, o[3]);
-  }
-  const float inv = L > 0.f ? 1.f / L : 0.f;
-#pragma unroll
-  for (int e = 0; e < 4; ++e) o[e] *= inv;
-  store4(out, o);
-  __syncthreads();
-  if (threadIdx.x == 0) a.counters[m * KVH + kvh] = 0;
+  __shared__ AttnItemSmem sm;
+  attn_item<Act, NREP>(a, blockIdx.z, blockIdx.x, blockIdx.y, threadIdx.x >> 5, threadIdx.x & 31,
+                       sm, 1);
 }
 
 // Prefill KV append: token t of the session at position p0+t.  One warp per
@@ -288,8 +55,7 @@ __global__ void kv_append_kernel(const AttnPrefillArgs a) {
   float k[4], v[4];
   load4(qkv + (QH + kvh) * kD + lane * 4, k);
   load4(qkv + (QH + KVH + kvh) * kD + lane * 4, v);
-  norm_rope<Act, true, true>(k, reinterpret_cast<const Act*>(a.k_norm_w), a.sh.eps, cos_row,
-                             sin_row, lane);
+  norm_rope<Act>(k, reinterpret_cast<const Act*>(a.k_norm_w), a.sh.eps, cos_row, sin_row, lane);
   const int blk = a.block_table[pos / kPageTokens];
   const size_t off =
       ((static_cast<size_t>(blk) * KVH + kvh) * kPageTokens + (pos % kPageTokens)) * kD + lane * 4;

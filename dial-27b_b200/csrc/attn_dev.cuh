@@ -1,0 +1,331 @@
+// Device-side decode attention over the paged KV cache, shared by the
+// decode attention kernels (attention.cu).
+//
+// One work item = (row m, kv head, split): NREP warps (one per query head of
+// the GQA group) run q-norm + RoPE, the item whose span holds the new token
+// normalizes/rotates its K, appends K/V to the pages and scores it from
+// shared memory, then an f32 online softmax over the span.  With several
+// splits the partials land in scratch and the last item to arrive on the
+// (row, kv head) counter combines them and writes the output.
+//
+// Reference: text.rs:1466-1467,1513-1514 (q/k norm), 1143-1153 (RoPE),
+// llama3/cache.rs:169-237 (KV append), text.rs:1258-1281 (grouped decode).
+#pragma once
+
+#include <cmath>
+
+#include "attention.h"
+#include "common.cuh"
+
+namespace dialb200 {
+
+constexpr int kHeadDim = 128;
+
+template <typename Act>
+__device__ __forceinline__ void load4(const Act* p, float (&v)[4]) {
+  const uint2 raw = *reinterpret_cast<const uint2*>(p);
+  const Act* h = reinterpret_cast<const Act*>(&raw);
+#pragma unroll
+  for (int e = 0; e < 4; ++e) v[e] = ActTraits<Act>::to_f(h[e]);
+}
+
+// L2-coherent load for data another CTA of the same grid may have written.
+template <typename Act>
+__device__ __forceinline__ void load4_cg(const Act* p, float (&v)[4]) {
+  const uint2 raw = __ldcg(reinterpret_cast<const uint2*>(p));
+  const Act* h = reinterpret_cast<const Act*>(&raw);
+#pragma unroll
+  for (int e = 0; e < 4; ++e) v[e] = ActTraits<Act>::to_f(h[e]);
+}
+
+template <typename Act>
+__device__ __forceinline__ void store4(Act* p, const float (&v)[4]) {
+  uint2 raw;
+  Act* h = reinterpret_cast<Act*>(&raw);
+#pragma unroll
+  for (int e = 0; e < 4; ++e) h[e] = ActTraits<Act>::from_f(v[e]);
+  *reinterpret_cast<uint2*>(p) = raw;
+}
+
+// Per-head RMSNorm + RoPE of one 128-wide head held 4 dims per lane
+// (lane l: dims 4l..4l+3), with the norm weight (w) and the cos/sin values
+// of dims (l % 16) * 4 .. +3 (c, s) already in registers.  Rounding points:
+// m = act(sqrt(ss/d + eps)), y = act(act(x/m) * w); RoPE element ops rounded
+// to act (candle CPU forms); the partner of dim i is i +/- d/2 (lane l^16).
+template <typename Act>
+__device__ __forceinline__ void norm_rope_pre(float (&x)[4], const float (&w)[4], float eps,
+                                              const float (&c)[4], const float (&s)[4], int lane) {
+  using AT = ActTraits<Act>;
+  float ss = 0.f;
+#pragma unroll
+  for (int e = 0; e < 4; ++e) ss = fmaf(x[e], x[e], ss);
+  ss = warp_sum(ss);
+  const float m = AT::round(__fsqrt_rn(__fdiv_rn(ss, static_cast<float>(kHeadDim)) + eps));
+#pragma unroll
+  for (int e = 0; e < 4; ++e) x[e] = AT::round(AT::round(__fdiv_rn(x[e], m)) * w[e]);
+  float partner[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) partner[e] = __shfl_xor_sync(0xffffffffu, x[e], 16);
+  const bool first = lane < 16;
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const float x1 = first ? x[e] : partner[e];
+    const float x2 = first ? partner[e] : x[e];
+    x[e] = first ? AT::round(AT::round(x1 * c[e]) - AT::round(x2 * s[e]))
+                 : AT::round(AT::round(x1 * s[e]) + AT::round(x2 * c[e]));
+  }
+}
+
+template <typename Act>
+__device__ __forceinline__ void norm_rope(float (&x)[4], const Act* norm_w, float eps,
+                                          const Act* cos_row, const Act* sin_row, int lane) {
+  float w[4], c[4], s[4];
+  load4(norm_w + lane * 4, w);
+  load4(cos_row + (lane & 15) * 4, c);
+  load4(sin_row + (lane & 15) * 4, s);
+  norm_rope_pre<Act>(x, w, eps, c, s, lane);
+}
+
+// A row's context is cut into at most `max_splits` spans of >= 16 tokens.
+constexpr int kMinSplitTokens = 16;
+
+__host__ __device__ __forceinline__ int active_splits(int ctx, int max_splits) {
+  const int need = (ctx + kMinSplitTokens - 1) / kMinSplitTokens;
+  return need < max_splits ? (need < 1 ? 1 : need) : max_splits;
+}
+
+__device__ __forceinline__ int lane_of_token(int t) {
+  return (((t >> 3) & 1) << 4) | (((t >> 2) & 1) << 3) | (((t >> 1) & 1) << 2) | ((t & 1) << 1);
+}
+
+// Scratch shared by the NREP warps of one item.
+struct AttnItemSmem {
+  float kn[kHeadDim];
+  float vn[kHeadDim];
+  int last;
+};
+
+// Process item (m, kvh, split) of `a` with NREP warps; `r` = this warp's
+// index in the group, `bar_id` a named barrier owned by the group.
+template <typename Act, int NREP>
+__device__ void attn_item(const AttnDecodeArgs& a, int m, int kvh, int split, int r, int lane,
+                          AttnItemSmem& sm, int bar_id) {
+  using AT = ActTraits<Act>;
+  const int QH = a.sh.q_heads, KVH = a.sh.kv_heads;
+  const int h = kvh * NREP + r;
+  auto group_sync = [&]() { named_bar_sync(bar_id, NREP * 32); };
+
+  const int sid = a.sid[m];
+  int pos = a.pos[m];
+  const bool bad = pos < 0 || pos >= a.sh.max_pos || pos / kPageTokens >= a.sh.max_blocks;
+  if (bad) {
+    if (lane == 0 && r == 0) set_status(a.status, kStatusBadArgs);
+    pos = 0;
+  }
+  const int ctx = pos + 1;
+  const int32_t* bt = a.block_table + static_cast<size_t>(sid) * a.sh.max_blocks;
+  // Splits actually used by this row: short contexts skip the partial/combine
+  // round trip.  Uniform over the group, so every warp returns together.
+  const int S = active_splits(ctx, a.splits);
+  if (split >= S) return;
+  const int span = ((ctx + S - 1) / S + kPageTokens - 1) / kPageTokens * kPageTokens;
+  const int tok0 = split * span;
+  const int tok1 = min(ctx, tok0 + span);
+  const bool owner = tok0 <= pos && pos < tok1;
+
+  const Act* qkv = reinterpret_cast<const Act*>(a.qkv) + static_cast<size_t>(m) * a.qkv_ld;
+  const Act* cos_row = reinterpret_cast<const Act*>(a.cos) + static_cast<size_t>(pos) * (kHeadDim / 2);
+  const Act* sin_row = reinterpret_cast<const Act*>(a.sin) + static_cast<size_t>(pos) * (kHeadDim / 2);
+  Act* kpool = reinterpret_cast<Act*>(a.kv.k);
+  Act* vpool = reinterpret_cast<Act*>(a.kv.v);
+  const bool do_kv = owner && r == 0 && !bad;
+
+  // Issue every load that does not depend on another one first: the block
+  // id of the span's first page, q (and the new k/v), norm weights, cos/sin.
+  const int blk_first = bt[tok0 / kPageTokens];
+  float q[4], kn[4] = {0.f, 0.f, 0.f, 0.f}, vn[4] = {0.f, 0.f, 0.f, 0.f};
+  load4_cg(qkv + h * kHeadDim + lane * 4, q);
+  if (do_kv) {
+    load4_cg(qkv + (QH + kvh) * kHeadDim + lane * 4, kn);
+    load4_cg(qkv + (QH + KVH + kvh) * kHeadDim + lane * 4, vn);
+  }
+  float qw[4], kw[4], cs[4], sn[4];
+  load4(reinterpret_cast<const Act*>(a.q_norm_w) + lane * 4, qw);
+  load4(reinterpret_cast<const Act*>(a.k_norm_w) + lane * 4, kw);
+  load4(cos_row + (lane & 15) * 4, cs);
+  load4(sin_row + (lane & 15) * 4, sn);
+  // first page's K/V (depends only on the block id)
+  uint2 kr[kPageTokens], vr[kPageTokens];
+  {
+    const size_t base =
+        (static_cast<size_t>(blk_first) * KVH + kvh) * kPageTokens * kHeadDim + lane * 4;
+#pragma unroll
+    for (int j = 0; j < kPageTokens; ++j) {
+      kr[j] = *reinterpret_cast<const uint2*>(kpool + base + j * kHeadDim);
+      vr[j] = *reinterpret_cast<const uint2*>(vpool + base + j * kHeadDim);
+    }
+  }
+
+  norm_rope_pre<Act>(q, qw, a.sh.eps, cs, sn, lane);
+  if (do_kv) {
+    norm_rope_pre<Act>(kn, kw, a.sh.eps, cs, sn, lane);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      sm.kn[lane * 4 + e] = kn[e];
+      sm.vn[lane * 4 + e] = vn[e];
+    }
+    const int blk = bt[pos / kPageTokens];
+    const size_t off = ((static_cast<size_t>(blk) * KVH + kvh) * kPageTokens + (pos % kPageTokens)) *
+                           kHeadDim + lane * 4;
+    store4(kpool + off, kn);
+    store4(vpool + off, vn);
+  }
+  group_sync();
+
+  const float scale = AT::round(1.0f / sqrtf(static_cast<float>(kHeadDim)));
+  float mrun = -INFINITY, lrun = 0.f, acc[4] = {0.f, 0.f, 0.f, 0.f};
+  const int my_tok = ((lane >> 4) & 1) * 8 + ((lane >> 3) & 1) * 4 + ((lane >> 2) & 1) * 2 +
+                     ((lane >> 1) & 1);
+
+  for (int b0 = tok0; b0 < tok1; b0 += kPageTokens) {
+    if (b0 != tok0) {
+      const int blk = bt[b0 / kPageTokens];
+      const size_t base = (static_cast<size_t>(blk) * KVH + kvh) * kPageTokens * kHeadDim + lane * 4;
+#pragma unroll
+      for (int j = 0; j < kPageTokens; ++j) {
+        kr[j] = *reinterpret_cast<const uint2*>(kpool + base + j * kHeadDim);
+        vr[j] = *reinterpret_cast<const uint2*>(vpool + base + j * kHeadDim);
+      }
+    }
+    float v16[kPageTokens];
+#pragma unroll
+    for (int j = 0; j < kPageTokens; ++j) {
+      const Act* kh = reinterpret_cast<const Act*>(&kr[j]);
+      float d = 0.f;
+      if (owner && b0 + j == pos) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) d = fmaf(q[e], sm.kn[lane * 4 + e], d);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) d = fmaf(q[e], AT::to_f(kh[e]), d);
+      }
+      v16[j] = d;
+    }
+    // reduce-scatter: afterwards lane holds the full dot of token my_tok
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float send = (lane & 16) ? v16[i] : v16[i + 8];
+      const float keep = (lane & 16) ? v16[i + 8] : v16[i];
+      v16[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float send = (lane & 8) ? v16[i] : v16[i + 4];
+      const float keep = (lane & 8) ? v16[i + 4] : v16[i];
+      v16[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+    }
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const float send = (lane & 4) ? v16[i] : v16[i + 2];
+      const float keep = (lane & 4) ? v16[i + 2] : v16[i];
+      v16[i] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+    }
+    {
+      const float send = (lane & 2) ? v16[0] : v16[1];
+      const float keep = (lane & 2) ? v16[1] : v16[0];
+      v16[0] = keep + __shfl_xor_sync(0xffffffffu, send, 2);
+    }
+    float s = v16[0] + __shfl_xor_sync(0xffffffffu, v16[0], 1);
+    const bool valid = b0 + my_tok < tok1;
+    s = valid ? AT::round(AT::round(s) * scale) : -INFINITY;
+    const float bm = warp_max(s);
+    const float mnew = fmaxf(mrun, bm);
+    const float p = valid ? expf(s - mnew) : 0.f;
+    const float alpha = expf(mrun - mnew);
+    const float lsum = warp_sum((lane & 1) ? 0.f : p);
+    lrun = lrun * alpha + lsum;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) acc[e] *= alpha;
+#pragma unroll
+    for (int j = 0; j < kPageTokens; ++j) {
+      const float pj = __shfl_sync(0xffffffffu, p, lane_of_token(j));
+      const Act* vh = reinterpret_cast<const Act*>(&vr[j]);
+      if (owner && b0 + j == pos) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc[e] = fmaf(pj, sm.vn[lane * 4 + e], acc[e]);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc[e] = fmaf(pj, AT::to_f(vh[e]), acc[e]);
+      }
+    }
+    mrun = mnew;
+  }
+
+  Act* out =
+      reinterpret_cast<Act*>(a.out) + static_cast<size_t>(m) * a.out_ld + h * kHeadDim + lane * 4;
+  if (S == 1) {
+    float o[4];
+    const float inv = lrun > 0.f ? 1.f / lrun : 0.f;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) o[e] = acc[e] * inv;
+    store4(out, o);
+    group_sync();  // kn/vn reuse by the group's next item
+    return;
+  }
+
+  // partial rows are laid out with the allocation stride a.splits
+  const size_t prow = (static_cast<size_t>(m) * QH + h) * a.splits;
+  __stcg(reinterpret_cast<float4*>(a.part_o + (prow + split) * kHeadDim + lane * 4),
+         make_float4(acc[0], acc[1], acc[2], acc[3]));
+  if (lane == 0) {
+    __stcg(a.part_ml + (prow + split) * 2, mrun);
+    __stcg(a.part_ml + (prow + split) * 2 + 1, lrun);
+  }
+  group_sync();
+  if (r == 0 && lane == 0) {
+    __threadfence();
+    const int old = atomicAdd(a.counters + m * KVH + kvh, 1);
+    sm.last = (old == S - 1);
+  }
+  group_sync();
+  const bool last = sm.last != 0;
+  if (last) {
+    __threadfence();
+    // lane s2 < S holds split s2's (m, l); weights are broadcast by shuffles
+    float ms_l = -INFINITY, ls_l = 0.f;
+    if (lane < S) {
+      ms_l = __ldcg(a.part_ml + (prow + lane) * 2);
+      ls_l = __ldcg(a.part_ml + (prow + lane) * 2 + 1);
+    }
+    const float M = warp_max(ms_l);
+    const float w_l = (lane < S && ms_l != -INFINITY) ? expf(ms_l - M) : 0.f;
+    const float L = warp_sum(w_l * ls_l);
+    float o[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int s0 = 0; s0 < S; s0 += 8) {
+      float4 po[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        po[u] = (s0 + u < S)
+                    ? __ldcg(reinterpret_cast<const float4*>(a.part_o + (prow + s0 + u) * kHeadDim + lane * 4))
+                    : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const float w = __shfl_sync(0xffffffffu, w_l, (s0 + u) & 31);
+        if (s0 + u < S) {
+          o[0] = fmaf(w, po[u].x, o[0]);
+          o[1] = fmaf(w, po[u].y, o[1]);
+          o[2] = fmaf(w, po[u].z, o[2]);
+          o[3] = fmaf(w, po[u].w, o[3]);
+        }
+      }
+    }
+    const float inv = L > 0.f ? 1.f / L : 0.f;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) o[e] *= inv;
+    store4(out, o);
+  }
+  group_sync();
+  if (last && r == 0 && lane == 0) a.counters[m * KVH + kvh] = 0;
+}
+
+}  // namespace dialb200

@@ -799,6 +799,68 @@ int64_t dial_b200_qlinear_resident_bytes(const dial_b200_qlinear* lin) {
   return lin ? lin->L.resident : -1;
 }
 
+int64_t dial_b200_attention_scratch_bytes(const dial_b200_attn_shape* sh, int64_t rows,
+                                          int32_t splits) {
+  if (!sh || rows < 1 || splits < 1) return -1;
+  AttnShape a{};
+  a.q_heads = sh->q_heads;
+  a.kv_heads = sh->kv_heads;
+  a.head_dim = sh->head_dim;
+  return static_cast<int64_t>(attn_decode_scratch_bytes(a, static_cast<int>(rows), splits));
+}
+
+int dial_b200_attention_decode(const dial_b200_attn_shape* sh, const void* qkv, int64_t qkv_ld,
+                               const void* q_norm_w, const void* k_norm_w, const void* cos,
+                               const void* sin, void* k_pages, void* v_pages,
+                               const int32_t* block_table, const int32_t* sids,
+                               const int32_t* positions, void* out, int64_t out_ld, int64_t rows,
+                               int32_t splits, void* scratch, void* stream, char* err, size_t n) {
+  return guarded(err, n, [&] {
+    DIAL_CHECK(sh && qkv && q_norm_w && k_norm_w && cos && sin && k_pages && v_pages &&
+                   block_table && sids && positions && out,
+               "null pointer argument");
+    DIAL_CHECK(sh->head_dim == 128, "head_dim must be 128 (got %d)", sh->head_dim);
+    DIAL_CHECK(sh->q_heads > 0 && sh->kv_heads > 0 && sh->q_heads % sh->kv_heads == 0,
+               "q_heads must be a positive multiple of kv_heads");
+    const int rep = sh->q_heads / sh->kv_heads;
+    DIAL_CHECK(rep == 1 || rep == 2 || rep == 4 || rep == 5 || rep == 8,
+               "q_heads / kv_heads must be 1, 2, 4, 5 or 8 (got %d)", rep);
+    DIAL_CHECK(sh->act == DIAL_ACT_BF16 || sh->act == DIAL_ACT_F16, "act must be BF16 or F16");
+    DIAL_CHECK(rows >= 1 && rows <= 65535, "rows %lld outside [1, 65535]", (long long)rows);
+    DIAL_CHECK(splits >= 1 && splits <= 32, "splits %d outside [1, 32]", splits);
+    DIAL_CHECK(splits == 1 || scratch, "splits > 1 needs scratch");
+    AttnDecodeArgs a{};
+    a.sh.q_heads = sh->q_heads;
+    a.sh.kv_heads = sh->kv_heads;
+    a.sh.head_dim = sh->head_dim;
+    a.sh.max_blocks = sh->max_blocks;
+    a.sh.max_pos = sh->max_pos;
+    a.sh.eps = sh->eps;
+    a.qkv = qkv;
+    a.qkv_ld = static_cast<int>(qkv_ld);
+    a.q_norm_w = q_norm_w;
+    a.k_norm_w = k_norm_w;
+    a.cos = cos;
+    a.sin = sin;
+    a.kv = KvLayer{k_pages, v_pages};
+    a.block_table = block_table;
+    a.sid = sids;
+    a.pos = positions;
+    a.out = out;
+    a.out_ld = static_cast<int>(out_ld);
+    a.M = static_cast<int>(rows);
+    a.splits = splits;
+    if (splits > 1) {
+      const size_t prow = static_cast<size_t>(rows) * sh->q_heads * splits;
+      a.part_o = static_cast<float*>(scratch);
+      a.part_ml = a.part_o + prow * 128;
+      a.counters = reinterpret_cast<int*>(a.part_ml + prow * 2);
+    }
+    a.status = device_status_word();
+    DIAL_CUDA(attn_decode_launch(a, sh->act, static_cast<cudaStream_t>(stream), false));
+  });
+}
+
 int dial_b200_engine_create(const dial_b200_model_config* cfg, int device, dial_b200_engine** out,
                             char* err, size_t n) {
   return guarded(err, n, [&] {

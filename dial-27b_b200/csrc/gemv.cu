@@ -25,6 +25,7 @@
 //    (o_proj/down), or SiLU(gate)*up (fused gate/up projection).
 #include "common.cuh"
 #include "gemv.h"
+#include "gemv_dev.cuh"
 
 namespace dialb200 {
 namespace {
@@ -170,100 +171,6 @@ __device__ void stage_x(const GemvArgs& a, XT* xs, int xs_stride, int* xexp, flo
   }
 }
 
-// ---------------------------------------------------------- chunk compute
-// acc: 16 rows x 8 tokens C fragment.  xrow: this lane's token row in smem.
-template <int FMT, typename XT>
-__device__ __forceinline__ void chunk_mma(const uint8_t* st, int kc, const XT* xrow, int lane,
-                                          float (&acc)[4]) {
-  const int c = lane & 3;
-  if constexpr (FMT == kFmtW8A16Row || FMT == kFmtFp8Row || FMT == kFmtFp8Block128) {
-    const uint4 w0 = *reinterpret_cast<const uint4*>(st + lane * 16);
-    const uint4 w1 = *reinterpret_cast<const uint4*>(st + 512 + lane * 16);
-    const XT* xp = xrow + kc * 64 + c * 16;
-    const uint4 xa = *reinterpret_cast<const uint4*>(xp);
-    const uint4 xb = *reinterpret_cast<const uint4*>(xp + 8);
-    const uint32_t xw[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
-    const uint32_t wa[4] = {w0.x, w0.y, w0.z, w0.w};
-    const uint32_t wb[4] = {w1.x, w1.y, w1.z, w1.w};
-#pragma unroll
-    for (int s = 0; s < 4; ++s) {
-      uint32_t A[4];
-      if constexpr (FMT == kFmtW8A16Row) {
-        A[0] = i8_lo_pair(wa[s]);
-        A[1] = i8_lo_pair(wb[s]);
-        A[2] = i8_hi_pair(wa[s]);
-        A[3] = i8_hi_pair(wb[s]);
-      } else {
-        A[0] = e4m3x2_to_f16x2(static_cast<uint16_t>(wa[s] & 0xffffu));
-        A[1] = e4m3x2_to_f16x2(static_cast<uint16_t>(wb[s] & 0xffffu));
-        A[2] = e4m3x2_to_f16x2(static_cast<uint16_t>(wa[s] >> 16));
-        A[3] = e4m3x2_to_f16x2(static_cast<uint16_t>(wb[s] >> 16));
-      }
-      mma_f16(acc, A, xw[2 * s], xw[2 * s + 1]);
-    }
-  } else if constexpr (FMT == kFmtNvfp4G16) {
-    const uint4 w0 = *reinterpret_cast<const uint4*>(st + lane * 16);
-    const uint4 w1 = *reinterpret_cast<const uint4*>(st + 512 + lane * 16);
-    const uint16_t s0 = *reinterpret_cast<const uint16_t*>(st + 1024 + lane * 2);
-    const uint16_t s1 = *reinterpret_cast<const uint16_t*>(st + 1024 + 64 + lane * 2);
-    const uint32_t sg0 = e4m3x2_to_f16x2(s0);  // row g   : groups (2c, 2c+1)
-    const uint32_t sg1 = e4m3x2_to_f16x2(s1);  // row g+8
-    const __half2 sc0[2] = {__low2half2(*reinterpret_cast<const __half2*>(&sg0)),
-                            __high2half2(*reinterpret_cast<const __half2*>(&sg0))};
-    const __half2 sc1[2] = {__low2half2(*reinterpret_cast<const __half2*>(&sg1)),
-                            __high2half2(*reinterpret_cast<const __half2*>(&sg1))};
-    const uint32_t wa[4] = {w0.x, w0.y, w0.z, w0.w};
-    const uint32_t wb[4] = {w1.x, w1.y, w1.z, w1.w};
-    const XT* xp = xrow + kc * 128 + c * 32;
-#pragma unroll
-    for (int s = 0; s < 4; ++s) {
-      uint32_t oa[4], ob[4];
-      e2m1x8_to_f16x2x4(wa[s], oa);
-      e2m1x8_to_f16x2x4(wb[s], ob);
-      const int gj = s >> 1;
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        __half2 ha = __hmul2(*reinterpret_cast<__half2*>(&oa[q]), sc0[gj]);
-        __half2 hb = __hmul2(*reinterpret_cast<__half2*>(&ob[q]), sc1[gj]);
-        oa[q] = *reinterpret_cast<uint32_t*>(&ha);
-        ob[q] = *reinterpret_cast<uint32_t*>(&hb);
-      }
-      const uint4 xv = *reinterpret_cast<const uint4*>(xp + 8 * s);
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const uint32_t A[4] = {oa[2 * h], ob[2 * h], oa[2 * h + 1], ob[2 * h + 1]};
-        const uint32_t b0 = h ? xv.z : xv.x;
-        const uint32_t b1 = h ? xv.w : xv.y;
-        mma_f16(acc, A, b0, b1);
-      }
-    }
-  } else {  // dense act-dtype weights
-    const uint4 w0 = *reinterpret_cast<const uint4*>(st + lane * 16);
-    const uint4 w1 = *reinterpret_cast<const uint4*>(st + 512 + lane * 16);
-    const XT* xp = xrow + kc * 32 + c * 8;
-    const uint4 xv = *reinterpret_cast<const uint4*>(xp);
-    const uint32_t A0[4] = {w0.x, w1.x, w0.y, w1.y};
-    const uint32_t A1[4] = {w0.z, w1.z, w0.w, w1.w};
-    if constexpr (std::is_same<XT, __nv_bfloat16>::value) {
-      mma_bf16(acc, A0, xv.x, xv.y);
-      mma_bf16(acc, A1, xv.z, xv.w);
-    } else {
-      mma_f16(acc, A0, xv.x, xv.y);
-      mma_f16(acc, A1, xv.z, xv.w);
-    }
-  }
-}
-
-template <typename Act>
-__device__ __forceinline__ float silu_mul_ref(float g, float u) {
-  using AT = ActTraits<Act>;
-  // act(act(g / act(1 + act(exp(-g)))) * u)  (text.rs:816-820 via candle silu)
-  const float e = AT::round(expf(-g));
-  const float d = AT::round(1.f + e);
-  const float s = AT::round(__fdiv_rn(g, d));
-  return s * u;
-}
-
 // ------------------------------------------------------------------ kernel
 template <typename Act, int FMT, int EPI, bool NORM>
 __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const GemvArgs a, const SmemPlan p) {
@@ -318,12 +225,12 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const GemvArgs a, con
                           sbar);
       }
       long long it = 0;
+      int slot = 0;         // ring position and fill round, advanced incrementally
+      uint32_t round = 0;
       bool ok = true;
       for (int t = t0; t < t1 && ok; ++t) {
         const uint8_t* src = a.w.tiles + static_cast<size_t>(t) * C * CB;
         for (int s = 0; s < spt; ++s, ++it) {
-          const int slot = static_cast<int>(it % NS);
-          const uint32_t round = static_cast<uint32_t>(it / NS);
           if (round > 0 && !mbar_wait(&empty[slot], (round - 1) & 1u, a.status,
                                       kStatusEmptyWaitTimeout)) {
             ok = false;
@@ -334,6 +241,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const GemvArgs a, con
           mbar_arrive_expect_tx(&full[slot], bytes);
           bulk_g2s(ring + static_cast<size_t>(slot) * kStageBytes,
                    src + static_cast<size_t>(s) * kStageChunks * CB, bytes, &full[slot]);
+          if (++slot == NS) {
+            slot = 0;
+            ++round;
+          }
         }
       }
       // Drain: the most recent NS stages must have landed before the CTA may
@@ -361,7 +272,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const GemvArgs a, con
   const XT* xrow = xs + static_cast<size_t>(tok) * p.xs_stride;
   const int I = a.w.N / 2;
 
-  long long it = 0;
+  int slot = 0;
+  uint32_t round = 0;
   bool ok = true;
   int tile_i = 0;
   for (int t = t0; t < t1; ++t, ++tile_i) {
@@ -376,11 +288,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const GemvArgs a, con
         rb_lo = rb_hi = (16 * t) / 128 - lo0;
       }
     }
-    for (int s = 0; s < spt; ++s, ++it) {
-      const int slot = static_cast<int>(it % NS);
-      if (ok && !mbar_wait(&full[slot], static_cast<uint32_t>(it / NS) & 1u, a.status,
-                           kStatusFullWaitTimeout))
-        ok = false;
+    for (int s = 0; s < spt; ++s) {
+      if (ok && !mbar_wait(&full[slot], round & 1u, a.status, kStatusFullWaitTimeout)) ok = false;
       const int nch = min(kStageChunks, C - s * kStageChunks);
       const uint8_t* st = ring + static_cast<size_t>(slot) * kStageBytes;
       if (ok) {
@@ -406,6 +315,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const GemvArgs a, con
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[slot]);
+      if (++slot == NS) {
+        slot = 0;
+        ++round;
+      }
     }
     // ---- cross-warp reduction (double-buffered by tile parity)
     float* rb = red + (tile_i & 1) * (kNW * 128);

@@ -1,0 +1,111 @@
+// Device-side pieces of the decode GEMV (chunk conversion + MMA, SwiGLU).
+//
+// Chunk layout (built by layout.cu): 16 weight rows x KCH inputs per chunk;
+// lane l = (g, c) = (l / 4, l % 4) owns bytes [16l, 16l+16) (row g) and
+// [512 + 16l, ...) (row g+8).  Within its 16 bytes the lane's inputs are in
+// natural order; the m16n8k16 K index is permuted identically for the
+// activation fragment, so no shuffle is needed.
+#pragma once
+
+#include <type_traits>
+
+#include "common.cuh"
+#include "qlinear.h"
+
+namespace dialb200 {
+
+// ---------------------------------------------------------- chunk compute
+// acc: 16 rows x 8 tokens C fragment.  xrow: this lane's token row in smem.
+template <int FMT, typename XT>
+__device__ __forceinline__ void chunk_mma(const uint8_t* st, int kc, const XT* xrow, int lane,
+                                          float (&acc)[4]) {
+  const int c = lane & 3;
+  if constexpr (FMT == kFmtW8A16Row || FMT == kFmtFp8Row || FMT == kFmtFp8Block128) {
+    const uint4 w0 = *reinterpret_cast<const uint4*>(st + lane * 16);
+    const uint4 w1 = *reinterpret_cast<const uint4*>(st + 512 + lane * 16);
+    const XT* xp = xrow + kc * 64 + c * 16;
+    const uint4 xa = *reinterpret_cast<const uint4*>(xp);
+    const uint4 xb = *reinterpret_cast<const uint4*>(xp + 8);
+    const uint32_t xw[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
+    const uint32_t wa[4] = {w0.x, w0.y, w0.z, w0.w};
+    const uint32_t wb[4] = {w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+    for (int s = 0; s < 4; ++s) {
+      uint32_t A[4];
+      if constexpr (FMT == kFmtW8A16Row) {
+        A[0] = i8_lo_pair(wa[s]);
+        A[1] = i8_lo_pair(wb[s]);
+        A[2] = i8_hi_pair(wa[s]);
+        A[3] = i8_hi_pair(wb[s]);
+      } else {
+        A[0] = e4m3x2_to_f16x2(static_cast<uint16_t>(wa[s] & 0xffffu));
+        A[1] = e4m3x2_to_f16x2(static_cast<uint16_t>(wb[s] & 0xffffu));
+        A[2] = e4m3x2_to_f16x2(static_cast<uint16_t>(wa[s] >> 16));
+        A[3] = e4m3x2_to_f16x2(static_cast<uint16_t>(wb[s] >> 16));
+      }
+      mma_f16(acc, A, xw[2 * s], xw[2 * s + 1]);
+    }
+  } else if constexpr (FMT == kFmtNvfp4G16) {
+    const uint4 w0 = *reinterpret_cast<const uint4*>(st + lane * 16);
+    const uint4 w1 = *reinterpret_cast<const uint4*>(st + 512 + lane * 16);
+    const uint16_t s0 = *reinterpret_cast<const uint16_t*>(st + 1024 + lane * 2);
+    const uint16_t s1 = *reinterpret_cast<const uint16_t*>(st + 1024 + 64 + lane * 2);
+    const uint32_t sg0 = e4m3x2_to_f16x2(s0);  // row g   : groups (2c, 2c+1)
+    const uint32_t sg1 = e4m3x2_to_f16x2(s1);  // row g+8
+    const __half2 sc0[2] = {__low2half2(*reinterpret_cast<const __half2*>(&sg0)),
+                            __high2half2(*reinterpret_cast<const __half2*>(&sg0))};
+    const __half2 sc1[2] = {__low2half2(*reinterpret_cast<const __half2*>(&sg1)),
+                            __high2half2(*reinterpret_cast<const __half2*>(&sg1))};
+    const uint32_t wa[4] = {w0.x, w0.y, w0.z, w0.w};
+    const uint32_t wb[4] = {w1.x, w1.y, w1.z, w1.w};
+    const XT* xp = xrow + kc * 128 + c * 32;
+#pragma unroll
+    for (int s = 0; s < 4; ++s) {
+      uint32_t oa[4], ob[4];
+      e2m1x8_to_f16x2x4(wa[s], oa);
+      e2m1x8_to_f16x2x4(wb[s], ob);
+      const int gj = s >> 1;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        __half2 ha = __hmul2(*reinterpret_cast<__half2*>(&oa[q]), sc0[gj]);
+        __half2 hb = __hmul2(*reinterpret_cast<__half2*>(&ob[q]), sc1[gj]);
+        oa[q] = *reinterpret_cast<uint32_t*>(&ha);
+        ob[q] = *reinterpret_cast<uint32_t*>(&hb);
+      }
+      const uint4 xv = *reinterpret_cast<const uint4*>(xp + 8 * s);
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const uint32_t A[4] = {oa[2 * h], ob[2 * h], oa[2 * h + 1], ob[2 * h + 1]};
+        const uint32_t b0 = h ? xv.z : xv.x;
+        const uint32_t b1 = h ? xv.w : xv.y;
+        mma_f16(acc, A, b0, b1);
+      }
+    }
+  } else {  // dense act-dtype weights
+    const uint4 w0 = *reinterpret_cast<const uint4*>(st + lane * 16);
+    const uint4 w1 = *reinterpret_cast<const uint4*>(st + 512 + lane * 16);
+    const XT* xp = xrow + kc * 32 + c * 8;
+    const uint4 xv = *reinterpret_cast<const uint4*>(xp);
+    const uint32_t A0[4] = {w0.x, w1.x, w0.y, w1.y};
+    const uint32_t A1[4] = {w0.z, w1.z, w0.w, w1.w};
+    if constexpr (std::is_same<XT, __nv_bfloat16>::value) {
+      mma_bf16(acc, A0, xv.x, xv.y);
+      mma_bf16(acc, A1, xv.z, xv.w);
+    } else {
+      mma_f16(acc, A0, xv.x, xv.y);
+      mma_f16(acc, A1, xv.z, xv.w);
+    }
+  }
+}
+
+template <typename Act>
+__device__ __forceinline__ float silu_mul_ref(float g, float u) {
+  using AT = ActTraits<Act>;
+  // act(act(g / act(1 + act(exp(-g)))) * u)  (text.rs:816-820 via candle silu)
+  const float e = AT::round(expf(-g));
+  const float d = AT::round(1.f + e);
+  const float s = AT::round(__fdiv_rn(g, d));
+  return s * u;
+}
+
+}  // namespace dialb200

@@ -32,6 +32,18 @@ if not LIB_PATH.exists():
 lib = C.CDLL(str(LIB_PATH))
 
 
+class AttnShape(C.Structure):
+    _fields_ = [
+        ("q_heads", C.c_int32),
+        ("kv_heads", C.c_int32),
+        ("head_dim", C.c_int32),
+        ("max_blocks", C.c_int32),
+        ("max_pos", C.c_int32),
+        ("eps", C.c_float),
+        ("act", C.c_int32),
+    ]
+
+
 class ModelConfig(C.Structure):
     _fields_ = [
         ("hidden_size", C.c_int32),
@@ -69,6 +81,10 @@ _SIGS = {
     "dial_b200_qlinear_in_dim": (_i64, [_vp]),
     "dial_b200_qlinear_out_dim": (_i64, [_vp]),
     "dial_b200_qlinear_resident_bytes": (_i64, [_vp]),
+    "dial_b200_attention_scratch_bytes": (_i64, [C.POINTER(AttnShape), _i64, _i32]),
+    "dial_b200_attention_decode": (C.c_int, [C.POINTER(AttnShape), _vp, _i64, _vp, _vp, _vp, _vp, _vp,
+                                             _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i32, _vp, _vp,
+                                             *_err]),
     "dial_b200_engine_create": (C.c_int, [C.POINTER(ModelConfig), C.c_int, C.POINTER(_vp), *_err]),
     "dial_b200_engine_destroy": (None, [_vp]),
     "dial_b200_engine_load_synthetic": (C.c_int, [_vp, _u64, _vp, *_err]),

@@ -99,6 +99,47 @@ int64_t dial_b200_qlinear_out_dim(const dial_b200_qlinear* lin);
 int64_t dial_b200_qlinear_resident_bytes(const dial_b200_qlinear* lin);
 
 /* ------------------------------------------------------------------------ */
+/* Decode attention op                                                      */
+/* ------------------------------------------------------------------------ */
+
+/* Shape of the fused decode attention (head_dim must be 128). */
+typedef struct {
+  int32_t q_heads;
+  int32_t kv_heads;
+  int32_t head_dim;
+  int32_t max_blocks; /* block-table row length (16-token pages per session) */
+  int32_t max_pos;    /* rows of the cos/sin tables */
+  float eps;          /* q/k RMSNorm epsilon */
+  int32_t act;        /* DIAL_ACT_BF16 or DIAL_ACT_F16 */
+} dial_b200_attn_shape;
+
+/* Bytes of scratch dial_b200_attention_decode needs for `rows` rows and
+ * `splits` KV splits (0 when splits == 1). */
+int64_t dial_b200_attention_scratch_bytes(const dial_b200_attn_shape* sh, int64_t rows,
+                                          int32_t splits);
+
+/* One decode token per row, the fusion of QwenAttention::forward's q/k
+ * RMSNorm (qwen3_vl/text.rs:1466-1467,1513-1514), RoPE (text.rs:1143-1153),
+ * KV append (Cache::process_kv_decode_in_place, llama3/cache.rs:169-237) and
+ * grouped_decode_attention (text.rs:1258-1281) over paged KV:
+ *   qkv [rows, qkv_ld]: q | k | v of the new tokens (before norm and RoPE);
+ *   k_pages / v_pages [num_blocks][kv_heads][16][128]; block_table
+ *   [sessions][max_blocks]; sids / positions [rows] (device);
+ *   out [rows, out_ld] receives the attention output (q_heads * 128 wide).
+ * Row m appends its K/V at positions[m] of session sids[m] and attends to
+ * positions 0..positions[m]; rows must name distinct sessions (a row reads
+ * only keys already in the pages plus its own).  `scratch` (device, >=
+ * dial_b200_attention_scratch_bytes) must be zero-filled before its first
+ * use; the kernels leave it ready for the next call. */
+int dial_b200_attention_decode(const dial_b200_attn_shape* sh, const void* qkv, int64_t qkv_ld,
+                               const void* q_norm_w, const void* k_norm_w, const void* cos,
+                               const void* sin, void* k_pages, void* v_pages,
+                               const int32_t* block_table, const int32_t* sids,
+                               const int32_t* positions, void* out, int64_t out_ld, int64_t rows,
+                               int32_t splits, void* scratch, void* stream, char* err,
+                               size_t err_size);
+
+/* ------------------------------------------------------------------------ */
 /* Decoder layers: Forwarder + per-session KV cache + Worker                */
 /* ------------------------------------------------------------------------ */
 
