@@ -40,3 +40,20 @@ def attention_decode(sh: AttnShape, qkv, q_norm_w, k_norm_w, cos, sin, k_pages, 
          C.c_void_p(scratch.data_ptr() if scratch is not None else 0), C.c_void_p(stream))
     return out
 
+
+NOALLOC_MAX_PART_ROWS = 2048
+NOALLOC_MAX_COUNTERS = 1024
+
+
+def attention_decode_noalloc(sh: AttnShape, qkv, q_norm_w, k_norm_w, cos, sin, k_pages, v_pages,
+                             block_table, sids, positions, out, splits: int = 1):
+    """attention_decode with the split-KV scratch in the library's static
+    device array: allocates nothing.  Limits: rows * q_heads * splits <=
+    2048 and rows * kv_heads <= 1024 when splits > 1.  Calls that overlap on
+    one device race on that scratch."""
+    rows = qkv.shape[0]
+    stream = torch.cuda.current_stream(qkv.device).cuda_stream
+    call("dial_b200_attention_decode_noalloc", C.byref(sh), _p(qkv), qkv.shape[1], _p(q_norm_w),
+         _p(k_norm_w), _p(cos), _p(sin), _p(k_pages), _p(v_pages), _p(block_table), _p(sids),
+         _p(positions), _p(out), out.shape[1], rows, splits, C.c_void_p(stream))
+    return out

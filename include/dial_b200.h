@@ -139,6 +139,29 @@ int dial_b200_attention_decode(const dial_b200_attn_shape* sh, const void* qkv, 
                                int32_t splits, void* scratch, void* stream, char* err,
                                size_t err_size);
 
+/* Limits of the static scratch behind dial_b200_attention_decode_noalloc. */
+#define DIAL_B200_NOALLOC_MAX_PART_ROWS 2048 /* rows * q_heads * splits */
+#define DIAL_B200_NOALLOC_MAX_COUNTERS 1024  /* rows * kv_heads */
+
+/* dial_b200_attention_decode without the scratch argument: the split-KV
+ * partials live in a fixed file-scope device array (about 1.07 MB per
+ * device), so the call allocates nothing, for hosts that may not allocate on
+ * the call path.  No counterpart in the reference (its attention allocates
+ * through candle on every call).  Rejects (DIAL_ERR_INVALID) splits > 1 when
+ * rows * q_heads * splits > DIAL_B200_NOALLOC_MAX_PART_ROWS or rows *
+ * kv_heads > DIAL_B200_NOALLOC_MAX_COUNTERS.  The first call on a device sets
+ * the scratch up (address lookup, zero fill, a synchronize): make it before
+ * any stream capture.  Calls that overlap in time on one device share the
+ * scratch and race: serialize them.  Device-side status of this entry point
+ * goes to its own static word, which dial_b200_device_status does not read. */
+int dial_b200_attention_decode_noalloc(const dial_b200_attn_shape* sh, const void* qkv,
+                                       int64_t qkv_ld, const void* q_norm_w, const void* k_norm_w,
+                                       const void* cos, const void* sin, void* k_pages,
+                                       void* v_pages, const int32_t* block_table,
+                                       const int32_t* sids, const int32_t* positions, void* out,
+                                       int64_t out_ld, int64_t rows, int32_t splits, void* stream,
+                                       char* err, size_t err_size);
+
 /* ------------------------------------------------------------------------ */
 /* Decoder layers: Forwarder + per-session KV cache + Worker                */
 /* ------------------------------------------------------------------------ */
