@@ -10,6 +10,7 @@
 #include <cstdio>
 #include <cstring>
 #include <map>
+#include <tuple>
 #include <memory>
 #include <string>
 #include <vector>
@@ -316,6 +317,9 @@ struct dial_b200_engine {
   int32_t* h_out = nullptr;  // pinned: [max_rows] tokens + status
   int* status = nullptr;
   std::map<int64_t, std::unique_ptr<Graph>> step_graphs, loop_graphs;
+  // pipeline-stage decode graphs keyed by (rows, tokens in, hidden, tokens out)
+  std::map<std::tuple<int64_t, const void*, const void*, const void*>, std::unique_ptr<Graph>>
+      stage_graphs;
 
   size_t esz() const { return 2; }
   LayerW& layer(int l) {
@@ -877,6 +881,7 @@ void dial_b200_engine_destroy(dial_b200_engine* eng) {
   cudaStreamSynchronize(eng->stream);
   eng->step_graphs.clear();
   eng->loop_graphs.clear();
+  eng->stage_graphs.clear();
   if (eng->h_in) cudaFreeHost(eng->h_in);
   if (eng->h_out) cudaFreeHost(eng->h_out);
   cudaStream_t s = eng->stream;
@@ -1117,6 +1122,68 @@ int dial_b200_decode_loop_state(dial_b200_engine* eng, int64_t rows, int32_t* to
     int st = 0;
     DIAL_CUDA(cudaMemcpy(&st, eng->status, 4, cudaMemcpyDeviceToHost));
     check_status(eng, st);
+  });
+}
+
+int dial_b200_stage_prepare(dial_b200_engine* eng, int64_t rows, const int32_t* sids,
+                            const int32_t* positions, char* err, size_t n) {
+  return guarded(err, n, [&] {
+    DIAL_CHECK(eng && sids && positions, "null pointer argument");
+    DIAL_CUDA(cudaSetDevice(eng->device));
+    const int M = static_cast<int>(rows);
+    DIAL_CHECK(M >= 1 && M <= eng->max_rows_decode && M <= 256, "rows %d out of range", M);
+    for (int i = 0; i < M; ++i) {
+      DIAL_CHECK(sids[i] >= 0 && sids[i] < eng->cfg.max_sessions, "session %d out of range",
+                 sids[i]);
+      DIAL_CHECK(positions[i] >= 0 && positions[i] < eng->cfg.max_seq_len,
+                 "position %d outside the KV capacity %d", positions[i], eng->cfg.max_seq_len);
+    }
+    DIAL_CUDA(cudaStreamSynchronize(eng->stream));
+    DIAL_CUDA(cudaMemcpy(eng->sid.p, sids, M * 4, cudaMemcpyHostToDevice));
+    DIAL_CUDA(cudaMemcpy(eng->pos.p, positions, M * 4, cudaMemcpyHostToDevice));
+  });
+}
+
+int dial_b200_stage_step(dial_b200_engine* eng, int64_t rows, const int32_t* tokens_dev,
+                         void* hidden, int32_t* tokens_out_dev, void* stream, char* err,
+                         size_t n) {
+  return guarded(err, n, [&] {
+    DIAL_CHECK(eng && hidden, "null pointer argument");
+    DIAL_CUDA(cudaSetDevice(eng->device));
+    const int M = static_cast<int>(rows);
+    DIAL_CHECK(M >= 1 && M <= eng->max_rows_decode && M <= 256, "rows %d out of range", M);
+    DIAL_CHECK(!eng->cfg.has_embed || tokens_dev, "the first stage needs device token ids");
+    DIAL_CHECK(!eng->cfg.has_head || tokens_out_dev, "the last stage needs a token output");
+    check_weights(eng, eng->cfg.first_layer, eng->cfg.num_layers);
+    if (eng->cfg.has_head) DIAL_CHECK(eng->lm_head.ready(), "lm_head weights not loaded");
+    const auto key = std::make_tuple(rows, static_cast<const void*>(tokens_dev),
+                                     static_cast<const void*>(hidden),
+                                     static_cast<const void*>(tokens_out_dev));
+    auto it = eng->stage_graphs.find(key);
+    if (it == eng->stage_graphs.end()) {
+      cudaStream_t s = eng->stream;
+      auto g = std::make_unique<Graph>();
+      DIAL_CUDA(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
+      try {
+        if (eng->cfg.has_embed)
+          DIAL_CUDA(embed_launch(eng->embed.p, tokens_dev, M, eng->V, eng->H, hidden, eng->H,
+                                 eng->status, s, g_tuning().pdl));
+        for (int li = 0; li < eng->cfg.num_layers; ++li)
+          layer_decode(eng, eng->layers[li], hidden, M, s);
+        if (eng->cfg.has_head) head_forward(eng, hidden, M, nullptr, tokens_out_dev, s);
+        DIAL_CUDA(advance_launch(nullptr, nullptr, eng->pos.as<int32_t>(), M, s,
+                                 g_tuning().pdl));
+      } catch (...) {
+        cudaGraph_t tmp = nullptr;
+        cudaStreamEndCapture(s, &tmp);
+        if (tmp) cudaGraphDestroy(tmp);
+        throw;
+      }
+      DIAL_CUDA(cudaStreamEndCapture(s, &g->g));
+      DIAL_CUDA(cudaGraphInstantiate(&g->exec, g->g, 0));
+      it = eng->stage_graphs.emplace(key, std::move(g)).first;
+    }
+    DIAL_CUDA(cudaGraphLaunch(it->second->exec, static_cast<cudaStream_t>(stream)));
   });
 }
 

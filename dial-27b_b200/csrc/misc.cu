@@ -73,14 +73,14 @@ __global__ void argmax_kernel(const Act* __restrict__ logits, int ld, int V,
   }
 }
 
-// next step: tokens <- sampled, pos += 1
+// next step: tokens <- sampled (when a stage samples), pos += 1
 __global__ void advance_kernel(const int32_t* __restrict__ sampled, int32_t* __restrict__ tokens,
                                int32_t* __restrict__ pos, int M) {
   pdl_launch_dependents();
   pdl_wait();
   const int i = threadIdx.x;
   if (i < M) {
-    tokens[i] = sampled[i];
+    if (sampled) tokens[i] = sampled[i];
     pos[i] += 1;
   }
 }

@@ -88,6 +88,8 @@ _SIGS = {
     "dial_b200_attention_decode_noalloc": (C.c_int, [C.POINTER(AttnShape), _vp, _i64, _vp, _vp, _vp, _vp,
                                                      _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i32,
                                                      _vp, *_err]),
+    "dial_b200_stage_prepare": (C.c_int, [_vp, _i64, _vp, _vp, *_err]),
+    "dial_b200_stage_step": (C.c_int, [_vp, _i64, _vp, _vp, _vp, _vp, *_err]),
     "dial_b200_engine_create": (C.c_int, [C.POINTER(ModelConfig), C.c_int, C.POINTER(_vp), *_err]),
     "dial_b200_engine_destroy": (None, [_vp]),
     "dial_b200_engine_load_synthetic": (C.c_int, [_vp, _u64, _vp, *_err]),

@@ -257,6 +257,22 @@ class Engine:
         call("dial_b200_decode_loop_state", self._h, rows, _np_ptr(t), _np_ptr(p))
         return t, p
 
+    def stage_prepare(self, sids, positions):
+        """Set the decode rows' sessions/positions on the device for stage_step."""
+        s = np.ascontiguousarray(np.asarray(sids, dtype=np.int32))
+        p = np.ascontiguousarray(np.asarray(positions, dtype=np.int32))
+        call("dial_b200_stage_prepare", self._h, s.size, _np_ptr(s), _np_ptr(p))
+
+    def stage_step(self, rows: int, tokens: torch.Tensor | None, hidden: torch.Tensor,
+                   tokens_out: torch.Tensor | None = None):
+        """One graph-captured decode step of this engine's stage on the current
+        stream (embed if it owns the embedding, head + argmax if it owns the
+        head); positions advance on the device."""
+        self._check_hidden(hidden)
+        ptr = lambda t: C.c_void_p(t.data_ptr() if t is not None else 0)  # noqa: E731
+        call("dial_b200_stage_step", self._h, rows, ptr(tokens), ptr(hidden), ptr(tokens_out),
+             self._stream_ptr())
+
     def session_fill_random(self, session: int, length: int, seed: int, std: float = 1.0):
         call("dial_b200_session_fill_random", self._h, session, length, seed,
              _np_ptr(normal_table_bits(std)))

@@ -1,0 +1,111 @@
+"""W8A16 linear microbenchmark over the Qwen3-8B projection shapes.
+
+    PYTHONPATH=dial-27b_b200 python -m dial_b200.microbench [--shapes q,gate_up] [--M 1,4,16]
+        [--iters 20] [--min-footprint-mb 512]
+
+Each case builds enough copies of the quantized weight that one rotation
+through them streams more than the L2 cache (126 MB) from HBM, captures the
+rotation of dial_b200_qlinear_forward calls in a CUDA graph, replays it and
+times the replays with CUDA events on the launching stream.  One JSON line per
+case: microseconds per forward, algorithmic bytes (int8 weights + f32 row
+scales + bf16 activations in and out) and FLOPs (2*M*N*K), GB/s and TFLOP/s,
+and the fraction of the measured HBM copy bandwidth.
+
+Shapes follow the W8A16 linear microbench of the baseline: K x N =
+4096x4096 (q/o), 4096x1024 (k/v), 4096x12288 (gate/up), 12288x4096 (down)
+plus the fused 4096x6144 (QKV) and 4096x24576 (gate+up) layouts the decoder
+uses (text.rs:1428-1432, 634-637).  Weights are int8 codes with per-row
+scales drawn from a seeded generator: the kernel's speed does not depend on
+the values.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+from pathlib import Path
+
+import numpy as np
+import torch
+
+from .linear import CudaW8A16Linear
+
+SHAPES = {  # name: (K, N)
+    "q": (4096, 4096),
+    "kv": (4096, 1024),
+    "gate": (4096, 12288),
+    "down": (12288, 4096),
+    "qkv": (4096, 6144),
+    "gate_up": (4096, 24576),
+}
+
+
+def measured_hbm_gbs() -> tuple[float, str]:
+    p = Path(__file__).resolve().parents[2] / "MEASURED_PEAKS.json"
+    if p.exists():
+        return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def run_case(name: str, M: int, iters: int, min_footprint: int, device: int = 0) -> dict:
+    K, N = SHAPES[name]
+    rng = np.random.default_rng(10 + list(SHAPES).index(name))
+    q = rng.integers(-127, 128, size=(N, K), dtype=np.int8)
+    s = (rng.random(N, dtype=np.float32) * 1e-3 + 1e-4).astype(np.float32)
+    wbytes = N * K + 4 * N
+    copies = max(2, math.ceil(min_footprint / wbytes))
+    lins = [CudaW8A16Linear.from_quantized(q, s, act=torch.bfloat16) for _ in range(copies)]
+    dev = torch.device("cuda", device)
+    x = torch.randn(M, K, generator=torch.Generator().manual_seed(20), dtype=torch.float32)
+    x = x.to(dev, torch.bfloat16)
+    for lin in lins:  # warm-up outside capture (first call per device sets up status memory)
+        lin(x)
+    torch.cuda.synchronize(dev)
+
+    g = torch.cuda.CUDAGraph()
+    stream = torch.cuda.Stream(dev)
+    with torch.cuda.stream(stream):
+        for lin in lins:
+            lin(x)
+        stream.synchronize()
+        with torch.cuda.graph(g, stream=stream, capture_error_mode="thread_local"):
+            outs = [lin(x) for lin in lins]
+    for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize(dev)
+    cur = torch.cuda.current_stream(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(cur)
+    for _ in range(iters):
+        g.replay()
+    e1.record(cur)
+    e1.synchronize()
+    us = e0.elapsed_time(e1) * 1000.0 / (iters * copies)
+    del outs
+    nbytes = lins[0].resident_bytes() + 2 * M * K + 2 * M * N
+    flops = 2.0 * M * N * K
+    peak, src = measured_hbm_gbs()
+    gbs = nbytes / (us * 1e-6) / 1e9
+    return {"shape": name, "K": K, "N": N, "M": M, "us": us, "bytes": nbytes, "GB_s": gbs,
+            "frac_hbm": gbs / peak, "TFLOP_s": flops / (us * 1e-6) / 1e12, "copies": copies,
+            "peak_gbs": peak, "peak_source": src,
+            "l2": f"rotation over {copies} weight copies ({copies * wbytes / 2**20:.0f} MiB)"}
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--shapes", default=",".join(SHAPES))
+    ap.add_argument("--M", default="1,4,16,128,2048")
+    ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--min-footprint-mb", type=int, default=512)
+    args = ap.parse_args(argv)
+    torch.cuda.set_device(0)
+    for name in args.shapes.split(","):
+        for M in (int(m) for m in args.M.split(",")):
+            r = run_case(name, M, args.iters, args.min_footprint_mb << 20)
+            print(json.dumps(r), flush=True)
+
+
+if __name__ == "__main__":
+    main()

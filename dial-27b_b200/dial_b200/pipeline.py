@@ -1,0 +1,170 @@
+"""Pipeline stages over NCCL: the in-box replacement of DIAL's Master/Worker
+layer handoff.
+
+In the reference the Master ships the hidden state of a token to each remote
+Worker that owns the next contiguous layer range and waits for it to come back
+(spm/client.rs:391-453 `Client::forward_batch`, spm/worker.rs:670-893
+`Worker::handle_master_client`), one TCP round trip per remote segment per
+token.  Inside one box the topology's layer ranges become one process per GPU
+(launched by torchrun) and the hidden state moves stage to stage with NCCL
+send/recv over NVLink; the last stage runs the head and returns the sampled
+token id to stage 0, which embeds it for the next step.  Everything is
+stream-ordered: no host synchronisation happens inside a step, so the host of
+every rank runs ahead and a stage's kernels start as soon as its input lands.
+
+`StageRunner` drives one rank.  It only needs an engine with `embed`,
+`forward_local_batch`, `head`, `dtype` and a torch device, so the same stage
+logic runs on CPU with `gloo` ranks in the tests.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+from .topology import Topology
+
+
+@dataclass
+class StagePlan:
+    rank: int
+    world: int
+    first_layer: int
+    num_layers: int
+
+    @property
+    def is_first(self) -> bool:
+        return self.rank == 0
+
+    @property
+    def is_last(self) -> bool:
+        return self.rank == self.world - 1
+
+
+def plan_stages(num_layers: int, world: int, topology: Topology | None = None) -> list[StagePlan]:
+    """Stage s owns one contiguous layer range: the topology's node ranges
+    ordered by first layer (spm/topology.rs), or an even split."""
+    topo = topology if topology is not None else Topology.even_split(num_layers, world)
+    stages = topo.stages(num_layers)
+    if len(stages) != world:
+        raise ValueError(f"topology has {len(stages)} stages but the job has {world} ranks")
+    return [StagePlan(r, world, first, count) for r, (_, first, count) in enumerate(stages)]
+
+
+class StageRunner:
+    """One pipeline stage on one rank (one GPU)."""
+
+    def __init__(self, engine, plan: StagePlan, hidden_size: int, session: int = 0,
+                 group=None):
+        self.eng = engine
+        self.plan = plan
+        self.H = hidden_size
+        self.session = session
+        self.group = group
+        self.device = getattr(engine, "torch_device", None) or torch.device("cuda", engine.device)
+        self.dtype = engine.dtype
+        self._batch_names = [f"model.layers.{i}" for i in
+                             range(plan.first_layer, plan.first_layer + plan.num_layers)]
+
+    def _batch(self, index_pos: int):
+        first = self.plan.first_layer
+        return [(n, index_pos, first + i) for i, n in enumerate(self._batch_names)]
+
+    def _send(self, t: torch.Tensor, dst: int):
+        dist.send(t, dst, group=self.group)
+
+    def _recv(self, t: torch.Tensor, src: int):
+        dist.recv(t, src, group=self.group)
+
+    def step(self, tokens: torch.Tensor | None, rows: int, index_pos: int) -> torch.Tensor | None:
+        """Run `rows` tokens starting at `index_pos` through this stage with the
+        engine's layer-range call (prefill, or decode without graphs).
+
+        Stage 0 takes the token ids (device int32 [rows]) and returns the next
+        token id (device int32 [1]) once the last stage sends it back; the
+        other stages return None (the last stage returns its token too)."""
+        p = self.plan
+        if p.is_first:
+            x = self.eng.embed(tokens)
+        else:
+            x = torch.empty(rows, self.H, dtype=self.dtype, device=self.device)
+            self._recv(x, p.rank - 1)
+        x = self.eng.forward_local_batch(x, self._batch(index_pos), self.session)
+        tok = None
+        if not p.is_last:
+            self._send(x, p.rank + 1)
+        else:
+            tok = self.eng.head(x[rows - 1:rows].contiguous())
+            if p.world > 1:
+                self._send(tok, 0)
+        if p.is_first and p.world > 1:
+            tok = torch.empty(1, dtype=torch.int32, device=self.device)
+            self._recv(tok, p.world - 1)
+        return tok
+
+    # ------------------------------------------------------- graph decode
+    @property
+    def graphs(self) -> bool:
+        return hasattr(self.eng, "stage_step")
+
+    def decode_prepare(self, index_pos: int):
+        """Fix the decode buffers and put the position on the device (engines
+        with stage_step: every later decode_step is one graph launch with no
+        host synchronisation)."""
+        self.pos = index_pos
+        if self.graphs:
+            self.eng.stage_prepare([self.session], [index_pos])
+            self._x = torch.empty(1, self.H, dtype=self.dtype, device=self.device)
+            self._tok_in = torch.zeros(1, dtype=torch.int32, device=self.device)
+            self._tok_out = torch.zeros(1, dtype=torch.int32, device=self.device)
+
+    def decode_step(self, token: torch.Tensor | None) -> torch.Tensor | None:
+        """One bs1 decode token through this stage; stage 0 passes the current
+        token (device int32 [1]) and gets the next one back."""
+        if not self.graphs:
+            tok = self.step(token, 1, self.pos)
+            self.pos += 1
+            return tok
+        p, x = self.plan, self._x
+        if p.is_first:
+            if token is not None and token.data_ptr() != self._tok_in.data_ptr():
+                self._tok_in.copy_(token)
+        else:
+            self._recv(x, p.rank - 1)
+        self.eng.stage_step(1, self._tok_in if p.is_first else None, x,
+                            self._tok_out if p.is_last else None)
+        self.pos += 1
+        tok = None
+        if not p.is_last:
+            self._send(x, p.rank + 1)
+        else:
+            tok = self._tok_out
+            if p.world > 1:
+                self._send(tok, 0)
+        if p.is_first:
+            if p.world > 1:
+                self._recv(self._tok_in, p.world - 1)
+            else:
+                self._tok_in.copy_(self._tok_out)
+            tok = self._tok_in
+        return tok
+
+    def generate(self, prompt, n_gen: int) -> np.ndarray | None:
+        """Greedy generation of `n_gen` tokens after `prompt` (host ids on
+        stage 0; ignored elsewhere).  Returns the ids on stage 0, else None."""
+        n = len(prompt)
+        toks = None
+        if self.plan.is_first:
+            toks = torch.as_tensor(np.asarray(prompt, dtype=np.int32), device=self.device)
+        tok = self.step(toks, n, 0)
+        out = [tok.clone() if tok is not None else None]
+        self.decode_prepare(n)
+        for _ in range(1, n_gen):
+            tok = self.decode_step(tok if self.plan.is_first else None)
+            out.append(tok.clone() if tok is not None else None)
+        if self.plan.is_first:
+            return torch.cat(out).cpu().numpy()
+        return None

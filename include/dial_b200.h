@@ -270,6 +270,22 @@ int dial_b200_decode_loop_prepare(dial_b200_engine* eng, int64_t rows, const int
                                   char* err, size_t err_size);
 int dial_b200_decode_loop_run(dial_b200_engine* eng, int64_t rows, int64_t n_steps, char* err,
                               size_t err_size);
+/* Pipeline stage decode: one stage's share of a decode step with no host
+ * synchronisation, for stages chained by NCCL send/recv (the in-box
+ * replacement of the Master -> Worker hop, spm/client.rs:391-453 and
+ * spm/worker.rs:740-796).  dial_b200_stage_prepare sets the rows' sessions
+ * and positions on the device (synchronous, host arrays); every
+ * dial_b200_stage_step then runs
+ *   [has_embed: tokens_dev -> embedding ->] owned layers on hidden [rows, H]
+ *   [-> has_head: ln_f + lm_head + argmax -> tokens_out_dev]
+ * and advances the positions by one, as one CUDA graph (captured on first use
+ * per (rows, buffer addresses)) launched on `stream`. */
+int dial_b200_stage_prepare(dial_b200_engine* eng, int64_t rows, const int32_t* sids_host,
+                            const int32_t* positions_host, char* err, size_t err_size);
+int dial_b200_stage_step(dial_b200_engine* eng, int64_t rows, const int32_t* tokens_dev,
+                         void* hidden, int32_t* tokens_out_dev, void* stream, char* err,
+                         size_t err_size);
+
 /* Copy the loop's current tokens/positions back to host (synchronizes). */
 int dial_b200_decode_loop_state(dial_b200_engine* eng, int64_t rows, int32_t* tokens_host,
                                 int32_t* positions_host, char* err, size_t err_size);
