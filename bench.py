@@ -228,12 +228,10 @@ def run_single(args) -> dict:
     # ---- dominant kernel live: fused gate/up GEMV, same launch config, rotating
     # over the 36 layers' weights (3.6 GB) so every launch streams from HBM
     iters = 72
-    for layer in range(3):
-        eng.linear_replay(layer, 2, 1, 1)
+    eng.linear_replay(-1, 2, 1, 3)
     torch.cuda.synchronize()
     ev0.record(stream)
-    for i in range(iters):
-        eng.linear_replay(i % cfg.num_hidden_layers, 2, 1, 1)
+    eng.linear_replay(-1, 2, 1, iters)
     ev1.record(stream)
     ev1.synchronize()
     k_us = ev0.elapsed_time(ev1) * 1000.0 / iters
@@ -365,13 +363,11 @@ def run_pipeline(args) -> None:
 
             # ---- dominant kernel live on this rank: fused gate/up GEMV, rotating layers
             layers = list(range(plan.first_layer, plan.first_layer + plan.num_layers))
-            for l in layers[:2]:
-                eng.linear_replay(l, 2, 1, 1)
+            eng.linear_replay(-1, 2, 1, 2)
             torch.cuda.synchronize()
             iters = 8 * len(layers)
             ev0.record(eng.stream)
-            for i in range(iters):
-                eng.linear_replay(layers[i % len(layers)], 2, 1, 1)
+            eng.linear_replay(-1, 2, 1, iters)
             ev1.record(eng.stream)
             ev1.synchronize()
             k_us = ev0.elapsed_time(ev1) * 1000.0 / iters

@@ -1230,14 +1230,19 @@ int dial_b200_engine_linear_replay(dial_b200_engine* eng, int layer, int which, 
     const float eps = eng->cfg.rms_norm_eps;
     cudaStream_t s = eng->stream;
     const int M = static_cast<int>(rows);
+    // layer < 0: rotate over every owned layer so that no launch finds its
+    // weights in L2
     for (int64_t i = 0; i < iters; ++i) {
+      const int layer_i = layer >= 0 ? layer
+                                     : eng->cfg.first_layer +
+                                           static_cast<int>(i % eng->cfg.num_layers);
       if (which == 4) {
         DIAL_CHECK(eng->lm_head.ready(), "lm_head not loaded");
         run_linear(eng->lm_head, eng->hidden.p, eng->H, eng->final_norm.p, eps, eng->logits.p,
                    eng->V, M, kEpiStore, s, eng->status);
         continue;
       }
-      LayerW& L = eng->layer(layer);
+      LayerW& L = eng->layer(layer_i);
       switch (which) {
         case 0: run_linear(L.qkv, eng->hidden.p, eng->H, L.input_norm.p, eps, eng->qkv.p, eng->QKV,
                            M, kEpiStore, s, eng->status); break;

@@ -279,6 +279,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const GemvArgs a, con
   for (int t = t0; t < t1; ++t, ++tile_i) {
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
     float acc2[4] = {0.f, 0.f, 0.f, 0.f};
+    float pacc[4][4] = {};
     int rb_lo = 0, rb_hi = 0;
     if constexpr (FMT == kFmtFp8Block128) {
       if (a.w.swiglu) {
@@ -309,8 +310,21 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const GemvArgs a, con
           acc[3] = fmaf(tmp[3], shi, acc[3]);
         } else {
           const int ch0 = warp * 2, ch1 = warp * 2 + 1;
-          if (ch0 < nch) chunk_mma<FMT, XT>(st + ch0 * CB, s * kStageChunks + ch0, xrow, lane, acc);
-          if (ch1 < nch) chunk_mma<FMT, XT>(st + ch1 * CB, s * kStageChunks + ch1, xrow, lane, acc2);
+          if constexpr (FMT == kFmtW8A16Row || FMT == kFmtFp8Row) {
+            if (nch == kStageChunks) {
+              chunk_pair_mma<FMT, XT>(st + ch0 * CB, s * kStageChunks + ch0, xrow, lane, pacc);
+            } else {
+              if (ch0 < nch)
+                chunk_mma<FMT, XT>(st + ch0 * CB, s * kStageChunks + ch0, xrow, lane, acc);
+              if (ch1 < nch)
+                chunk_mma<FMT, XT>(st + ch1 * CB, s * kStageChunks + ch1, xrow, lane, acc2);
+            }
+          } else {
+            if (ch0 < nch)
+              chunk_mma<FMT, XT>(st + ch0 * CB, s * kStageChunks + ch0, xrow, lane, acc);
+            if (ch1 < nch)
+              chunk_mma<FMT, XT>(st + ch1 * CB, s * kStageChunks + ch1, xrow, lane, acc2);
+          }
         }
       }
       __syncwarp();
@@ -322,8 +336,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const GemvArgs a, con
     }
     // ---- cross-warp reduction (double-buffered by tile parity)
     float* rb = red + (tile_i & 1) * (kNW * 128);
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+      acc[q] += acc2[q] + ((pacc[0][q] + pacc[1][q]) + (pacc[2][q] + pacc[3][q]));
     *reinterpret_cast<float4*>(rb + (warp * 32 + lane) * 4) =
-        make_float4(acc[0] + acc2[0], acc[1] + acc2[1], acc[2] + acc2[2], acc[3] + acc2[3]);
+        make_float4(acc[0], acc[1], acc[2], acc[3]);
     named_bar_sync(1, kNW * 32);
     const int i = threadIdx.x;
     auto gather = [&](int rr, int tt) {
@@ -387,6 +404,10 @@ cudaError_t launch_one(const GemvArgs& a, int slots_req, int grid_req, cudaStrea
   auto kern = gemv_kernel<Act, FMT, EPI, NORM>;
   cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          kSmemBudget);
+  if (err != cudaSuccess) return err;
+  // Largest shared-memory carveout, so that two CTAs of consecutive launches
+  // can share an SM when their plans are small enough.
+  err = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
   if (err != cudaSuccess) return err;
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(grid);

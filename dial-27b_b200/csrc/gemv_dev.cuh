@@ -98,6 +98,49 @@ __device__ __forceinline__ void chunk_mma(const uint8_t* st, int kc, const XT* x
   }
 }
 
+// Two neighbouring int8 / e4m3 chunks of one stage with their MMAs
+// interleaved into four independent accumulator chains (chunk 0 -> acc[0..1],
+// chunk 1 -> acc[2..3], even/odd k16 steps alternating), so the tensor pipe's
+// dependent-issue latency is hidden within one warp.
+template <int FMT, typename XT>
+__device__ __forceinline__ void chunk_pair_mma(const uint8_t* st, int kc, const XT* xrow, int lane,
+                                               float (&acc)[4][4]) {
+  static_assert(FMT == kFmtW8A16Row || FMT == kFmtFp8Row || FMT == kFmtFp8Block128, "int8/e4m3");
+  const int c = lane & 3;
+  uint4 w[2][2];
+  uint32_t xw[2][8];
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    w[h][0] = *reinterpret_cast<const uint4*>(st + h * 1024 + lane * 16);
+    w[h][1] = *reinterpret_cast<const uint4*>(st + h * 1024 + 512 + lane * 16);
+    const XT* xp = xrow + (kc + h) * 64 + c * 16;
+    const uint4 xa = *reinterpret_cast<const uint4*>(xp);
+    const uint4 xb = *reinterpret_cast<const uint4*>(xp + 8);
+    xw[h][0] = xa.x; xw[h][1] = xa.y; xw[h][2] = xa.z; xw[h][3] = xa.w;
+    xw[h][4] = xb.x; xw[h][5] = xb.y; xw[h][6] = xb.z; xw[h][7] = xb.w;
+  }
+#pragma unroll
+  for (int s = 0; s < 4; ++s) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const uint32_t wa = (&w[h][0].x)[s], wb = (&w[h][1].x)[s];
+      uint32_t A[4];
+      if constexpr (FMT == kFmtW8A16Row) {
+        A[0] = i8_lo_pair(wa);
+        A[1] = i8_lo_pair(wb);
+        A[2] = i8_hi_pair(wa);
+        A[3] = i8_hi_pair(wb);
+      } else {
+        A[0] = e4m3x2_to_f16x2(static_cast<uint16_t>(wa & 0xffffu));
+        A[1] = e4m3x2_to_f16x2(static_cast<uint16_t>(wb & 0xffffu));
+        A[2] = e4m3x2_to_f16x2(static_cast<uint16_t>(wa >> 16));
+        A[3] = e4m3x2_to_f16x2(static_cast<uint16_t>(wb >> 16));
+      }
+      mma_f16(acc[2 * h + (s & 1)], A, xw[h][2 * s], xw[h][2 * s + 1]);
+    }
+  }
+}
+
 template <typename Act>
 __device__ __forceinline__ float silu_mul_ref(float g, float u) {
   using AT = ActTraits<Act>;

@@ -305,7 +305,9 @@ int64_t dial_b200_step_kernel_count(dial_b200_engine* eng, int64_t rows);
 
 /* Measurement hook: launch one owned layer's linear (`which` as in
  * set_linear, with the epilogue the decode step uses) `iters` times back to
- * back on the engine stream over the engine's work buffers.  Asynchronous. */
+ * back on the engine stream over the engine's work buffers; layer < 0
+ * rotates over every owned layer (no launch finds its weights in L2).
+ * Asynchronous. */
 int dial_b200_engine_linear_replay(dial_b200_engine* eng, int layer, int which, int64_t rows,
                                    int64_t iters, char* err, size_t err_size);
 
