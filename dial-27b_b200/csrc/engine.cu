@@ -310,9 +310,10 @@ struct dial_b200_engine {
   DevBuf embed, final_norm;
   Linear lm_head;
   DevBuf cos, sin, block_table;
-  DevBuf hidden, qkv, attn, inter, logits;
+  DevBuf hidden, qkv, attn, inter;
   DevBuf tok_in, sid, pos, tok_out, rows_scratch;
   DevBuf part_o, part_ml, counters;
+  DevBuf amax_key, amax_count;  // head argmax keys / arrival counters, zero between steps
   int32_t* h_in = nullptr;   // pinned: [3][max_rows] tokens, sids, positions
   int32_t* h_out = nullptr;  // pinned: [max_rows] tokens + status
   int* status = nullptr;
@@ -437,15 +438,17 @@ void engine_init(dial_b200_engine* e, const dial_b200_model_config& c, int devic
   e->qkv.alloc(T * e->QKV * es);
   e->attn.alloc(T * e->QH * e->D * es);
   e->inter.alloc(T * e->I * es);
-  if (c.has_head) {
-    const size_t lrows = std::max<size_t>(1, std::min<size_t>(T, 256));
-    e->logits.alloc(lrows * e->V * es);
-  }
   e->tok_in.alloc(T * 4);
   e->sid.alloc(T * 4);
   e->pos.alloc(T * 4);
   e->tok_out.alloc(T * 4);
   e->rows_scratch.alloc(2 * T * 4);
+  if (c.has_head) {
+    e->amax_key.alloc(static_cast<size_t>(T) * 8);
+    e->amax_count.alloc(static_cast<size_t>(T) * 4);
+    DIAL_CUDA(cudaMemset(e->amax_key.p, 0, e->amax_key.bytes));
+    DIAL_CUDA(cudaMemset(e->amax_count.p, 0, e->amax_count.bytes));
+  }
   // split-KV scratch: largest M * splits over decode batch sizes
   size_t max_rows_splits = 0;
   for (int M = 1; M <= e->max_rows_decode; ++M) {
@@ -633,12 +636,24 @@ void head_forward(dial_b200_engine* e, const void* hidden, int rows, void* logit
                   cudaStream_t s) {
   DIAL_CHECK(e->cfg.has_head, "this engine does not own the head");
   DIAL_CHECK(e->lm_head.ready(), "lm_head weights not loaded");
-  void* lg = logits ? logits : e->logits.p;
-  DIAL_CHECK(logits || static_cast<size_t>(rows) * e->V * 2 <= e->logits.bytes,
-             "too many head rows for the internal logits buffer");
-  run_linear(e->lm_head, hidden, e->H, e->final_norm.p, e->cfg.rms_norm_eps, lg, e->V, rows,
-             kEpiStore, s, e->status);
-  DIAL_CUDA(argmax_launch(lg, e->V, e->V, rows, e->cfg.act, toks, s, g_tuning().pdl));
+  DIAL_CHECK(rows <= e->max_rows_decode, "too many head rows (%d > %d)", rows,
+             e->max_rows_decode);
+  // ln_f + lm_head GEMV with the greedy argmax in its epilogue; the logits are
+  // written only when the caller asks for them.
+  GemvArgs a{};
+  a.w = e->lm_head.d;
+  a.x = hidden;
+  a.x_ld = e->H;
+  a.norm_w = e->final_norm.p;
+  a.eps = e->cfg.rms_norm_eps;
+  a.out = logits;
+  a.out_ld = e->V;
+  a.M = rows;
+  a.status = e->status;
+  a.amax_key = e->amax_key.as<unsigned long long>();
+  a.amax_count = e->amax_count.as<int>();
+  a.amax_tok = toks;
+  DIAL_CUDA(gemv_launch(a, e->lm_head.act, kEpiArgmax, true, s, g_tuning()));
 }
 
 // Whole decode step on device buffers (tok_in, sid, pos -> tok_out).

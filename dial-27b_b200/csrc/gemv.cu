@@ -262,6 +262,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const GemvArgs a, con
   }
 
   // -------------------------------------------------------------- consumers
+  int* sflag = reinterpret_cast<int*>(smem + p.misc_off + 128);
+  unsigned long long* skey = reinterpret_cast<unsigned long long*>(smem + p.misc_off + 192);
+  if constexpr (EPI == kEpiArgmax) {
+    if (threadIdx.x < kMaxM) skey[threadIdx.x] = 0ull;
+  }
   pdl_wait();
   stage_x<Act, XT, NORM, kScaleX>(a, xs, p.xs_stride, xexp, scratch);
   named_bar_sync(1, kNW * 32);
@@ -379,14 +384,40 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const GemvArgs a, con
           if constexpr (FMT == kFmtNvfp4G16) mul *= a.w.global_scale;
           if (a.w.row_scale) mul *= a.w.row_scale[t * 16 + rr];
           const float y = AT::round(v * mul);
-          Act* out = reinterpret_cast<Act*>(a.out) + static_cast<size_t>(tt) * a.out_ld + n;
-          if constexpr (EPI == kEpiResidual) {
-            *out = AT::from_f(y + AT::to_f(*out));
+          if constexpr (EPI == kEpiArgmax) {
+            if (a.out)
+              reinterpret_cast<Act*>(a.out)[static_cast<size_t>(tt) * a.out_ld + n] = AT::from_f(y);
+            atomicMax(&skey[tt], argmax_key(y, n));
           } else {
-            *out = AT::from_f(y);
+            Act* out = reinterpret_cast<Act*>(a.out) + static_cast<size_t>(tt) * a.out_ld + n;
+            if constexpr (EPI == kEpiResidual) {
+              *out = AT::from_f(y + AT::to_f(*out));
+            } else {
+              *out = AT::from_f(y);
+            }
           }
         }
       }
+    }
+  }
+  if constexpr (EPI == kEpiArgmax) {
+    // CTA best -> global keys; the last CTA to arrive decodes and resets them.
+    named_bar_sync(1, kNW * 32);
+    if (threadIdx.x < a.M) atomicMax(&a.amax_key[threadIdx.x], skey[threadIdx.x]);
+    __threadfence();
+    named_bar_sync(1, kNW * 32);
+    if (threadIdx.x == 0) {
+      const int prev = atomicAdd(a.amax_count, 1);
+      *sflag = prev == static_cast<int>(gridDim.x) - 1;
+    }
+    named_bar_sync(1, kNW * 32);
+    if (*sflag) {
+      __threadfence();
+      if (threadIdx.x < a.M) {
+        const unsigned long long k = atomicExch(&a.amax_key[threadIdx.x], 0ull);
+        a.amax_tok[threadIdx.x] = static_cast<int32_t>(0xFFFFFFFFu - static_cast<uint32_t>(k));
+      }
+      if (threadIdx.x == 0) atomicExch(a.amax_count, 0);
     }
   }
 }
@@ -425,6 +456,12 @@ cudaError_t launch_one(const GemvArgs& a, int slots_req, int grid_req, cudaStrea
 template <typename Act, int FMT>
 cudaError_t dispatch_epi(const GemvArgs& a, int epi, bool norm, int slots, int grid,
                          cudaStream_t s, bool pdl) {
+  if (epi == kEpiArgmax) {
+    if constexpr (FMT == kFmtDense || FMT == kFmtW8A16Row)
+      return norm ? launch_one<Act, FMT, kEpiArgmax, true>(a, slots, grid, s, pdl)
+                  : launch_one<Act, FMT, kEpiArgmax, false>(a, slots, grid, s, pdl);
+    return cudaErrorInvalidValue;
+  }
   if (epi == kEpiStore)
     return norm ? launch_one<Act, FMT, kEpiStore, true>(a, slots, grid, s, pdl)
                 : launch_one<Act, FMT, kEpiStore, false>(a, slots, grid, s, pdl);
@@ -468,7 +505,14 @@ cudaError_t gemv_launch(const GemvArgs& args, int act, int epi, bool norm, cudaS
   for (int r0 = 0; r0 < args.M; r0 += group) {
     a.M = std::min(group, args.M - r0);
     a.x = static_cast<const char*>(args.x) + static_cast<size_t>(r0) * args.x_ld * esz;
-    a.out = static_cast<char*>(args.out) + static_cast<size_t>(r0) * args.out_ld * esz;
+    a.out = args.out ? static_cast<char*>(args.out) + static_cast<size_t>(r0) * args.out_ld * esz
+                     : nullptr;
+    if (epi == kEpiArgmax) {
+      if (!args.amax_key || !args.amax_count || !args.amax_tok) return cudaErrorInvalidValue;
+      a.amax_key = args.amax_key + r0;
+      a.amax_count = args.amax_count + r0;
+      a.amax_tok = args.amax_tok + r0;
+    }
     cudaError_t e = act == 0 ? dispatch_fmt<__nv_bfloat16>(a, epi, norm, tune.slots, tune.grid,
                                                            stream, tune.pdl)
                              : dispatch_fmt<__half>(a, epi, norm, tune.slots, tune.grid, stream,

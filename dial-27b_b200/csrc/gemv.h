@@ -13,6 +13,7 @@ enum GemvEpilogue : int {
   kEpiStore = 0,     // out = act(acc * scale)
   kEpiResidual = 1,  // out = act(out + act(acc * scale))      (in-place residual)
   kEpiSwiglu = 2,    // out[:, j] = act(silu(gate_j) * up_j)   (fused gate/up rows)
+  kEpiArgmax = 3,    // store (when out != null) + greedy argmax per row -> amax_tok
 };
 
 struct GemvArgs {
@@ -25,6 +26,11 @@ struct GemvArgs {
   int out_ld;
   int M;
   int* status;         // device status word (first error code wins)
+  // kEpiArgmax: per-row packed (value, index) keys and a CTA arrival counter,
+  // both zero on entry and left zero on exit; amax_tok [M] receives the ids.
+  unsigned long long* amax_key;
+  int* amax_count;
+  int32_t* amax_tok;
 };
 
 struct GemvTuning {

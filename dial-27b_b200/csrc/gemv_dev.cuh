@@ -141,6 +141,15 @@ __device__ __forceinline__ void chunk_pair_mma(const uint8_t* st, int kc, const 
   }
 }
 
+// Greedy-argmax key: larger value wins, then the lower index (the first of
+// equal maxima, as candle's argmax over the logits, qwen3_vl.rs:138-143).
+// -0 counts as +0.
+__device__ __forceinline__ unsigned long long argmax_key(float y, int n) {
+  uint32_t b = __float_as_uint(y == 0.f ? 0.f : y);
+  b = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+  return (static_cast<unsigned long long>(b) << 32) | (0xFFFFFFFFu - static_cast<uint32_t>(n));
+}
+
 template <typename Act>
 __device__ __forceinline__ float silu_mul_ref(float g, float u) {
   using AT = ActTraits<Act>;

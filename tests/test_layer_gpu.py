@@ -206,3 +206,36 @@ def test_layer_forward_rejects_bad_requests(cuda):
         eng.forward(torch.zeros(40, cfg.hidden, dtype=torch.bfloat16, device=cuda), 0, 0)
     with pytest.raises(dial_b200.DialError, match="contiguous layer range"):
         eng.forward_local_batch(x, [("a", 0, 0), ("b", 0, 2)])
+
+
+@pytest.mark.parametrize("rows", [1, 3, 11])
+def test_head_argmax_first_of_ties_and_logits(cuda, rows):
+    """ln_f + lm_head + greedy argmax (qwen3_vl.rs:138-143, 2462-2487): the
+    fused argmax returns the lowest index among equal maxima, and the
+    optional logits match the oracle's dense lm_head."""
+    import dial_b200
+
+    cfg = small_cfg(vocab=3000, layers=1)
+    eng = engine_for(cfg, dial_b200, max_tokens=16)
+    rng = np.random.default_rng(9)
+    lm = O.bf16_round(rng.standard_normal((cfg.vocab, cfg.hidden)).astype(np.float32) * 0.02)
+    x = O.bf16_round(rng.standard_normal((rows, cfg.hidden)).astype(np.float32))
+    h = O.rms_norm(x, np.ones(cfg.hidden, np.float32), cfg.eps)
+    # plant a tie at the top for every row: indices 2900 and 77 share the row
+    # aligned with row 0's normalised input, scaled up so it wins
+    best = O.bf16_round(h[0] / np.linalg.norm(h[0]) * 0.5)
+    lm[77] = best
+    lm[2900] = best
+    eng.set_linear(0, eng.LINEAR_LM_HEAD, dial_b200.FMT_DENSE, O.bf16_bits(lm).view(np.uint16))
+    eng.set_tensor(0, eng.T_FINAL_NORM, np.ones(cfg.hidden, np.float32))
+    xt = torch.from_numpy(x).to(cuda).to(torch.bfloat16)
+    toks, logits = eng.head(xt, return_logits=True)
+    toks2 = eng.head(xt)
+    torch.cuda.synchronize()
+    ref = O.dense_linear(h, lm)
+    want = np.array([O.argmax_first(r) for r in ref], np.int32)
+    got = logits.float().cpu().numpy()
+    assert np.max(np.abs(got - ref)) <= 2 ** -7 * np.max(np.abs(ref)) + 1e-3
+    np.testing.assert_array_equal(toks.cpu().numpy(), want)
+    np.testing.assert_array_equal(toks2.cpu().numpy(), want)
+    assert want[0] == 77
