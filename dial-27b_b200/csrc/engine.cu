@@ -1253,8 +1253,7 @@ int dial_b200_engine_linear_replay(dial_b200_engine* eng, int layer, int which, 
                                            static_cast<int>(i % eng->cfg.num_layers);
       if (which == 4) {
         DIAL_CHECK(eng->lm_head.ready(), "lm_head not loaded");
-        run_linear(eng->lm_head, eng->hidden.p, eng->H, eng->final_norm.p, eps, eng->logits.p,
-                   eng->V, M, kEpiStore, s, eng->status);
+        head_forward(eng, eng->hidden.p, M, nullptr, eng->tok_out.as<int32_t>(), s);
         continue;
       }
       LayerW& L = eng->layer(layer_i);

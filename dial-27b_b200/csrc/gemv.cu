@@ -97,80 +97,6 @@ __host__ inline SmemPlan make_plan(const DevQLinear& w, int M, int grid, int slo
 template <int FMT>
 struct XType { using T = __half; };
 
-// --------------------------------------------------------------- x staging
-template <typename Act, typename XT, bool NORM, bool SCALE>
-__device__ void stage_x(const GemvArgs& a, XT* xs, int xs_stride, int* xexp, float* scratch) {
-  using AT = ActTraits<Act>;
-  const int tid = threadIdx.x;
-  constexpr int NT = kNW * 32;
-  const int K = a.w.K, Kp = a.w.K_pad;
-  const Act* nw = reinterpret_cast<const Act*>(a.norm_w);
-  const int warp = tid >> 5, lane = tid & 31;
-
-  float wmax = 1.f;
-  if (NORM && SCALE) {
-    float m = 0.f;
-    for (int k = tid; k < K; k += NT) m = fmaxf(m, fabsf(AT::to_f(nw[k])));
-    m = warp_max(m);
-    if (lane == 0) scratch[warp] = m;
-    named_bar_sync(1, NT);
-    m = 0.f;
-#pragma unroll
-    for (int i = 0; i < kNW; ++i) m = fmaxf(m, scratch[i]);
-    wmax = m;
-    named_bar_sync(1, NT);
-  }
-  for (int r = 0; r < a.M; ++r) {
-    const Act* xr = reinterpret_cast<const Act*>(a.x) + static_cast<size_t>(r) * a.x_ld;
-    float ss = 0.f, am = 0.f;
-    for (int k = tid; k < K; k += NT) {
-      const float v = AT::to_f(xr[k]);
-      ss = fmaf(v, v, ss);
-      am = fmaxf(am, fabsf(v));
-    }
-    ss = warp_sum(ss);
-    am = warp_max(am);
-    if (lane == 0) {
-      scratch[warp] = ss;
-      scratch[kNW + warp] = am;
-    }
-    named_bar_sync(1, NT);
-    ss = 0.f;
-    am = 0.f;
-#pragma unroll
-    for (int i = 0; i < kNW; ++i) {
-      ss += scratch[i];
-      am = fmaxf(am, scratch[kNW + i]);
-    }
-    named_bar_sync(1, NT);
-    float rms = 1.f;
-    if (NORM) rms = AT::round(__fsqrt_rn(__fdiv_rn(ss, static_cast<float>(K)) + a.eps));
-    int e = 0;
-    if (SCALE) {
-      const float bound = NORM ? __fdiv_rn(am, rms) * wmax * 1.02f : am;
-      if (bound >= 16384.f) e = ilogbf(bound) - 13;
-    }
-    const float sc = exp2i(-e);
-    XT* xrow = xs + static_cast<size_t>(r) * xs_stride;
-    for (int k = tid; k < Kp; k += NT) {
-      float v = 0.f;
-      if (k < K) {
-        v = AT::to_f(xr[k]);
-        if (NORM) {
-          v = AT::round(__fdiv_rn(v, rms));
-          v = AT::round(v * AT::to_f(nw[k]));
-        }
-      }
-      if constexpr (sizeof(XT) == 2 && std::is_same<XT, __half>::value) {
-        xrow[k] = __float2half_rn(v * sc);
-      } else {
-        xrow[k] = ActTraits<XT>::from_f(v);
-      }
-    }
-    if (tid == 0) xexp[r] = e;
-  }
-}
-
 // ------------------------------------------------------------------ kernel
 template <typename Act, int FMT, int EPI, bool NORM>
 __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const GemvArgs a, const SmemPlan p) {
@@ -268,7 +194,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const GemvArgs a, con
     if (threadIdx.x < kMaxM) skey[threadIdx.x] = 0ull;
   }
   pdl_wait();
-  stage_x<Act, XT, NORM, kScaleX>(a, xs, p.xs_stride, xexp, scratch);
+  stage_x<Act, XT, NORM, kScaleX, kNW>(a, xs, p.xs_stride, xexp, scratch);
   named_bar_sync(1, kNW * 32);
   if constexpr (FMT == kFmtFp8Block128) mbar_wait(sbar, 0, a.status, kStatusFullWaitTimeout);
 

@@ -10,6 +10,7 @@
 #include <type_traits>
 
 #include "common.cuh"
+#include "gemv.h"
 #include "qlinear.h"
 
 namespace dialb200 {
@@ -138,6 +139,84 @@ __device__ __forceinline__ void chunk_pair_mma(const uint8_t* st, int kc, const 
       }
       mma_f16(acc[2 * h + (s & 1)], A, xw[h][2 * s], xw[h][2 * s + 1]);
     }
+  }
+}
+
+// ------------------------------------------------------------ x staging
+// Stage the M activation rows of a GEMV in shared memory (NW consumer warps,
+// named barrier 1): optional RMSNorm (text.rs:1620-1626 rounding), then f16
+// with a power-of-two pre-scale xexp[r] when the values would overflow f16
+// (bf16 inputs), or the activation dtype itself for dense weights.
+template <typename Act, typename XT, bool NORM, bool SCALE, int NW>
+__device__ void stage_x(const GemvArgs& a, XT* xs, int xs_stride, int* xexp, float* scratch) {
+  using AT = ActTraits<Act>;
+  const int tid = threadIdx.x;
+  constexpr int NT = NW * 32;
+  const int K = a.w.K, Kp = a.w.K_pad;
+  const Act* nw = reinterpret_cast<const Act*>(a.norm_w);
+  const int warp = tid >> 5, lane = tid & 31;
+
+  float wmax = 1.f;
+  if (NORM && SCALE) {
+    float m = 0.f;
+    for (int k = tid; k < K; k += NT) m = fmaxf(m, fabsf(AT::to_f(nw[k])));
+    m = warp_max(m);
+    if (lane == 0) scratch[warp] = m;
+    named_bar_sync(1, NT);
+    m = 0.f;
+#pragma unroll
+    for (int i = 0; i < NW; ++i) m = fmaxf(m, scratch[i]);
+    wmax = m;
+    named_bar_sync(1, NT);
+  }
+  for (int r = 0; r < a.M; ++r) {
+    const Act* xr = reinterpret_cast<const Act*>(a.x) + static_cast<size_t>(r) * a.x_ld;
+    float ss = 0.f, am = 0.f;
+    for (int k = tid; k < K; k += NT) {
+      const float v = AT::to_f(xr[k]);
+      ss = fmaf(v, v, ss);
+      am = fmaxf(am, fabsf(v));
+    }
+    ss = warp_sum(ss);
+    am = warp_max(am);
+    if (lane == 0) {
+      scratch[warp] = ss;
+      scratch[NW + warp] = am;
+    }
+    named_bar_sync(1, NT);
+    ss = 0.f;
+    am = 0.f;
+#pragma unroll
+    for (int i = 0; i < NW; ++i) {
+      ss += scratch[i];
+      am = fmaxf(am, scratch[NW + i]);
+    }
+    named_bar_sync(1, NT);
+    float rms = 1.f;
+    if (NORM) rms = AT::round(__fsqrt_rn(__fdiv_rn(ss, static_cast<float>(K)) + a.eps));
+    int e = 0;
+    if (SCALE) {
+      const float bound = NORM ? __fdiv_rn(am, rms) * wmax * 1.02f : am;
+      if (bound >= 16384.f) e = ilogbf(bound) - 13;
+    }
+    const float sc = exp2i(-e);
+    XT* xrow = xs + static_cast<size_t>(r) * xs_stride;
+    for (int k = tid; k < Kp; k += NT) {
+      float v = 0.f;
+      if (k < K) {
+        v = AT::to_f(xr[k]);
+        if (NORM) {
+          v = AT::round(__fdiv_rn(v, rms));
+          v = AT::round(v * AT::to_f(nw[k]));
+        }
+      }
+      if constexpr (sizeof(XT) == 2 && std::is_same<XT, __half>::value) {
+        xrow[k] = __float2half_rn(v * sc);
+      } else {
+        xrow[k] = ActTraits<XT>::from_f(v);
+      }
+    }
+    if (tid == 0) xexp[r] = e;
   }
 }
 
