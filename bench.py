@@ -250,7 +250,7 @@ def run_single(args) -> dict:
                      "launch_us": k_us, "bytes_per_launch": k_bytes, "peak_source": peaks["source"],
                      "step_bytes": step_bytes,
                      "step_frac": step_bytes / (step_ms * 1e-3) / 1e9 / peaks["hbm_gbs"]},
-        "gpu_launches": (eng.step_kernel_count(1) + 1) * args.steps,
+        "gpu_launches": eng.step_kernel_count(1) * args.steps,
         "final_token": int(toks[0]), "final_pos": int(positions[0]),
     }
 

@@ -37,6 +37,7 @@ struct GemvTuning {
   int slots = 0;   // ring stages (0 = as many as fit)
   int grid = 0;    // CTAs (0 = one per SM)
   bool pdl = true; // programmatic dependent launch
+  bool step_kernel = false;  // whole decode step as one persistent kernel when supported
 };
 
 // act: 0 = bf16, 1 = f16.  Launches ceil(M/8) kernels on `stream`.

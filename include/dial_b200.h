@@ -300,7 +300,8 @@ int dial_b200_session_fill_random(dial_b200_engine* eng, int32_t session, int64_
                                   uint64_t seed, const uint16_t* normal_table_bits, char* err,
                                   size_t err_size);
 
-/* Number of kernels one decode step launches for `rows` rows. */
+/* Number of kernels one device-loop decode step launches for `rows` rows
+ * (1 when the persistent step kernel runs the step). */
 int64_t dial_b200_step_kernel_count(dial_b200_engine* eng, int64_t rows);
 
 /* Measurement hook: launch one owned layer's linear (`which` as in
