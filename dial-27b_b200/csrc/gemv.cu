@@ -208,6 +208,25 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const GemvArgs a, con
   bool ok = true;
   int tile_i = 0;
   for (int t = t0; t < t1; ++t, ++tile_i) {
+    // Epilogue operands of this tile (row scales, residual inputs) are loaded
+    // now, so their latency hides behind the tile's stages.
+    float pre_a = 1.f, pre_b = 1.f, pre_o = 0.f;
+    if (threadIdx.x < 128) {
+      const int rr = threadIdx.x >> 3, tt = threadIdx.x & 7;
+      if constexpr (EPI == kEpiSwiglu) {
+        if (threadIdx.x < 64 && a.w.row_scale) {
+          pre_a = a.w.row_scale[t * 16 + rr];
+          pre_b = a.w.row_scale[t * 16 + 8 + rr];
+        }
+      } else {
+        const int n = t * 16 + rr;
+        if (a.w.row_scale) pre_a = a.w.row_scale[t * 16 + rr];
+        if constexpr (EPI == kEpiResidual) {
+          if (tt < a.M && n < a.w.N)
+            pre_o = AT::to_f(reinterpret_cast<const Act*>(a.out)[static_cast<size_t>(tt) * a.out_ld + n]);
+        }
+      }
+    }
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
     float acc2[4] = {0.f, 0.f, 0.f, 0.f};
     float pacc[4][4] = {};
@@ -290,11 +309,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const GemvArgs a, con
           float vg = gather(rr, tt), vu = gather(rr + 8, tt);
           float mul = exp2i(xexp[tt]);
           if constexpr (FMT == kFmtNvfp4G16) mul *= a.w.global_scale;
-          float sg = mul, su = mul;
-          if (a.w.row_scale) {
-            sg *= a.w.row_scale[t * 16 + rr];
-            su *= a.w.row_scale[t * 16 + 8 + rr];
-          }
+          const float sg = mul * pre_a, su = mul * pre_b;
           const float gq = AT::round(vg * sg), uq = AT::round(vu * su);
           Act* out = reinterpret_cast<Act*>(a.out) + static_cast<size_t>(tt) * a.out_ld + j;
           *out = AT::from_f(silu_mul_ref<Act>(gq, uq));
@@ -308,7 +323,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const GemvArgs a, con
           float v = gather(rr, tt);
           float mul = exp2i(xexp[tt]);
           if constexpr (FMT == kFmtNvfp4G16) mul *= a.w.global_scale;
-          if (a.w.row_scale) mul *= a.w.row_scale[t * 16 + rr];
+          mul *= pre_a;
           const float y = AT::round(v * mul);
           if constexpr (EPI == kEpiArgmax) {
             if (a.out)
@@ -317,7 +332,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const GemvArgs a, con
           } else {
             Act* out = reinterpret_cast<Act*>(a.out) + static_cast<size_t>(tt) * a.out_ld + n;
             if constexpr (EPI == kEpiResidual) {
-              *out = AT::from_f(y + AT::to_f(*out));
+              *out = AT::from_f(y + pre_o);
             } else {
               *out = AT::from_f(y);
             }

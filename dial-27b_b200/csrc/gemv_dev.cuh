@@ -148,7 +148,8 @@ __device__ __forceinline__ void chunk_pair_mma(const uint8_t* st, int kc, const 
 // with a power-of-two pre-scale xexp[r] when the values would overflow f16
 // (bf16 inputs), or the activation dtype itself for dense weights.
 template <typename Act, typename XT, bool NORM, bool SCALE, int NW>
-__device__ void stage_x(const GemvArgs& a, XT* xs, int xs_stride, int* xexp, float* scratch) {
+__device__ void stage_x_scalar(const GemvArgs& a, XT* xs, int xs_stride, int* xexp,
+                               float* scratch) {
   using AT = ActTraits<Act>;
   const int tid = threadIdx.x;
   constexpr int NT = NW * 32;
@@ -216,6 +217,117 @@ __device__ void stage_x(const GemvArgs& a, XT* xs, int xs_stride, int* xexp, flo
         xrow[k] = ActTraits<XT>::from_f(v);
       }
     }
+    if (tid == 0) xexp[r] = e;
+  }
+}
+
+// 16-byte vector form of stage_x: every load of a row is issued at once
+// (one L2 round trip), the sum of squares and the pre-scale bound come from
+// one block reduction, and the converted row is written with 16-byte stores.
+// Rows whose length, stride or address do not allow 16-byte access, or that
+// exceed kStageVec vectors per thread, take stage_x_scalar.
+constexpr int kStageVec = 6;
+
+template <typename Act>
+__device__ __forceinline__ void unpack8(const uint4& v, float (&f)[8]) {
+  const Act* p = reinterpret_cast<const Act*>(&v);
+#pragma unroll
+  for (int e = 0; e < 8; ++e) f[e] = ActTraits<Act>::to_f(p[e]);
+}
+
+template <typename Act, typename XT, bool NORM, bool SCALE, int NW>
+__device__ void stage_x(const GemvArgs& a, XT* xs, int xs_stride, int* xexp, float* scratch) {
+  using AT = ActTraits<Act>;
+  constexpr int NT = NW * 32;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int K = a.w.K, Kp = a.w.K_pad;
+  const bool vec = (K % 8) == 0 && (a.x_ld % 8) == 0 &&
+                   (reinterpret_cast<uintptr_t>(a.x) & 15) == 0 &&
+                   (!NORM || (reinterpret_cast<uintptr_t>(a.norm_w) & 15) == 0) &&
+                   K <= kStageVec * 8 * NT && (xs_stride % 8) == 0;
+  if (!vec) {
+    stage_x_scalar<Act, XT, NORM, SCALE, NW>(a, xs, xs_stride, xexp, scratch);
+    return;
+  }
+  const int nv = K / 8;
+  const uint4* wr = reinterpret_cast<const uint4*>(a.norm_w);
+  for (int r = 0; r < a.M; ++r) {
+    const uint4* xr =
+        reinterpret_cast<const uint4*>(reinterpret_cast<const Act*>(a.x) + static_cast<size_t>(r) * a.x_ld);
+    uint4 xv[kStageVec], wv[kStageVec];
+#pragma unroll
+    for (int j = 0; j < kStageVec; ++j) {
+      const int i = tid + j * NT;
+      if (i < nv) {
+        xv[j] = __ldcg(xr + i);  // produced by other SMs: read through L2
+        if (NORM) wv[j] = __ldg(wr + i);
+      }
+    }
+    float ss = 0.f, am = 0.f;
+#pragma unroll
+    for (int j = 0; j < kStageVec; ++j) {
+      if (tid + j * NT < nv) {
+        float xf[8], wf[8];
+        unpack8<Act>(xv[j], xf);
+        if (NORM) unpack8<Act>(wv[j], wf);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          ss = fmaf(xf[e], xf[e], ss);
+          am = fmaxf(am, fabsf(NORM ? xf[e] * wf[e] : xf[e]));
+        }
+      }
+    }
+    ss = warp_sum(ss);
+    am = warp_max(am);
+    if (lane == 0) {
+      scratch[warp] = ss;
+      scratch[NW + warp] = am;
+    }
+    named_bar_sync(1, NT);
+    ss = 0.f;
+    am = 0.f;
+#pragma unroll
+    for (int i = 0; i < NW; ++i) {
+      ss += scratch[i];
+      am = fmaxf(am, scratch[NW + i]);
+    }
+    named_bar_sync(1, NT);
+    float rms = 1.f;
+    if (NORM) rms = AT::round(__fsqrt_rn(__fdiv_rn(ss, static_cast<float>(K)) + a.eps));
+    int e = 0;
+    if (SCALE) {
+      // NORM: staged values are act(act(x/rms)*w) <= |x*w|/rms * (1 + 2^-7)
+      const float bound = NORM ? __fdiv_rn(am, rms) * 1.02f : am;
+      if (bound >= 16384.f) e = ilogbf(bound) - 13;
+    }
+    const float sc = exp2i(-e);
+    XT* xrow = xs + static_cast<size_t>(r) * xs_stride;
+#pragma unroll
+    for (int j = 0; j < kStageVec; ++j) {
+      const int i = tid + j * NT;
+      if (i < nv) {
+        float xf[8], wf[8];
+        unpack8<Act>(xv[j], xf);
+        if (NORM) unpack8<Act>(wv[j], wf);
+        uint4 o;
+        XT* op = reinterpret_cast<XT*>(&o);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          float v = xf[q];
+          if (NORM) {
+            v = AT::round(__fdiv_rn(v, rms));
+            v = AT::round(v * wf[q]);
+          }
+          if constexpr (std::is_same<XT, __half>::value) {
+            op[q] = __float2half_rn(v * sc);
+          } else {
+            op[q] = ActTraits<XT>::from_f(v);
+          }
+        }
+        *reinterpret_cast<uint4*>(xrow + static_cast<size_t>(i) * 8) = o;
+      }
+    }
+    for (int k = K + tid; k < Kp; k += NT) xrow[k] = ActTraits<XT>::from_f(0.f);
     if (tid == 0) xexp[r] = e;
   }
 }

@@ -66,6 +66,7 @@ struct Smem {
   AttnItemSmem* attn;
   uint64_t* full;
   uint64_t* empty;
+  uint64_t* xbar;    // activation-row bulk copy
 };
 
 // --------------------------------------------------------------- producer
@@ -177,8 +178,36 @@ __device__ void attn_op(const StepOp& op, int M, const Smem& sm) {
 
 // ------------------------------------------------------------------ GEMV
 // Epilogue of one finished 16-row tile from the tile sums tv[(row << 3) | tok].
+// Row scales and residual inputs of tile t for thread i < 128, loaded when
+// the tile starts so that their latency hides behind the tile's stages.
 template <typename Act>
-__device__ void tile_epilogue(const StepOp& op, int M, int t, const Smem& sm) {
+__device__ __forceinline__ void tile_prefetch(const StepOp& op, int M, int t, float& pre_a,
+                                              float& pre_b, float& pre_o) {
+  const int i = threadIdx.x;
+  pre_a = pre_b = 1.f;
+  pre_o = 0.f;
+  if (i >= 128) return;
+  const DevQLinear& w = op.w;
+  const int rr = i >> 3, tt = i & 7;
+  if (op.epi == kEpiSwiglu) {
+    if (i < 64 && w.row_scale) {
+      pre_a = __ldg(w.row_scale + t * 16 + rr);
+      pre_b = __ldg(w.row_scale + t * 16 + 8 + rr);
+    }
+    return;
+  }
+  if (w.row_scale) pre_a = __ldg(w.row_scale + t * 16 + rr);
+  const int n = t * 16 + rr;
+  if (op.epi == kEpiResidual && tt < M && n < w.N) {
+    const unsigned short bits = __ldcg(reinterpret_cast<const unsigned short*>(op.out) +
+                                       static_cast<size_t>(tt) * op.out_ld + n);
+    pre_o = ActTraits<Act>::to_f(*reinterpret_cast<const Act*>(&bits));
+  }
+}
+
+template <typename Act>
+__device__ void tile_epilogue(const StepOp& op, int M, int t, const Smem& sm, float pre_a,
+                              float pre_b, float pre_o) {
   using AT = ActTraits<Act>;
   const int i = threadIdx.x;
   const DevQLinear& w = op.w;
@@ -189,11 +218,7 @@ __device__ void tile_epilogue(const StepOp& op, int M, int t, const Smem& sm) {
       const int j = t * 8 + rr;
       if (tt < M && j < I) {
         const float mul = exp2i(sm.xexp[tt]);
-        float sg = mul, su = mul;
-        if (w.row_scale) {
-          sg *= w.row_scale[t * 16 + rr];
-          su *= w.row_scale[t * 16 + 8 + rr];
-        }
+        const float sg = mul * pre_a, su = mul * pre_b;
         const float gq = AT::round(sm.tv[(rr << 3) | tt] * sg);
         const float uq = AT::round(sm.tv[((rr + 8) << 3) | tt] * su);
         reinterpret_cast<Act*>(op.out)[static_cast<size_t>(tt) * op.out_ld + j] =
@@ -206,8 +231,7 @@ __device__ void tile_epilogue(const StepOp& op, int M, int t, const Smem& sm) {
     const int rr = i >> 3, tt = i & 7;
     const int n = t * 16 + rr;
     if (tt < M && n < w.N) {
-      float mul = exp2i(sm.xexp[tt]);
-      if (w.row_scale) mul *= w.row_scale[t * 16 + rr];
+      const float mul = exp2i(sm.xexp[tt]) * pre_a;
       const float y = AT::round(sm.tv[i] * mul);
       if (op.epi == kEpiArgmax) {
         if (op.out)
@@ -215,15 +239,122 @@ __device__ void tile_epilogue(const StepOp& op, int M, int t, const Smem& sm) {
         atomicMax(&sm.skey[tt], argmax_key(y, n));
       } else {
         Act* o = reinterpret_cast<Act*>(op.out) + static_cast<size_t>(tt) * op.out_ld + n;
-        *o = op.epi == kEpiResidual ? AT::from_f(y + AT::to_f(*o)) : AT::from_f(y);
+        *o = op.epi == kEpiResidual ? AT::from_f(y + pre_o) : AT::from_f(y);
       }
     }
   }
 }
 
+// Stage the op's activation rows: one 1-D bulk copy per row into shared
+// memory (no registers held), then RMSNorm / pre-scale / conversion in place
+// with the same rounding as stage_x in gemv_dev.cuh.  The RMSNorm weights
+// (K <= kStepNormVec * 8 * 256) are loaded into registers while the copy
+// is in flight.
+constexpr int kStepNormVec = 4;
+
+template <typename Act, typename XT, bool NORM, bool SCALE>
+__device__ void stage_op_x(const StepArgs& a, const StepOp& op, const Smem& sm, int xs_stride,
+                           uint32_t& xphase) {
+  using AT = ActTraits<Act>;
+  constexpr int NT = kNC * 32;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int K = op.w.K, Kp = op.w.K_pad, nv = K / 8;
+  uint4 wv[kStepNormVec];
+  if (NORM) {
+    const uint4* wr = reinterpret_cast<const uint4*>(op.norm_w);
+#pragma unroll
+    for (int j = 0; j < kStepNormVec; ++j)
+      if (tid + j * NT < nv) wv[j] = __ldg(wr + tid + j * NT);
+  }
+  Act* raw = reinterpret_cast<Act*>(sm.xs);
+  if (tid == 0) {
+    asm volatile("fence.proxy.async;" ::: "memory");
+    mbar_arrive_expect_tx(sm.xbar, static_cast<uint32_t>(a.M * K * 2));
+    for (int r = 0; r < a.M; ++r)
+      bulk_g2s(raw + static_cast<size_t>(r) * xs_stride,
+               reinterpret_cast<const Act*>(op.x) + static_cast<size_t>(r) * op.x_ld,
+               static_cast<uint32_t>(K * 2), sm.xbar);
+  }
+  mbar_wait(sm.xbar, xphase, a.status, kStatusFullWaitTimeout);
+  xphase ^= 1u;
+  // NORM: thread tid owns vectors tid + j*NT (weights held in wv[j]);
+  // otherwise any number of vectors per thread.
+  auto for_each_vec = [&](auto&& f) {
+    if (NORM) {
+#pragma unroll
+      for (int j = 0; j < kStepNormVec; ++j)
+        if (tid + j * NT < nv) f(tid + j * NT, wv[j]);
+    } else {
+      for (int i = tid; i < nv; i += NT) f(i, wv[0]);
+    }
+  };
+  for (int r = 0; r < a.M; ++r) {
+    uint4* row = reinterpret_cast<uint4*>(raw + static_cast<size_t>(r) * xs_stride);
+    float ss = 0.f, am = 0.f;
+    for_each_vec([&](int i, const uint4& w) {
+      float xf[8], wf[8];
+      unpack8<Act>(row[i], xf);
+      if (NORM) unpack8<Act>(w, wf);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        ss = fmaf(xf[e], xf[e], ss);
+        am = fmaxf(am, fabsf(NORM ? xf[e] * wf[e] : xf[e]));
+      }
+    });
+    ss = warp_sum(ss);
+    am = warp_max(am);
+    if (lane == 0) {
+      sm.scratch[warp] = ss;
+      sm.scratch[kNC + warp] = am;
+    }
+    named_bar_sync(1, NT);
+    ss = 0.f;
+    am = 0.f;
+#pragma unroll
+    for (int i = 0; i < kNC; ++i) {
+      ss += sm.scratch[i];
+      am = fmaxf(am, sm.scratch[kNC + i]);
+    }
+    named_bar_sync(1, NT);
+    float rms = 1.f;
+    if (NORM) rms = AT::round(__fsqrt_rn(__fdiv_rn(ss, static_cast<float>(K)) + a.eps));
+    int e = 0;
+    if (SCALE) {
+      const float bound = NORM ? __fdiv_rn(am, rms) * 1.02f : am;
+      if (bound >= 16384.f) e = ilogbf(bound) - 13;
+    }
+    const float sc = exp2i(-e);
+    for_each_vec([&](int i, const uint4& w) {
+      float xf[8], wf[8];
+      unpack8<Act>(row[i], xf);
+      if (NORM) unpack8<Act>(w, wf);
+      uint4 o;
+      XT* op8 = reinterpret_cast<XT*>(&o);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        float v = xf[q];
+        if (NORM) {
+          v = AT::round(__fdiv_rn(v, rms));
+          v = AT::round(v * wf[q]);
+        }
+        if constexpr (std::is_same<XT, __half>::value) {
+          op8[q] = __float2half_rn(v * sc);
+        } else {
+          op8[q] = ActTraits<XT>::from_f(v);
+        }
+      }
+      row[i] = o;
+    });
+    XT* xrow = reinterpret_cast<XT*>(row);
+    for (int k = K + tid; k < Kp; k += NT) xrow[k] = ActTraits<XT>::from_f(0.f);
+    if (tid == 0) sm.xexp[r] = e;
+  }
+}
+
 template <typename Act>
 __device__ void gemv_op(const StepArgs& a, const StepOp& op, int op_index, const Smem& sm,
-                        const StepPlan& p, int& slot, uint32_t& round, int& parity, bool& ok) {
+                        const StepPlan& p, int& slot, uint32_t& round, int& parity, bool& ok,
+                        uint32_t& xphase) {
   const int G = gridDim.x, b = blockIdx.x;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int fmt = op.w.fmt;
@@ -233,27 +364,16 @@ __device__ void gemv_op(const StepArgs& a, const StepOp& op, int op_index, const
   constexpr bool kScaleX = std::is_same<Act, __nv_bfloat16>::value;
 
   if (op.epi == kEpiArgmax && tid < kStepMaxM) sm.skey[tid] = 0ull;
-  GemvArgs ga{};
-  ga.w = op.w;
-  ga.x = op.x;
-  ga.x_ld = op.x_ld;
-  ga.norm_w = op.norm_w;
-  ga.eps = a.eps;
-  ga.M = a.M;
   if (fmt == kFmtDense) {
     if (op.norm_w)
-      stage_x<Act, Act, true, false, kNC>(ga, reinterpret_cast<Act*>(sm.xs), p.xs_stride, sm.xexp,
-                                          sm.scratch);
+      stage_op_x<Act, Act, true, false>(a, op, sm, p.xs_stride, xphase);
     else
-      stage_x<Act, Act, false, false, kNC>(ga, reinterpret_cast<Act*>(sm.xs), p.xs_stride,
-                                           sm.xexp, sm.scratch);
+      stage_op_x<Act, Act, false, false>(a, op, sm, p.xs_stride, xphase);
   } else {
     if (op.norm_w)
-      stage_x<Act, __half, true, kScaleX, kNC>(ga, reinterpret_cast<__half*>(sm.xs), p.xs_stride,
-                                               sm.xexp, sm.scratch);
+      stage_op_x<Act, __half, true, kScaleX>(a, op, sm, p.xs_stride, xphase);
     else
-      stage_x<Act, __half, false, kScaleX, kNC>(ga, reinterpret_cast<__half*>(sm.xs),
-                                                p.xs_stride, sm.xexp, sm.scratch);
+      stage_op_x<Act, __half, false, kScaleX>(a, op, sm, p.xs_stride, xphase);
   }
   named_bar_sync(1, kNC * 32);
   if (a.trace && tid == 0) atomicMax(a.trace + op_index * kTraceFields + 1, global_ns());
@@ -264,14 +384,21 @@ __device__ void gemv_op(const StepArgs& a, const StepOp& op, int op_index, const
   const int ch0 = warp * 2, ch1 = warp * 2 + 1;
 
   float acc[4], acc2[4], pacc[4][4];
+  float pre_a = 1.f, pre_b = 1.f, pre_o = 0.f;
+  int t_next = static_cast<int>(u0 / S), s_next = static_cast<int>(u0 % S);
   for (long long u = u0; u < u1; ++u) {
-    const int t = static_cast<int>(u / S), s = static_cast<int>(u % S);
+    const int t = t_next, s = s_next;
+    if (++s_next == S) {
+      s_next = 0;
+      ++t_next;
+    }
     if (u == u0 || s == 0) {
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
         acc[q] = acc2[q] = 0.f;
         pacc[0][q] = pacc[1][q] = pacc[2][q] = pacc[3][q] = 0.f;
       }
+      tile_prefetch<Act>(op, a.M, t, pre_a, pre_b, pre_o);
     }
     if (ok && !mbar_wait(&sm.full[slot], round & 1u, a.status, kStatusFullWaitTimeout)) ok = false;
     if (ok) {
@@ -353,7 +480,7 @@ __device__ void gemv_op(const StepArgs& a, const StepOp& op, int op_index, const
       if (tid == 0) a.tile_cnt[t] = 0;
       named_bar_sync(1, kNC * 32);
     }
-    tile_epilogue<Act>(op, a.M, t, sm);
+    tile_epilogue<Act>(op, a.M, t, sm, pre_a, pre_b, pre_o);
   }
 
   if (op.epi == kEpiArgmax) {
@@ -398,6 +525,7 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const StepArgs a, con
   sm.attn = reinterpret_cast<AttnItemSmem*>(smem + p.attn_off);
   sm.full = reinterpret_cast<uint64_t*>(smem + p.bar_off);
   sm.empty = sm.full + kMaxSlots;
+  sm.xbar = sm.empty + kMaxSlots;
   const int NS = p.slots;
 
   if (threadIdx.x == 0) {
@@ -405,6 +533,7 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const StepArgs a, con
       mbar_init(&sm.full[i], 1);
       mbar_init(&sm.empty[i], kNC);
     }
+    mbar_init(sm.xbar, 1);
     fence_mbar_init();
   }
   __syncthreads();
@@ -416,7 +545,7 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const StepArgs a, con
 
   const unsigned G = gridDim.x;
   int slot = 0, parity = 0;
-  uint32_t round = 0;
+  uint32_t round = 0, xphase = 0;
   bool ok = true;
   for (int k = 0; k < a.n_ops; ++k) {
     if (k > 0 && !grid_wait(a, G * static_cast<unsigned>(k), sm)) break;
@@ -427,7 +556,7 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const StepArgs a, con
     } else if (op.kind == kOpAttn) {
       attn_op<Act, NREP>(op, a.M, sm);
     } else {
-      gemv_op<Act>(a, op, k, sm, p, slot, round, parity, ok);
+      gemv_op<Act>(a, op, k, sm, p, slot, round, parity, ok, xphase);
     }
     if (a.trace) {
       named_bar_sync(1, kNC * 32);
@@ -481,7 +610,7 @@ StepPlan step_plan(int k_pad_max, int rows) {
   const int tv_bytes = 128 * 4;
   const int misc_bytes = 256;
   const int attn_bytes = (kNC * static_cast<int>(sizeof(AttnItemSmem)) + 127) / 128 * 128;
-  const int bar_bytes = 2 * kMaxSlots * 8;
+  const int bar_bytes = (2 * kMaxSlots + 1) * 8;
   const int fixed = x_bytes + red_bytes + tv_bytes + misc_bytes + attn_bytes + bar_bytes + 1024;
   int slots = (kSmemBudget - fixed) / kStageBytes;
   if (slots > kMaxSlots) slots = kMaxSlots;
