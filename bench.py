@@ -36,6 +36,11 @@ sys.path.insert(0, str(ROOT / "dial-27b_b200"))
 
 PROMPT_LEN = 128
 WORKLOAD = "qwen3-8b-w8a16-bs1-decode"
+# DRAM bytes (read + write) of one launch of the W8A16 GEMV on the fused gate/up weight
+# (N=24576, K=4096, M=1), from an `ncu --set full` capture of the same kernel and weight shape
+# with the store epilogue (summary: profiles/gemv_w8a16_gate_up_m1.md).
+GATE_UP_TRAFFIC_BYTES = 100_809_216 + 3_417_088
+GATE_UP_TRAFFIC_SOURCE = "ncu dram__bytes_read+write, gemv_kernel<bf16,W8A16,store> N=24576 K=4096 M=1"
 
 
 def load_peaks() -> dict:
@@ -245,7 +250,8 @@ def run_single(args) -> dict:
         "value": 1000.0 / step_ms, "ms_per_step": step_ms, "e2e_tok_s": args.steps / e2e_s,
         "ttft_s": ttft, "clocks": clk.summary(), "status": status,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                     "frac": achieved / peaks["hbm_gbs"], "traffic": None,
+                     "frac": achieved / peaks["hbm_gbs"], "traffic": GATE_UP_TRAFFIC_BYTES,
+                     "traffic_source": GATE_UP_TRAFFIC_SOURCE,
                      "kernel": "gemv_kernel<bf16,W8A16,SwiGLU,norm> (fused gate/up, N=24576 K=4096 M=1)",
                      "launch_us": k_us, "bytes_per_launch": k_bytes, "peak_source": peaks["source"],
                      "step_bytes": step_bytes,
