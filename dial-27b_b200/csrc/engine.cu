@@ -17,6 +17,7 @@
 
 #include "../../include/dial_b200.h"
 #include "attention.h"
+#include "gemm.h"
 #include "gemv.h"
 #include "layout.h"
 #include "misc.h"
@@ -257,11 +258,42 @@ GemvTuning g_tuning() {
   if (const char* v = std::getenv("DIAL_B200_GEMV_GRID")) t.grid = std::atoi(v);
   if (const char* v = std::getenv("DIAL_B200_PDL")) t.pdl = std::atoi(v) != 0;
   if (const char* v = std::getenv("DIAL_B200_STEP_KERNEL")) t.step_kernel = std::atoi(v) != 0;
+  if (const char* v = std::getenv("DIAL_B200_GEMM_MIN_ROWS")) t.gemm_min_rows = std::atoi(v);
   return t;
 }
 
+// Prefill-sized calls (M >= gemm_min_rows) on a supported W8A16 weight take
+// the tcgen05 GEMM with `scratch` (gemm_scratch_bytes(M, K_pad) bytes);
+// everything else the decode GEMV.
+bool use_gemm(const Linear& L, int M, const void* scratch) {
+  const int min_rows = g_tuning().gemm_min_rows;
+  return scratch && min_rows > 0 && M >= min_rows && gemm_w8a16_supported(L.d);
+}
+
+void run_gemm(const Linear& L, const void* x, int x_ld, const void* norm_w, float eps, void* out,
+              int out_ld, int M, int epi, cudaStream_t s, int* status, void* scratch) {
+  GemmArgs g{};
+  g.w = L.d;
+  g.x = x;
+  g.x_ld = x_ld;
+  g.norm_w = norm_w;
+  g.eps = eps;
+  g.out = out;
+  g.out_ld = out_ld;
+  g.M = M;
+  g.xh = static_cast<__half*>(scratch);
+  const size_t xh_bytes = (static_cast<size_t>(M) * L.d.K_pad * 2 + 255) / 256 * 256;
+  g.xexp = reinterpret_cast<int*>(static_cast<char*>(scratch) + xh_bytes);
+  g.status = status;
+  DIAL_CUDA(gemm_w8a16_launch(g, L.act, epi, s));
+}
+
 void run_linear(const Linear& L, const void* x, int x_ld, const void* norm_w, float eps, void* out,
-                int out_ld, int M, int epi, cudaStream_t s, int* status) {
+                int out_ld, int M, int epi, cudaStream_t s, int* status, void* scratch = nullptr) {
+  if (use_gemm(L, M, scratch)) {
+    run_gemm(L, x, x_ld, norm_w, eps, out, out_ld, M, epi, s, status, scratch);
+    return;
+  }
   GemvArgs a{};
   a.w = L.d;
   a.x = x;
@@ -280,6 +312,7 @@ void run_linear(const Linear& L, const void* x, int x_ld, const void* norm_w, fl
 struct dial_b200_qlinear {
   Linear L;
   int device = 0;
+  DevBuf scratch;  // tcgen05 GEMM staging, grown on the first call with that many rows
 };
 
 // =================================================================== engine
@@ -325,6 +358,7 @@ struct dial_b200_engine {
   DevBuf tok_in, sid, pos, tok_out, rows_scratch;
   DevBuf part_o, part_ml, counters;
   DevBuf amax_key, amax_count;  // head argmax keys / arrival counters, zero between steps
+  DevBuf gemm_scratch;          // prefill GEMM activation staging (max_tokens rows)
   int32_t* h_in = nullptr;   // pinned: [3][max_rows] tokens, sids, positions
   int32_t* h_out = nullptr;  // pinned: [max_rows] tokens + status
   int* status = nullptr;
@@ -455,6 +489,11 @@ void engine_init(dial_b200_engine* e, const dial_b200_model_config& c, int devic
   e->pos.alloc(T * 4);
   e->tok_out.alloc(T * 4);
   e->rows_scratch.alloc(2 * T * 4);
+  {
+    const int kmax = std::max({e->H, e->I, e->QH * e->D});
+    const int kpad = (kmax + 63) / 64 * 64;
+    e->gemm_scratch.alloc(gemm_scratch_bytes(static_cast<int>(T), kpad));
+  }
   if (c.has_head) {
     e->amax_key.alloc(static_cast<size_t>(T) * 8);
     e->amax_count.alloc(static_cast<size_t>(T) * 4);
@@ -594,7 +633,9 @@ void layer_decode(dial_b200_engine* e, LayerW& L, void* hidden, int M, cudaStrea
 void layer_prefill(dial_b200_engine* e, LayerW& L, void* hidden, int M, int session, int p0,
                    cudaStream_t s) {
   const float eps = e->cfg.rms_norm_eps;
-  run_linear(L.qkv, hidden, e->H, L.input_norm.p, eps, e->qkv.p, e->QKV, M, kEpiStore, s, e->status);
+  void* gs = e->gemm_scratch.p;
+  run_linear(L.qkv, hidden, e->H, L.input_norm.p, eps, e->qkv.p, e->QKV, M, kEpiStore, s, e->status,
+             gs);
   AttnPrefillArgs a{};
   a.sh = e->shape();
   a.qkv = e->qkv.p;
@@ -612,10 +653,12 @@ void layer_prefill(dial_b200_engine* e, LayerW& L, void* hidden, int M, int sess
   a.out_ld = e->QH * e->D;
   a.status = e->status;
   DIAL_CUDA(attn_prefill_launch(a, e->cfg.act, s, g_tuning().pdl));
-  run_linear(L.o, e->attn.p, e->QH * e->D, nullptr, eps, hidden, e->H, M, kEpiResidual, s, e->status);
+  run_linear(L.o, e->attn.p, e->QH * e->D, nullptr, eps, hidden, e->H, M, kEpiResidual, s, e->status,
+             gs);
   run_linear(L.gate_up, hidden, e->H, L.post_norm.p, eps, e->inter.p, e->I, M, kEpiSwiglu, s,
-             e->status);
-  run_linear(L.down, e->inter.p, e->I, nullptr, eps, hidden, e->H, M, kEpiResidual, s, e->status);
+             e->status, gs);
+  run_linear(L.down, e->inter.p, e->I, nullptr, eps, hidden, e->H, M, kEpiResidual, s, e->status,
+             gs);
 }
 
 void check_weights(dial_b200_engine* e, int first, int count) {
@@ -971,9 +1014,19 @@ int dial_b200_qlinear_forward(dial_b200_qlinear* lin, const void* x, void* y, in
   return guarded(err, n, [&] {
     DIAL_CHECK(lin && x && y, "null pointer argument");
     DIAL_CHECK(rows >= 1 && rows < (1 << 24), "row count %lld out of range", (long long)rows);
+    const int M = static_cast<int>(rows);
+    void* scratch = nullptr;
+    if (use_gemm(lin->L, M, reinterpret_cast<void*>(1))) {
+      const size_t need = gemm_scratch_bytes(M, lin->L.d.K_pad);
+      if (lin->scratch.bytes < need) {
+        DIAL_CUDA(cudaStreamSynchronize(static_cast<cudaStream_t>(stream)));
+        lin->scratch.alloc(need);
+      }
+      scratch = lin->scratch.p;
+    }
     run_linear(lin->L, x, static_cast<int>(lin->L.in_dim), nullptr, 0.f, y,
-               static_cast<int>(lin->L.out_dim), static_cast<int>(rows), kEpiStore,
-               static_cast<cudaStream_t>(stream), device_status_word());
+               static_cast<int>(lin->L.out_dim), M, kEpiStore, static_cast<cudaStream_t>(stream),
+               device_status_word(), scratch);
   });
 }
 

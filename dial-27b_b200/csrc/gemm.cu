@@ -1,0 +1,428 @@
+// Prefill W8A16 linear (M >= 64 tokens) on the 5th-generation tensor cores.
+//
+// Replaces the reference's prefill kernel dial_w8a16_prefill_f16
+// (dial-core/src/models/qwen3_vl/worker_w8a16.rs:186-224, a 16x16 shared-memory
+// FMA tile) with a tcgen05 GEMM: y[m, n] = s[n] * sum_k q[n, k] * x[m, k].
+//
+// Two kernels per linear:
+//  * prep: one CTA per token row stages x as f16 (RMSNorm fused when the
+//    linear has one, same rounding as the decode path) with a power-of-two
+//    pre-scale per row, into a scratch matrix read by TMA;
+//  * gemm: one CTA per 128 output rows x 128 tokens.  Warp 0 streams the
+//    int8 weight chunks (1-D bulk copies) and the f16 activation tile (2-D
+//    TMA, 128-byte swizzle) into a 4-stage ring; warps 4-11 turn the int8
+//    bytes into f16 (exact: PRMT into the 0x6400 exponent + HSUB2) written in
+//    the same 128-byte-swizzled K-major layout; warp 1 issues
+//    tcgen05.mma.kind::f16 (M=128, N=128, K=16, f32 accumulate in TMEM) and
+//    frees each stage with tcgen05.commit; warps 4-7 read the accumulator
+//    back with tcgen05.ld and apply the row scale, the row pre-scale and the
+//    epilogue (store, residual add, SiLU(gate)*up).
+// All mbarrier waits are bounded: on expiry a status code is recorded and the
+// CTA drains its copies, waits for its MMAs, frees its TMEM and returns.
+#include <cuda.h>
+
+#include "common.cuh"
+#include "gemm.h"
+#include "gemv.h"
+#include "gemv_dev.cuh"
+
+namespace dialb200 {
+namespace {
+
+constexpr int BM = 128;  // output rows (weight rows) per CTA: the MMA M
+constexpr int BN = 128;  // tokens per CTA: the MMA N
+constexpr int BK = 64;   // K per ring stage (one 1 KB int8 chunk per 16 rows)
+constexpr int STAGES = 4;
+constexpr int kThreads = 384;
+constexpr int A_BYTES = BM * BK * 2;
+constexpr int B_BYTES = BN * BK * 2;
+constexpr int RAW_BYTES = BM * BK;
+constexpr int OFF_A = 0;
+constexpr int OFF_B = OFF_A + STAGES * A_BYTES;
+constexpr int OFF_RAW = OFF_B + STAGES * B_BYTES;
+constexpr int OFF_BAR = OFF_RAW + STAGES * RAW_BYTES;  // full, aready, empty [STAGES], accfull
+constexpr int OFF_TMEM = OFF_BAR + (3 * STAGES + 1) * 8;
+constexpr int OFF_XEXP = OFF_TMEM + 16;
+constexpr int SMEM_USED = OFF_XEXP + BN * 4;
+constexpr int SMEM_BYTES = SMEM_USED + 1024;  // room to align the base to 1024
+constexpr int kTmemCols = 128;
+constexpr int kStatusGemmWait = 0x401;
+
+// Instruction descriptor: f32 accumulator, f16 A and B, both K-major,
+// N = BN, M = BM.
+constexpr uint32_t kIdesc = (1u << 4) | (static_cast<uint32_t>(BN >> 3) << 17) |
+                            (static_cast<uint32_t>(BM >> 4) << 24);
+
+// Shared-memory operand descriptor of a K-major tile with 128-byte rows and
+// the 128-byte swizzle: 8-row groups 1024 bytes apart, descriptor version 1.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+  return static_cast<uint64_t>((saddr >> 4) & 0x3FFFu) | (1ull << 16) | (64ull << 32) |
+         (1ull << 46) | (2ull << 61);
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y,
+                                            uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, "
+      "{%2, %3}], [%4];" ::"r"(smem_u32(dst)),
+      "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void tc_mma(uint32_t tmem, uint64_t da, uint64_t db, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(tmem),
+      "l"(da), "l"(db), "r"(kIdesc), "r"(acc));
+}
+
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+      "%11, %12, %13, %14, %15}, [%16];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
+        "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]),
+        "=r"(v[14]), "=r"(v[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// ------------------------------------------------------------------ prep
+// Row m of x -> xh[m][0..Kp) as f16 * 2^-xexp[m] (RMSNorm first when norm_w).
+template <typename Act, bool NORM>
+__global__ void __launch_bounds__(256) prep_kernel(const GemmArgs a) {
+  using AT = ActTraits<Act>;
+  constexpr bool SCALE = std::is_same<Act, __nv_bfloat16>::value;
+  constexpr int NT = 256, VEC = 6;
+  __shared__ float red[16];
+  const int m = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int K = a.w.K, Kp = a.w.K_pad, nv = K / 8;
+  const uint4* xr =
+      reinterpret_cast<const uint4*>(reinterpret_cast<const Act*>(a.x) + static_cast<size_t>(m) * a.x_ld);
+  const uint4* wr = reinterpret_cast<const uint4*>(a.norm_w);
+  uint4 xv[VEC], wv[VEC];
+#pragma unroll
+  for (int j = 0; j < VEC; ++j) {
+    const int i = tid + j * NT;
+    if (i < nv) {
+      xv[j] = xr[i];
+      if (NORM) wv[j] = wr[i];
+    }
+  }
+  float ss = 0.f, am = 0.f;
+#pragma unroll
+  for (int j = 0; j < VEC; ++j) {
+    if (tid + j * NT < nv) {
+      float xf[8], wf[8];
+      unpack8<Act>(xv[j], xf);
+      if (NORM) unpack8<Act>(wv[j], wf);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        ss = fmaf(xf[e], xf[e], ss);
+        am = fmaxf(am, fabsf(NORM ? xf[e] * wf[e] : xf[e]));
+      }
+    }
+  }
+  ss = warp_sum(ss);
+  am = warp_max(am);
+  if (lane == 0) {
+    red[warp] = ss;
+    red[8 + warp] = am;
+  }
+  __syncthreads();
+  ss = 0.f;
+  am = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    ss += red[i];
+    am = fmaxf(am, red[8 + i]);
+  }
+  float rms = 1.f;
+  if (NORM) rms = AT::round(__fsqrt_rn(__fdiv_rn(ss, static_cast<float>(K)) + a.eps));
+  int e = 0;
+  if (SCALE) {
+    const float bound = NORM ? __fdiv_rn(am, rms) * 1.02f : am;
+    if (bound >= 16384.f) e = ilogbf(bound) - 13;
+  }
+  const float sc = exp2i(-e);
+  __half* orow = a.xh + static_cast<size_t>(m) * Kp;
+#pragma unroll
+  for (int j = 0; j < VEC; ++j) {
+    const int i = tid + j * NT;
+    if (i < nv) {
+      float xf[8], wf[8];
+      unpack8<Act>(xv[j], xf);
+      if (NORM) unpack8<Act>(wv[j], wf);
+      uint4 o;
+      __half* h = reinterpret_cast<__half*>(&o);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        float v = xf[q];
+        if (NORM) {
+          v = AT::round(__fdiv_rn(v, rms));
+          v = AT::round(v * wf[q]);
+        }
+        h[q] = __float2half_rn(v * sc);
+      }
+      *reinterpret_cast<uint4*>(orow + static_cast<size_t>(i) * 8) = o;
+    }
+  }
+  for (int k = K + tid; k < Kp; k += NT) orow[k] = __float2half_rn(0.f);
+  if (tid == 0) a.xexp[m] = e;
+}
+
+// ------------------------------------------------------------------ gemm
+template <typename Act, int EPI>
+__global__ void __launch_bounds__(kThreads, 1)
+    w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmap, const GemmArgs a) {
+  using AT = ActTraits<Act>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
+  uint64_t* aready = full + STAGES;
+  uint64_t* empty = aready + STAGES;
+  uint64_t* accfull = empty + STAGES;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + OFF_TMEM);
+  int* sxexp = reinterpret_cast<int*>(smem + OFF_XEXP);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int tok0 = blockIdx.x * BN;
+  const int blk = blockIdx.y;  // 128-row block = tiles [8 blk, 8 blk + 8)
+  const int C = a.w.C;         // k-steps (BK = one chunk)
+
+  if (tid == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&aready[s], 8);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(accfull, 1);
+    fence_mbar_init();
+  }
+  if (warp == 2) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_slot)),
+                 "r"(kTmemCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  if (tid >= 128 && tid < 128 + BN) {
+    const int t = tok0 + (tid - 128);
+    sxexp[tid - 128] = t < a.M ? a.xexp[t] : 0;
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int kb = 0;
+      for (; kb < C; ++kb) {
+        const int s = kb % STAGES;
+        if (kb >= STAGES &&
+            !mbar_wait(&empty[s], static_cast<uint32_t>(kb / STAGES - 1) & 1u, a.status,
+                       kStatusGemmWait))
+          break;
+        mbar_arrive_expect_tx(&full[s], B_BYTES + RAW_BYTES);
+        tma_load_2d(smem + OFF_B + s * B_BYTES, &tmap, kb * BK, tok0, &full[s]);
+        uint8_t* raw = smem + OFF_RAW + s * RAW_BYTES;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          const size_t t = static_cast<size_t>(blk) * 8 + c;
+          bulk_g2s(raw + c * 1024, a.w.tiles + (t * C + kb) * 1024, 1024, &full[s]);
+        }
+      }
+      // every copy issued must land before the CTA retires
+      for (int j = kb > STAGES ? kb - STAGES : 0; j < kb; ++j)
+        if (!mbar_wait(&full[j % STAGES], static_cast<uint32_t>(j / STAGES) & 1u, a.status,
+                       kStatusGemmWait))
+          break;
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA
+    if (lane == 0) {
+      for (int kb = 0; kb < C; ++kb) {
+        const int s = kb % STAGES;
+        const uint32_t ph = static_cast<uint32_t>(kb / STAGES) & 1u;
+        if (!mbar_wait(&aready[s], ph, a.status, kStatusGemmWait)) break;
+        if (!mbar_wait(&full[s], ph, a.status, kStatusGemmWait)) break;
+        tc_fence_after();
+        const uint32_t sa = smem_u32(smem + OFF_A + s * A_BYTES);
+        const uint32_t sb = smem_u32(smem + OFF_B + s * B_BYTES);
+#pragma unroll
+        for (int k16 = 0; k16 < BK / 16; ++k16)
+          tc_mma(tmem, sw128_desc(sa + k16 * 32), sw128_desc(sb + k16 * 32),
+                 (kb | k16) != 0 ? 1u : 0u);
+        tc_commit(&empty[s]);
+      }
+      tc_commit(accfull);
+      // the accumulator (and TMEM) stays in use until every MMA has finished
+      mbar_wait(accfull, 0, a.status, kStatusGemmWait);
+    }
+  } else if (warp >= 4) {
+    // ------------------------------------------------------------ dequant
+    const int dt = tid - 128;
+    const int c = dt >> 5, l = dt & 31;
+    const int row = l >> 1, half = l & 1;
+    const int r = c * 16 + row;  // row of the 128-row block
+    for (int kb = 0; kb < C; ++kb) {
+      const int s = kb % STAGES;
+      if (!mbar_wait(&full[s], static_cast<uint32_t>(kb / STAGES) & 1u, a.status,
+                     kStatusGemmWait))
+        break;
+      const uint8_t* src = smem + OFF_RAW + s * RAW_BYTES + c * 1024 + row * 64 + half * 32;
+      const uint4 w0 = *reinterpret_cast<const uint4*>(src);
+      const uint4 w1 = *reinterpret_cast<const uint4*>(src + 16);
+      const uint32_t wd[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+      uint8_t* arow = smem + OFF_A + s * A_BYTES + (r >> 3) * 1024 + (r & 7) * 128;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int j = half * 4 + q;  // 16-byte chunk = k 8j .. 8j+7
+        uint4 o;
+        o.x = i8_lo_pair(wd[2 * q]);
+        o.y = i8_hi_pair(wd[2 * q]);
+        o.z = i8_lo_pair(wd[2 * q + 1]);
+        o.w = i8_hi_pair(wd[2 * q + 1]);
+        *reinterpret_cast<uint4*>(arow + ((j ^ (r & 7)) << 4)) = o;
+      }
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&aready[s]);
+    }
+
+    // ---------------------------------------------------------- epilogue
+    // the whole warp takes the same branch (tcgen05.ld is warp-collective)
+    const bool acc_ok =
+        warp < 8 && __all_sync(0xffffffffu, mbar_wait(accfull, 0, a.status, kStatusGemmWait));
+    if (acc_ok) {
+      tc_fence_after();
+      const int q = warp - 4;
+      const int rr = 32 * q + lane;  // accumulator lane = row of the block
+      const float rs = a.w.row_scale ? a.w.row_scale[static_cast<size_t>(blk) * 128 + rr] : 1.f;
+      const int n = blk * 128 + rr;
+      const int tr = rr & 15;  // row inside the 16-row tile
+      const int jcol = (blk * 8 + (rr >> 4)) * 8 + (tr & 7);  // SwiGLU output column
+      for (int cb = 0; cb < BN / 16; ++cb) {
+        uint32_t v[16];
+        tmem_ld16(tmem + (static_cast<uint32_t>(32 * q) << 16) + cb * 16, v);
+#pragma unroll
+        for (int jj = 0; jj < 16; ++jj) {
+          const int tk = cb * 16 + jj, tok = tok0 + tk;
+          const float y = AT::round(__uint_as_float(v[jj]) * (exp2i(sxexp[tk]) * rs));
+          if constexpr (EPI == kEpiSwiglu) {
+            const float yu = __shfl_down_sync(0xffffffffu, y, 8);
+            if (tr < 8 && tok < a.M && jcol < a.w.N / 2)
+              reinterpret_cast<Act*>(a.out)[static_cast<size_t>(tok) * a.out_ld + jcol] =
+                  AT::from_f(silu_mul_ref<Act>(y, yu));
+          } else {
+            if (tok < a.M && n < a.w.N) {
+              Act* o = reinterpret_cast<Act*>(a.out) + static_cast<size_t>(tok) * a.out_ld + n;
+              *o = EPI == kEpiResidual ? AT::from_f(y + AT::to_f(*o)) : AT::from_f(y);
+            }
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 2)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                 "r"(kTmemCols));
+}
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) !=
+            cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return static_cast<EncodeTiledFn>(nullptr);
+    return reinterpret_cast<EncodeTiledFn>(p);
+  }();
+  return fn;
+}
+
+template <typename Act, int EPI>
+cudaError_t launch_gemm(const CUtensorMap& map, const GemmArgs& a, cudaStream_t s) {
+  auto kern = w8a16_gemm_kernel<Act, EPI>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+  if (e != cudaSuccess) return e;
+  const dim3 grid((a.M + BN - 1) / BN, a.w.T / 8);
+  kern<<<grid, kThreads, SMEM_BYTES, s>>>(map, a);
+  return cudaGetLastError();
+}
+
+template <typename Act>
+cudaError_t launch_act(const CUtensorMap& map, const GemmArgs& a, int epi, cudaStream_t s) {
+  if (a.norm_w)
+    prep_kernel<Act, true><<<a.M, 256, 0, s>>>(a);
+  else
+    prep_kernel<Act, false><<<a.M, 256, 0, s>>>(a);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  switch (epi) {
+    case kEpiStore: return launch_gemm<Act, kEpiStore>(map, a, s);
+    case kEpiResidual: return launch_gemm<Act, kEpiResidual>(map, a, s);
+    case kEpiSwiglu: return launch_gemm<Act, kEpiSwiglu>(map, a, s);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+}  // namespace
+
+bool gemm_w8a16_supported(const DevQLinear& w) {
+  return w.fmt == kFmtW8A16Row && w.T % 8 == 0 && w.K % 8 == 0 && w.K <= 6 * 8 * 256 &&
+         w.row_scale != nullptr && (w.swiglu ? (w.N / 2) % 64 == 0 : w.N % 128 == 0);
+}
+
+size_t gemm_scratch_bytes(int rows, int k_pad) {
+  const size_t xh = (static_cast<size_t>(rows) * k_pad * 2 + 255) / 256 * 256;
+  return xh + (static_cast<size_t>(rows) * 4 + 255) / 256 * 256;
+}
+
+cudaError_t gemm_w8a16_launch(const GemmArgs& a, int act, int epi, cudaStream_t s) {
+  if (!gemm_w8a16_supported(a.w) || a.M < 1 || !a.xh || !a.xexp || !a.out) return cudaErrorInvalidValue;
+  if ((reinterpret_cast<uintptr_t>(a.x) & 15) || (a.x_ld % 8) ||
+      (a.norm_w && (reinterpret_cast<uintptr_t>(a.norm_w) & 15)) ||
+      (reinterpret_cast<uintptr_t>(a.xh) & 255))
+    return cudaErrorInvalidValue;
+  if (epi == kEpiSwiglu && !a.w.swiglu) return cudaErrorInvalidValue;
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return cudaErrorNotSupported;
+  CUtensorMap map;
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(a.w.K_pad), static_cast<cuuint64_t>(a.M)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(a.w.K_pad) * 2};
+  const cuuint32_t box[2] = {BK, BN};
+  const cuuint32_t estr[2] = {1, 1};
+  if (enc(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, a.xh, dims, strides, box, estr,
+          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    return cudaErrorInvalidValue;
+  return act == 0 ? launch_act<__nv_bfloat16>(map, a, epi, s) : launch_act<__half>(map, a, epi, s);
+}
+
+}  // namespace dialb200

@@ -1,0 +1,36 @@
+// Host interface of the prefill W8A16 GEMM on the 5th-generation tensor cores (gemm.cu).
+#pragma once
+
+#include <cstddef>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include "qlinear.h"
+
+namespace dialb200 {
+
+struct GemmArgs {
+  DevQLinear w;         // W8A16 tiles (int8 ^ 0x80) + f32 row scales
+  const void* x;        // [M][x_ld] activations (bf16 or f16)
+  int x_ld;
+  const void* norm_w;   // RMSNorm weight [K] applied to x first, or null
+  float eps;
+  void* out;            // [M][out_ld]
+  int out_ld;
+  int M;
+  __half* xh;           // scratch [M][w.K_pad]: staged f16 activations
+  int* xexp;            // scratch [M]: per-row power-of-two pre-scale
+  int* status;
+};
+
+// True when the weight can take the tensor-core path: W8A16, 128-row blocks
+// (N % 128 == 0, or 64 gate + 64 up rows for the fused gate/up layout).
+bool gemm_w8a16_supported(const DevQLinear& w);
+
+// Scratch bytes for `rows` rows (xh + xexp), 256-byte aligned pieces.
+size_t gemm_scratch_bytes(int rows, int k_pad);
+
+// act: 0 = bf16, 1 = f16; epi: GemvEpilogue (store, residual, swiglu).
+cudaError_t gemm_w8a16_launch(const GemmArgs& a, int act, int epi, cudaStream_t s);
+
+}  // namespace dialb200
