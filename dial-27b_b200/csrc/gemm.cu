@@ -10,9 +10,9 @@
 //    pre-scale per row, into a scratch matrix read by TMA;
 //  * gemm: one CTA per 128 output rows x 128 tokens.  Warp 0 streams the
 //    int8 weight chunks (1-D bulk copies) and the f16 activation tile (2-D
-//    TMA, 128-byte swizzle) into a 4-stage ring; warps 4-11 turn the int8
+//    TMA, 128-byte swizzle) into a 5-stage ring; warps 4-11 turn the int8
 //    bytes into f16 (exact: PRMT into the 0x6400 exponent + HSUB2) written in
-//    the same 128-byte-swizzled K-major layout; warp 1 issues
+//    the same 128-byte-swizzled K-major layout (4-stage ring); warp 1 issues
 //    tcgen05.mma.kind::f16 (M=128, N=128, K=16, f32 accumulate in TMEM) and
 //    frees each stage with tcgen05.commit; warps 4-7 read the accumulator
 //    back with tcgen05.ld and apply the row scale, the row pre-scale and the
@@ -32,16 +32,18 @@ namespace {
 constexpr int BM = 128;  // output rows (weight rows) per CTA: the MMA M
 constexpr int BN = 128;  // tokens per CTA: the MMA N
 constexpr int BK = 64;   // K per ring stage (one 1 KB int8 chunk per 16 rows)
-constexpr int STAGES = 4;
+constexpr int STAGES = 5;   // load ring: activation tile + int8 weight chunks
+constexpr int ASTAGES = 4;  // dequantized-weight ring (dequant -> MMA -> release latency)
 constexpr int kThreads = 384;
 constexpr int A_BYTES = BM * BK * 2;
 constexpr int B_BYTES = BN * BK * 2;
 constexpr int RAW_BYTES = BM * BK;
 constexpr int OFF_A = 0;
-constexpr int OFF_B = OFF_A + STAGES * A_BYTES;
+constexpr int OFF_B = OFF_A + ASTAGES * A_BYTES;
 constexpr int OFF_RAW = OFF_B + STAGES * B_BYTES;
-constexpr int OFF_BAR = OFF_RAW + STAGES * RAW_BYTES;  // full, aready, empty [STAGES], accfull
-constexpr int OFF_TMEM = OFF_BAR + (3 * STAGES + 1) * 8;
+// barriers: full, lfree [STAGES]; aready, afree [ASTAGES]; accfull
+constexpr int OFF_BAR = OFF_RAW + STAGES * RAW_BYTES;
+constexpr int OFF_TMEM = OFF_BAR + (2 * STAGES + 2 * ASTAGES + 1) * 8;
 constexpr int OFF_XEXP = OFF_TMEM + 16;
 constexpr int SMEM_USED = OFF_XEXP + BN * 4;
 constexpr int SMEM_BYTES = SMEM_USED + 1024;  // room to align the base to 1024
@@ -192,10 +194,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
-  uint64_t* aready = full + STAGES;
-  uint64_t* empty = aready + STAGES;
-  uint64_t* accfull = empty + STAGES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + OFF_BAR);  // loads landed
+  uint64_t* lfree = full + STAGES;       // load slot consumed by dequant (8) and MMA (1)
+  uint64_t* aready = lfree + STAGES;     // dequantized weights written (8 warps)
+  uint64_t* afree = aready + ASTAGES;    // MMAs reading them finished
+  uint64_t* accfull = afree + ASTAGES;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + OFF_TMEM);
   int* sxexp = reinterpret_cast<int*>(smem + OFF_XEXP);
 
@@ -207,8 +210,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (tid == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
+      mbar_init(&lfree[s], 9);
+    }
+    for (int s = 0; s < ASTAGES; ++s) {
       mbar_init(&aready[s], 8);
-      mbar_init(&empty[s], 1);
+      mbar_init(&afree[s], 1);
     }
     mbar_init(accfull, 1);
     fence_mbar_init();
@@ -235,7 +241,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (; kb < C; ++kb) {
         const int s = kb % STAGES;
         if (kb >= STAGES &&
-            !mbar_wait(&empty[s], static_cast<uint32_t>(kb / STAGES - 1) & 1u, a.status,
+            !mbar_wait(&lfree[s], static_cast<uint32_t>(kb / STAGES - 1) & 1u, a.status,
                        kStatusGemmWait))
           break;
         mbar_arrive_expect_tx(&full[s], B_BYTES + RAW_BYTES);
@@ -257,18 +263,22 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---------------------------------------------------------------- MMA
     if (lane == 0) {
       for (int kb = 0; kb < C; ++kb) {
-        const int s = kb % STAGES;
-        const uint32_t ph = static_cast<uint32_t>(kb / STAGES) & 1u;
-        if (!mbar_wait(&aready[s], ph, a.status, kStatusGemmWait)) break;
-        if (!mbar_wait(&full[s], ph, a.status, kStatusGemmWait)) break;
+        const int s = kb % STAGES, sa_i = kb % ASTAGES;
+        if (!mbar_wait(&aready[sa_i], static_cast<uint32_t>(kb / ASTAGES) & 1u, a.status,
+                       kStatusGemmWait))
+          break;
+        if (!mbar_wait(&full[s], static_cast<uint32_t>(kb / STAGES) & 1u, a.status,
+                       kStatusGemmWait))
+          break;
         tc_fence_after();
-        const uint32_t sa = smem_u32(smem + OFF_A + s * A_BYTES);
+        const uint32_t sa = smem_u32(smem + OFF_A + sa_i * A_BYTES);
         const uint32_t sb = smem_u32(smem + OFF_B + s * B_BYTES);
 #pragma unroll
         for (int k16 = 0; k16 < BK / 16; ++k16)
           tc_mma(tmem, sw128_desc(sa + k16 * 32), sw128_desc(sb + k16 * 32),
                  (kb | k16) != 0 ? 1u : 0u);
-        tc_commit(&empty[s]);
+        tc_commit(&afree[sa_i]);
+        tc_commit(&lfree[s]);
       }
       tc_commit(accfull);
       // the accumulator (and TMEM) stays in use until every MMA has finished
@@ -281,15 +291,21 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int row = l >> 1, half = l & 1;
     const int r = c * 16 + row;  // row of the 128-row block
     for (int kb = 0; kb < C; ++kb) {
-      const int s = kb % STAGES;
+      const int s = kb % STAGES, sa_i = kb % ASTAGES;
       if (!mbar_wait(&full[s], static_cast<uint32_t>(kb / STAGES) & 1u, a.status,
                      kStatusGemmWait))
         break;
       const uint8_t* src = smem + OFF_RAW + s * RAW_BYTES + c * 1024 + row * 64 + half * 32;
       const uint4 w0 = *reinterpret_cast<const uint4*>(src);
       const uint4 w1 = *reinterpret_cast<const uint4*>(src + 16);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&lfree[s]);  // raw bytes are in registers
+      if (kb >= ASTAGES &&
+          !mbar_wait(&afree[sa_i], static_cast<uint32_t>(kb / ASTAGES - 1) & 1u, a.status,
+                     kStatusGemmWait))
+        break;
       const uint32_t wd[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
-      uint8_t* arow = smem + OFF_A + s * A_BYTES + (r >> 3) * 1024 + (r & 7) * 128;
+      uint8_t* arow = smem + OFF_A + sa_i * A_BYTES + (r >> 3) * 1024 + (r & 7) * 128;
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
         const int j = half * 4 + q;  // 16-byte chunk = k 8j .. 8j+7
@@ -302,7 +318,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       __syncwarp();
-      if (lane == 0) mbar_arrive(&aready[s]);
+      if (lane == 0) mbar_arrive(&aready[sa_i]);
     }
 
     // ---------------------------------------------------------- epilogue
