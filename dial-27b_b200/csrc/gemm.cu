@@ -8,12 +8,12 @@
 //  * prep: one CTA per token row stages x as f16 (RMSNorm fused when the
 //    linear has one, same rounding as the decode path) with a power-of-two
 //    pre-scale per row, into a scratch matrix read by TMA;
-//  * gemm: one CTA per 128 output rows x 128 tokens.  Warp 0 streams the
+//  * gemm: one CTA per 128 output rows x 256 tokens.  Warp 0 streams the
 //    int8 weight chunks (1-D bulk copies) and the f16 activation tile (2-D
-//    TMA, 128-byte swizzle) into a 5-stage ring; warps 4-11 turn the int8
+//    TMA, 128-byte swizzle) into a 4-stage ring; warps 4-11 turn the int8
 //    bytes into f16 (exact: PRMT into the 0x6400 exponent + HSUB2) written in
-//    the same 128-byte-swizzled K-major layout (4-stage ring); warp 1 issues
-//    tcgen05.mma.kind::f16 (M=128, N=128, K=16, f32 accumulate in TMEM) and
+//    the same 128-byte-swizzled K-major layout (2-stage ring); warp 1 issues
+//    tcgen05.mma.kind::f16 (M=128, N=256, K=16, f32 accumulate in TMEM) and
 //    frees each stage with tcgen05.commit; warps 4-7 read the accumulator
 //    back with tcgen05.ld and apply the row scale, the row pre-scale and the
 //    epilogue (store, residual add, SiLU(gate)*up).
@@ -30,10 +30,10 @@ namespace dialb200 {
 namespace {
 
 constexpr int BM = 128;  // output rows (weight rows) per CTA: the MMA M
-constexpr int BN = 128;  // tokens per CTA: the MMA N
+constexpr int BN = 256;  // tokens per CTA: the MMA N
 constexpr int BK = 64;   // K per ring stage (one 1 KB int8 chunk per 16 rows)
-constexpr int STAGES = 5;   // load ring: activation tile + int8 weight chunks
-constexpr int ASTAGES = 4;  // dequantized-weight ring (dequant -> MMA -> release latency)
+constexpr int STAGES = 4;   // load ring: activation tile + int8 weight chunks
+constexpr int ASTAGES = 2;  // dequantized-weight ring (dequant -> MMA -> release latency)
 constexpr int kThreads = 384;
 constexpr int A_BYTES = BM * BK * 2;
 constexpr int B_BYTES = BN * BK * 2;
@@ -47,7 +47,7 @@ constexpr int OFF_TMEM = OFF_BAR + (2 * STAGES + 2 * ASTAGES + 1) * 8;
 constexpr int OFF_XEXP = OFF_TMEM + 16;
 constexpr int SMEM_USED = OFF_XEXP + BN * 4;
 constexpr int SMEM_BYTES = SMEM_USED + 1024;  // room to align the base to 1024
-constexpr int kTmemCols = 128;
+constexpr int kTmemCols = BN;
 constexpr int kStatusGemmWait = 0x401;
 
 // Instruction descriptor: f32 accumulator, f16 A and B, both K-major,
