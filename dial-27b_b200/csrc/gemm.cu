@@ -8,13 +8,15 @@
 //  * prep: one CTA per token row stages x as f16 (RMSNorm fused when the
 //    linear has one, same rounding as the decode path) with a power-of-two
 //    pre-scale per row, into a scratch matrix read by TMA;
-//  * gemm: one CTA per 128 output rows x 256 tokens.  Warp 0 streams the
+//  * gemm: one CTA per 256 output rows x 256 tokens (128 x 128 when the grid
+//    would not cover the SMs).  Warp 0 streams the
 //    int8 weight chunks (1-D bulk copies) and the f16 activation tile (2-D
-//    TMA, 128-byte swizzle) into a 4-stage ring; warps 4-11 turn the int8
+//    TMA, 128-byte swizzle) into a 3-5 stage ring; warps 4-11 turn the int8
 //    bytes into f16 (exact: PRMT into the 0x6400 exponent + HSUB2) written in
-//    the same 128-byte-swizzled K-major layout (2-stage ring); warp 1 issues
-//    tcgen05.mma.kind::f16 (M=128, N=256, K=16, f32 accumulate in TMEM) and
-//    frees each stage with tcgen05.commit; warps 4-7 read the accumulator
+//    the same 128-byte-swizzled K-major layout (2-4 stage ring); warp 1 issues
+//    tcgen05.mma.kind::f16 (two M=128 halves sharing the activation tile,
+//    N=256, K=16, f32 accumulate in TMEM) and frees each stage with
+//    tcgen05.commit; warps 4-11 read the accumulators
 //    back with tcgen05.ld and apply the row scale, the row pre-scale and the
 //    epilogue (store, residual add, SiLU(gate)*up).
 // All mbarrier waits are bounded: on expiry a status code is recorded and the
@@ -29,31 +31,36 @@
 namespace dialb200 {
 namespace {
 
-constexpr int BM = 128;  // output rows (weight rows) per CTA: the MMA M
-constexpr int BN = 256;  // tokens per CTA: the MMA N
 constexpr int BK = 64;   // K per ring stage (one 1 KB int8 chunk per 16 rows)
-constexpr int STAGES = 4;   // load ring: activation tile + int8 weight chunks
-constexpr int ASTAGES = 2;  // dequantized-weight ring (dequant -> MMA -> release latency)
 constexpr int kThreads = 384;
-constexpr int A_BYTES = BM * BK * 2;
-constexpr int B_BYTES = BN * BK * 2;
-constexpr int RAW_BYTES = BM * BK;
-constexpr int OFF_A = 0;
-constexpr int OFF_B = OFF_A + ASTAGES * A_BYTES;
-constexpr int OFF_RAW = OFF_B + STAGES * B_BYTES;
-// barriers: full, lfree [STAGES]; aready, afree [ASTAGES]; accfull
-constexpr int OFF_BAR = OFF_RAW + STAGES * RAW_BYTES;
-constexpr int OFF_TMEM = OFF_BAR + (2 * STAGES + 2 * ASTAGES + 1) * 8;
-constexpr int OFF_XEXP = OFF_TMEM + 16;
-constexpr int SMEM_USED = OFF_XEXP + BN * 4;
-constexpr int SMEM_BYTES = SMEM_USED + 1024;  // room to align the base to 1024
-constexpr int kTmemCols = BN;
 constexpr int kStatusGemmWait = 0x401;
 
-// Instruction descriptor: f32 accumulator, f16 A and B, both K-major,
-// N = BN, M = BM.
-constexpr uint32_t kIdesc = (1u << 4) | (static_cast<uint32_t>(BN >> 3) << 17) |
-                            (static_cast<uint32_t>(BM >> 4) << 24);
+// Tile configurations: 256 weight rows (two M=128 MMAs sharing the activation
+// tile) x 256 tokens for large grids, 128 x 128 when that would leave SMs idle.
+template <int BM_, int BN_>
+struct Cfg {
+  static constexpr int BM = BM_;  // weight rows per CTA
+  static constexpr int BN = BN_;  // tokens per CTA: the MMA N
+  static constexpr int STAGES = BM == 256 ? 3 : 5;   // load ring: activations + int8 chunks
+  static constexpr int ASTAGES = BM == 256 ? 2 : 4;  // dequantized-weight ring
+  static constexpr int A_BYTES = BM * BK * 2;
+  static constexpr int A_HALF = 128 * BK * 2;  // one 128-row MMA operand
+  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int RAW_BYTES = BM * BK;
+  static constexpr int OFF_A = 0;
+  static constexpr int OFF_B = OFF_A + ASTAGES * A_BYTES;
+  static constexpr int OFF_RAW = OFF_B + STAGES * B_BYTES;
+  // barriers: full, lfree [STAGES]; aready, afree [ASTAGES]; accfull
+  static constexpr int OFF_BAR = OFF_RAW + STAGES * RAW_BYTES;
+  static constexpr int OFF_TMEM = OFF_BAR + (2 * STAGES + 2 * ASTAGES + 1) * 8;
+  static constexpr int OFF_XEXP = OFF_TMEM + 16;
+  static constexpr int SMEM_BYTES = OFF_XEXP + BN * 4 + 1024;  // + room to align to 1024
+  static constexpr int kTmemCols = (BM / 128) * BN;  // one BN-column accumulator per half
+  // instruction descriptor: f32 accumulator, f16 A and B, both K-major, N = BN, M = 128
+  static constexpr uint32_t kIdesc = (1u << 4) | (static_cast<uint32_t>(BN >> 3) << 17) |
+                                     (static_cast<uint32_t>(128 >> 4) << 24);
+  static_assert(SMEM_BYTES <= 232448, "shared memory plan too large");
+};
 
 // Shared-memory operand descriptor of a K-major tile with 128-byte rows and
 // the 128-byte swizzle: 8-row groups 1024 bytes apart, descriptor version 1.
@@ -71,11 +78,12 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
       : "memory");
 }
 
-__device__ __forceinline__ void tc_mma(uint32_t tmem, uint64_t da, uint64_t db, uint32_t acc) {
+__device__ __forceinline__ void tc_mma(uint32_t tmem, uint64_t da, uint64_t db, uint32_t idesc,
+                                       uint32_t acc) {
   asm volatile(
       "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(tmem),
-      "l"(da), "l"(db), "r"(kIdesc), "r"(acc));
+      "l"(da), "l"(db), "r"(idesc), "r"(acc));
 }
 
 __device__ __forceinline__ void tc_commit(uint64_t* bar) {
@@ -187,10 +195,16 @@ __global__ void __launch_bounds__(256) prep_kernel(const GemmArgs a) {
 }
 
 // ------------------------------------------------------------------ gemm
-template <typename Act, int EPI>
+template <typename Act, int EPI, int BM_, int BN_>
 __global__ void __launch_bounds__(kThreads, 1)
     w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmap, const GemmArgs a) {
   using AT = ActTraits<Act>;
+  using G = Cfg<BM_, BN_>;
+  constexpr int BM = G::BM, BN = G::BN, STAGES = G::STAGES, ASTAGES = G::ASTAGES;
+  constexpr int A_BYTES = G::A_BYTES, A_HALF = G::A_HALF, B_BYTES = G::B_BYTES;
+  constexpr int RAW_BYTES = G::RAW_BYTES, OFF_A = G::OFF_A, OFF_B = G::OFF_B;
+  constexpr int OFF_RAW = G::OFF_RAW, OFF_BAR = G::OFF_BAR, OFF_TMEM = G::OFF_TMEM;
+  constexpr int OFF_XEXP = G::OFF_XEXP, kTmemCols = G::kTmemCols;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -204,7 +218,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int tok0 = blockIdx.x * BN;
-  const int blk = blockIdx.y;  // 128-row block = tiles [8 blk, 8 blk + 8)
+  const int blk = blockIdx.y;  // 256-row block = tiles [16 blk, 16 blk + 16)
   const int C = a.w.C;         // k-steps (BK = one chunk)
 
   if (tid == 0) {
@@ -248,8 +262,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         tma_load_2d(smem + OFF_B + s * B_BYTES, &tmap, kb * BK, tok0, &full[s]);
         uint8_t* raw = smem + OFF_RAW + s * RAW_BYTES;
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          const size_t t = static_cast<size_t>(blk) * 8 + c;
+        for (int c = 0; c < BM / 16; ++c) {
+          const size_t t = static_cast<size_t>(blk) * (BM / 16) + c;
           bulk_g2s(raw + c * 1024, a.w.tiles + (t * C + kb) * 1024, 1024, &full[s]);
         }
       }
@@ -274,9 +288,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t sa = smem_u32(smem + OFF_A + sa_i * A_BYTES);
         const uint32_t sb = smem_u32(smem + OFF_B + s * B_BYTES);
 #pragma unroll
-        for (int k16 = 0; k16 < BK / 16; ++k16)
-          tc_mma(tmem, sw128_desc(sa + k16 * 32), sw128_desc(sb + k16 * 32),
-                 (kb | k16) != 0 ? 1u : 0u);
+        for (int k16 = 0; k16 < BK / 16; ++k16) {
+          const uint32_t acc = (kb | k16) != 0 ? 1u : 0u;
+          const uint64_t db = sw128_desc(sb + k16 * 32);
+          tc_mma(tmem, sw128_desc(sa + k16 * 32), db, G::kIdesc, acc);  // rows 0..127
+          if constexpr (BM == 256)  // rows 128..255 into the second accumulator
+            tc_mma(tmem + BN, sw128_desc(sa + A_HALF + k16 * 32), db, G::kIdesc, acc);
+        }
         tc_commit(&afree[sa_i]);
         tc_commit(&lfree[s]);
       }
@@ -286,35 +304,43 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp >= 4) {
     // ------------------------------------------------------------ dequant
+    // thread dt converts BPT bytes: part `part` of row `row` of 16-row chunk c
+    constexpr int BPT = BM / 4;        // 64 (BM 256) or 32 (BM 128) bytes
+    constexpr int TPR = 64 / BPT;      // threads per 64-byte row
+    constexpr int NV = BPT / 16;       // 16-byte loads per thread
     const int dt = tid - 128;
-    const int c = dt >> 5, l = dt & 31;
-    const int row = l >> 1, half = l & 1;
-    const int r = c * 16 + row;  // row of the 128-row block
+    const int c = dt / (16 * TPR), within = dt % (16 * TPR);
+    const int row = within / TPR, part = within % TPR;
+    const int r = c * 16 + row;           // row of the block
+    const int h = r >> 7, rh = r & 127;   // MMA half and row inside it
     for (int kb = 0; kb < C; ++kb) {
       const int s = kb % STAGES, sa_i = kb % ASTAGES;
       if (!mbar_wait(&full[s], static_cast<uint32_t>(kb / STAGES) & 1u, a.status,
                      kStatusGemmWait))
         break;
-      const uint8_t* src = smem + OFF_RAW + s * RAW_BYTES + c * 1024 + row * 64 + half * 32;
-      const uint4 w0 = *reinterpret_cast<const uint4*>(src);
-      const uint4 w1 = *reinterpret_cast<const uint4*>(src + 16);
+      const uint4* src = reinterpret_cast<const uint4*>(smem + OFF_RAW + s * RAW_BYTES +
+                                                        c * 1024 + row * 64 + part * BPT);
+      uint4 wv[NV];
+#pragma unroll
+      for (int i = 0; i < NV; ++i) wv[i] = src[i];
       __syncwarp();
       if (lane == 0) mbar_arrive(&lfree[s]);  // raw bytes are in registers
       if (kb >= ASTAGES &&
           !mbar_wait(&afree[sa_i], static_cast<uint32_t>(kb / ASTAGES - 1) & 1u, a.status,
                      kStatusGemmWait))
         break;
-      const uint32_t wd[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
-      uint8_t* arow = smem + OFF_A + sa_i * A_BYTES + (r >> 3) * 1024 + (r & 7) * 128;
+      uint8_t* arow = smem + OFF_A + sa_i * A_BYTES + h * A_HALF + (rh >> 3) * 1024 + (rh & 7) * 128;
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const int j = half * 4 + q;  // 16-byte chunk = k 8j .. 8j+7
+      for (int i = 0; i < 2 * NV; ++i) {  // 16-byte output chunk j = k 8j .. 8j+7
+        const int j = part * 2 * NV + i;
+        const uint32_t w0 = (&wv[i >> 1].x)[(i & 1) * 2];
+        const uint32_t w1 = (&wv[i >> 1].x)[(i & 1) * 2 + 1];
         uint4 o;
-        o.x = i8_lo_pair(wd[2 * q]);
-        o.y = i8_hi_pair(wd[2 * q]);
-        o.z = i8_lo_pair(wd[2 * q + 1]);
-        o.w = i8_hi_pair(wd[2 * q + 1]);
-        *reinterpret_cast<uint4*>(arow + ((j ^ (r & 7)) << 4)) = o;
+        o.x = i8_lo_pair(w0);
+        o.y = i8_hi_pair(w0);
+        o.z = i8_lo_pair(w1);
+        o.w = i8_hi_pair(w1);
+        *reinterpret_cast<uint4*>(arow + ((j ^ (rh & 7)) << 4)) = o;
       }
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       __syncwarp();
@@ -324,18 +350,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---------------------------------------------------------- epilogue
     // the whole warp takes the same branch (tcgen05.ld is warp-collective)
     const bool acc_ok =
-        warp < 8 && __all_sync(0xffffffffu, mbar_wait(accfull, 0, a.status, kStatusGemmWait));
-    if (acc_ok) {
+        __all_sync(0xffffffffu, mbar_wait(accfull, 0, a.status, kStatusGemmWait));
+    const int hh = (warp - 4) >> 2;  // accumulator half (rows 0-127 or 128-255)
+    if (acc_ok && hh < BM / 128) {
       tc_fence_after();
-      const int q = warp - 4;
-      const int rr = 32 * q + lane;  // accumulator lane = row of the block
-      const float rs = a.w.row_scale ? a.w.row_scale[static_cast<size_t>(blk) * 128 + rr] : 1.f;
-      const int n = blk * 128 + rr;
+      const int q = warp & 3;          // TMEM lane quarter this warp may read
+      const int rr = hh * 128 + 32 * q + lane;  // row of the block
+      const float rs = a.w.row_scale ? a.w.row_scale[static_cast<size_t>(blk) * BM + rr] : 1.f;
+      const int n = blk * BM + rr;
       const int tr = rr & 15;  // row inside the 16-row tile
-      const int jcol = (blk * 8 + (rr >> 4)) * 8 + (tr & 7);  // SwiGLU output column
+      const int jcol = (blk * (BM / 16) + (rr >> 4)) * 8 + (tr & 7);  // SwiGLU output column
       for (int cb = 0; cb < BN / 16; ++cb) {
         uint32_t v[16];
-        tmem_ld16(tmem + (static_cast<uint32_t>(32 * q) << 16) + cb * 16, v);
+        tmem_ld16(tmem + (static_cast<uint32_t>(32 * q) << 16) + hh * BN + cb * 16, v);
 #pragma unroll
         for (int jj = 0; jj < 16; ++jj) {
           const int tk = cb * 16 + jj, tok = tok0 + tk;
@@ -382,18 +409,32 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
-template <typename Act, int EPI>
+template <typename Act, int EPI, int BM, int BN>
 cudaError_t launch_gemm(const CUtensorMap& map, const GemmArgs& a, cudaStream_t s) {
-  auto kern = w8a16_gemm_kernel<Act, EPI>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+  using G = Cfg<BM, BN>;
+  auto kern = w8a16_gemm_kernel<Act, EPI, BM, BN>;
+  cudaError_t e =
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, G::SMEM_BYTES);
   if (e != cudaSuccess) return e;
-  const dim3 grid((a.M + BN - 1) / BN, a.w.T / 8);
-  kern<<<grid, kThreads, SMEM_BYTES, s>>>(map, a);
+  const dim3 grid((a.M + BN - 1) / BN, a.w.T / (BM / 16));
+  kern<<<grid, kThreads, G::SMEM_BYTES, s>>>(map, a);
   return cudaGetLastError();
 }
 
+// 256 x 256 tiles when they give at least half the SMs a CTA (measured: a
+// half-empty wave of the larger tile still beats 3+ waves of 128 x 128),
+// else 128 x 128.
+bool use_big_tiles(const GemmArgs& a) {
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const bool fits = a.w.T % 16 == 0 && (a.w.swiglu ? (a.w.N / 2) % 128 == 0 : a.w.N % 256 == 0);
+  return fits && 2 * static_cast<long long>((a.M + 255) / 256) * (a.w.T / 16) >= sms;
+}
+
 template <typename Act>
-cudaError_t launch_act(const CUtensorMap& map, const GemmArgs& a, int epi, cudaStream_t s) {
+cudaError_t launch_act(const CUtensorMap& map, const GemmArgs& a, int epi, bool big,
+                       cudaStream_t s) {
   if (a.norm_w)
     prep_kernel<Act, true><<<a.M, 256, 0, s>>>(a);
   else
@@ -401,9 +442,15 @@ cudaError_t launch_act(const CUtensorMap& map, const GemmArgs& a, int epi, cudaS
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   switch (epi) {
-    case kEpiStore: return launch_gemm<Act, kEpiStore>(map, a, s);
-    case kEpiResidual: return launch_gemm<Act, kEpiResidual>(map, a, s);
-    case kEpiSwiglu: return launch_gemm<Act, kEpiSwiglu>(map, a, s);
+    case kEpiStore:
+      return big ? launch_gemm<Act, kEpiStore, 256, 256>(map, a, s)
+                 : launch_gemm<Act, kEpiStore, 128, 128>(map, a, s);
+    case kEpiResidual:
+      return big ? launch_gemm<Act, kEpiResidual, 256, 256>(map, a, s)
+                 : launch_gemm<Act, kEpiResidual, 128, 128>(map, a, s);
+    case kEpiSwiglu:
+      return big ? launch_gemm<Act, kEpiSwiglu, 256, 256>(map, a, s)
+                 : launch_gemm<Act, kEpiSwiglu, 128, 128>(map, a, s);
     default: return cudaErrorInvalidValue;
   }
 }
@@ -432,13 +479,15 @@ cudaError_t gemm_w8a16_launch(const GemmArgs& a, int act, int epi, cudaStream_t 
   CUtensorMap map;
   const cuuint64_t dims[2] = {static_cast<cuuint64_t>(a.w.K_pad), static_cast<cuuint64_t>(a.M)};
   const cuuint64_t strides[1] = {static_cast<cuuint64_t>(a.w.K_pad) * 2};
-  const cuuint32_t box[2] = {BK, BN};
+  const bool big = use_big_tiles(a);
+  const cuuint32_t box[2] = {BK, big ? 256u : 128u};
   const cuuint32_t estr[2] = {1, 1};
   if (enc(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, a.xh, dims, strides, box, estr,
           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
     return cudaErrorInvalidValue;
-  return act == 0 ? launch_act<__nv_bfloat16>(map, a, epi, s) : launch_act<__half>(map, a, epi, s);
+  return act == 0 ? launch_act<__nv_bfloat16>(map, a, epi, big, s)
+                  : launch_act<__half>(map, a, epi, big, s);
 }
 
 }  // namespace dialb200
