@@ -297,6 +297,17 @@ def run_pipeline(args) -> None:
         with torch.cuda.stream(stream):
             prompt = torch.as_tensor(_prompt_tokens(cfg.vocab_size), device=dev) \
                 if plan.is_first else None
+            # bring up the NCCL p2p communicators of the stage ring before timing
+            probe = torch.zeros(PROMPT_LEN, cfg.hidden_size, dtype=torch.bfloat16, device=dev)
+            tok_probe = torch.zeros(1, dtype=torch.int32, device=dev)
+            if not plan.is_first:
+                dist.recv(probe, rank - 1)
+            if not plan.is_last:
+                dist.send(probe, rank + 1)
+            else:
+                dist.send(tok_probe, 0)
+            if plan.is_first:
+                dist.recv(tok_probe, world - 1)
             torch.cuda.synchronize()
             dist.barrier()
             t0 = time.perf_counter()
@@ -398,7 +409,9 @@ def run_pipeline(args) -> None:
                 "e2e": {"value": args.steps / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": 4,
                         "d2h_bytes_per_step": 4},
                 "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"],
-                             "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"], "traffic": None,
+                             "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"],
+                             "traffic": GATE_UP_TRAFFIC_BYTES,
+                             "traffic_source": GATE_UP_TRAFFIC_SOURCE,
                              "kernel": "gemv_kernel<bf16,W8A16,SwiGLU,norm> (fused gate/up, "
                                        "N=24576 K=4096 M=1), stage 0",
                              "launch_us": k_us, "bytes_per_launch": k_bytes,
