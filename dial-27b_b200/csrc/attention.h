@@ -38,6 +38,7 @@ struct AttnDecodeArgs {
   int out_ld;
   int M;
   int splits;                // KV splits per (row, kv head); 1 = no scratch use.
+  int min_split_tokens;      // context tokens per split at least (0: 16)
                              // Each row's context is cut into `splits` equal
                              // 16-token-aligned spans at run time.
   float* part_o;             // [M][q_heads][splits][head_dim]

@@ -89,8 +89,12 @@ __device__ __forceinline__ void norm_rope(float (&x)[4], const Act* norm_w, floa
 // A row's context is cut into at most `max_splits` spans of >= 16 tokens.
 constexpr int kMinSplitTokens = 16;
 
-__host__ __device__ __forceinline__ int active_splits(int ctx, int max_splits) {
-  const int need = (ctx + kMinSplitTokens - 1) / kMinSplitTokens;
+// Splits a row of context `ctx` uses: at most max_splits, at least
+// min_tokens (kMinSplitTokens when 0) context tokens per split.
+__host__ __device__ __forceinline__ int active_splits(int ctx, int max_splits,
+                                                      int min_tokens = 0) {
+  const int mt = min_tokens > 0 ? min_tokens : kMinSplitTokens;
+  const int need = (ctx + mt - 1) / mt;
   return need < max_splits ? (need < 1 ? 1 : need) : max_splits;
 }
 
@@ -126,7 +130,7 @@ __device__ void attn_item(const AttnDecodeArgs& a, int m, int kvh, int split, in
   const int32_t* bt = a.block_table + static_cast<size_t>(sid) * a.sh.max_blocks;
   // Splits actually used by this row: short contexts skip the partial/combine
   // round trip.  Uniform over the group, so every warp returns together.
-  const int S = active_splits(ctx, a.splits);
+  const int S = active_splits(ctx, a.splits, a.min_split_tokens);
   if (split >= S) return;
   const int span = ((ctx + S - 1) / S + kPageTokens - 1) / kPageTokens * kPageTokens;
   const int tok0 = split * span;

@@ -259,6 +259,7 @@ GemvTuning g_tuning() {
   if (const char* v = std::getenv("DIAL_B200_PDL")) t.pdl = std::atoi(v) != 0;
   if (const char* v = std::getenv("DIAL_B200_STEP_KERNEL")) t.step_kernel = std::atoi(v) != 0;
   if (const char* v = std::getenv("DIAL_B200_GEMM_MIN_ROWS")) t.gemm_min_rows = std::atoi(v);
+  if (const char* v = std::getenv("DIAL_B200_ATTN_MIN_SPLIT")) t.attn_min_split = std::atoi(v);
   return t;
 }
 
@@ -616,6 +617,7 @@ AttnDecodeArgs decode_attn_args(dial_b200_engine* e, LayerW& L, int M) {
   a.part_ml = e->part_ml.as<float>();
   a.counters = e->counters.as<int>();
   a.status = e->status;
+  a.min_split_tokens = g_tuning().attn_min_split;
   return a;
 }
 
