@@ -440,7 +440,106 @@ def _relaunch_with_torchrun(args) -> None:
     raise SystemExit(subprocess.call(cmd))
 
 
-def _prompt_tokens(vocab: int):
+def run_prefill2048(args) -> dict:
+    """BASELINE config 3 on one GPU: prefill of 2048 seeded token ids (TTFT,
+    first token on the host), then bs1 greedy decode of 256 tokens."""
+    import torch
+
+    import dial_b200
+
+    torch.cuda.set_device(0)
+    n_prompt, n_gen = 2048, 256
+    cfg = dial_b200.Config(max_seq_len=n_prompt + n_gen + 64, max_sessions=1, max_tokens=n_prompt)
+    eng = dial_b200.Engine(cfg, device=0)
+    eng.load_synthetic(seed=0)
+    prompt = _prompt_tokens(cfg.vocab_size, n_prompt)
+    ttfts = []
+    for i in range(args.warmup + args.steps):
+        _, ttft, _ = eng.generate(prompt, 1)
+        if i >= args.warmup:
+            ttfts.append(ttft)
+    ttft = statistics.median(ttfts)
+    first, _, _ = eng.generate(prompt, 1)
+    stream = eng.stream
+    eng.loop_prepare([int(first[0])], [0], [n_prompt])
+    eng.loop_run(1, 8)
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(0) as clk:
+        ev0.record(stream)
+        eng.loop_run(1, n_gen - 8)
+        ev1.record(stream)
+        ev1.synchronize()
+    dec_ms = ev0.elapsed_time(ev1) / (n_gen - 8)
+    status = dial_b200.device_status()
+    H, I, QKV = cfg.hidden_size, cfg.intermediate_size, cfg.qkv_dim
+    flops = 2.0 * n_prompt * cfg.num_hidden_layers * (QKV * H + H * H + 2 * I * H + H * I)
+    return {"metric": "TTFT ms (prefill 2048 tokens, Qwen3-8B W8A16)", "value": ttft * 1e3,
+            "unit": "ms", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ttft * 1e3, "higher_is_better": False, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "qwen3-8b-w8a16-prefill2048-decode256", "prompt_len": n_prompt,
+                       "gen_tokens": n_gen, "batch": 1, "parallelism": "single GPU",
+                       "l2": "inputs larger than L2"},
+            "prefill_tok_s": n_prompt / ttft, "decode_tok_s": 1000.0 / dec_ms,
+            "decode_ms_per_token": dec_ms, "clocks": clk.summary(), "device_status": status,
+            "linear_tflop_per_prefill_approx": flops / 1e12,
+            "e2e": {"value": ttft * 1e3, "unit": "ms", "h2d_bytes_per_step": 4 * n_prompt,
+                    "d2h_bytes_per_step": 4}}
+
+
+def run_ragged32(args) -> dict:
+    """BASELINE config 4 on one GPU: 32 sessions with KV lengths uniform in
+    [128, 8192] (seed 2) in 16-token pages, one decode token per session per
+    iteration (device loop)."""
+    import numpy as np
+    import torch
+
+    import dial_b200
+
+    torch.cuda.set_device(0)
+    n_sess = 32
+    lengths = np.random.default_rng(2).integers(128, 8193, size=n_sess).astype(np.int32)
+    cfg = dial_b200.Config(max_seq_len=8192 + args.steps + args.warmup + 16, max_sessions=n_sess,
+                           max_tokens=64)
+    eng = dial_b200.Engine(cfg, device=0)
+    eng.load_synthetic(seed=0)
+    for sidx in range(n_sess):
+        eng.session_fill_random(sidx, int(lengths[sidx]), seed=2 + sidx)
+    toks = _prompt_tokens(cfg.vocab_size, n_sess)
+    sids = np.arange(n_sess, dtype=np.int32)
+    eng.loop_prepare(toks, sids, lengths)
+    eng.loop_run(n_sess, args.warmup)
+    torch.cuda.synchronize()
+    stream = eng.stream
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(0) as clk:
+        ev0.record(stream)
+        eng.loop_run(n_sess, args.steps)
+        ev1.record(stream)
+        ev1.synchronize()
+    it_ms = ev0.elapsed_time(ev1) / args.steps
+    _, pos = eng.loop_state(n_sess)
+    status = dial_b200.device_status()
+    kv_bytes = float(np.sum(lengths + args.warmup + args.steps / 2)) * 36 * 2 * 8 * 128 * 2
+    w_bytes = sum(eng.linear_bytes(0, w, n_sess) for w in range(4)) * 36 + eng.linear_bytes(0, 4, n_sess)
+    gbs = (kv_bytes + w_bytes) / (it_ms * 1e-3) / 1e9
+    peaks = load_peaks()
+    return {"metric": "decode tok/s (32 ragged sessions, KV 128-8192, Qwen3-8B W8A16)",
+            "value": n_sess * 1000.0 / it_ms, "unit": "tok/s", "n_gpus": 1, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": it_ms, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "qwen3-8b-w8a16-ragged32", "sessions": n_sess,
+                       "kv_lengths": "U[128, 8192] seed 2", "kv_tokens": int(lengths.sum()),
+                       "page_tokens": 16, "parallelism": "single GPU",
+                       "l2": "inputs larger than L2"},
+            "hbm": {"bytes_per_iteration": kv_bytes + w_bytes, "achieved_gbs": gbs,
+                    "frac": gbs / peaks["hbm_gbs"], "peak": peaks["hbm_gbs"]},
+            "clocks": clk.summary(), "device_status": status,
+            "positions_advanced": bool(np.all(pos == lengths + args.warmup + args.steps))}
+
+
+def _prompt_tokens(vocab: int, n: int = PROMPT_LEN):
     import numpy as np
 
     from dial_b200.synth import STREAM_TOKENS
@@ -454,7 +553,7 @@ def _prompt_tokens(vocab: int):
     seed = 1
     base = np.uint64(((seed * 0x9E3779B97F4A7C15) ^ (STREAM_TOKENS * 0xD1B54A32D192ED03)) & ((1 << 64) - 1))
     with np.errstate(over="ignore"):
-        h = mix64(np.arange(PROMPT_LEN, dtype=np.uint64) + base)
+        h = mix64(np.arange(n, dtype=np.uint64) + base)
     return (h % np.uint64(vocab)).astype(np.int32)
 
 
@@ -465,11 +564,19 @@ def main():
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", default="decode", choices=["decode", "prefill2048", "ragged32"],
+                    help="decode (BASELINE config 1, the headline), prefill2048 (config 3 on one "
+                         "GPU), ragged32 (config 4 on one GPU)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
+        return
+    if args.workload != "decode":
+        r = run_prefill2048(args) if args.workload == "prefill2048" else run_ragged32(args)
+        r["gpu_launches"] = None
+        print(json.dumps(r), flush=True)
         return
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if world > 1:

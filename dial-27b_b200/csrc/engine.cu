@@ -376,8 +376,11 @@ struct dial_b200_engine {
                cfg.first_layer + cfg.num_layers - 1);
     return layers[l - cfg.first_layer];
   }
+  // KV splits available to a decode batch of M rows: up to 32 per (row, kv
+  // head), fewer for large batches (4096 / (kv_heads * M), at least 1); the
+  // kernel uses as many as the row's context fills with 16-token spans.
   int splits_for(int M) const {
-    int s = (2 * 148 + KVH * M - 1) / (KVH * M);
+    const int s = 4096 / std::max(1, KVH * M);
     return std::max(1, std::min(32, s));
   }
   AttnShape shape() const {
@@ -623,13 +626,17 @@ AttnDecodeArgs decode_attn_args(dial_b200_engine* e, LayerW& L, int M) {
 
 void layer_decode(dial_b200_engine* e, LayerW& L, void* hidden, int M, cudaStream_t s) {
   const float eps = e->cfg.rms_norm_eps;
-  run_linear(L.qkv, hidden, e->H, L.input_norm.p, eps, e->qkv.p, e->QKV, M, kEpiStore, s, e->status);
+  void* gs = e->gemm_scratch.p;
+  run_linear(L.qkv, hidden, e->H, L.input_norm.p, eps, e->qkv.p, e->QKV, M, kEpiStore, s, e->status,
+             gs);
   const AttnDecodeArgs a = decode_attn_args(e, L, M);
   DIAL_CUDA(attn_decode_launch(a, e->cfg.act, s, g_tuning().pdl));
-  run_linear(L.o, e->attn.p, e->QH * e->D, nullptr, eps, hidden, e->H, M, kEpiResidual, s, e->status);
+  run_linear(L.o, e->attn.p, e->QH * e->D, nullptr, eps, hidden, e->H, M, kEpiResidual, s, e->status,
+             gs);
   run_linear(L.gate_up, hidden, e->H, L.post_norm.p, eps, e->inter.p, e->I, M, kEpiSwiglu, s,
-             e->status);
-  run_linear(L.down, e->inter.p, e->I, nullptr, eps, hidden, e->H, M, kEpiResidual, s, e->status);
+             e->status, gs);
+  run_linear(L.down, e->inter.p, e->I, nullptr, eps, hidden, e->H, M, kEpiResidual, s, e->status,
+             gs);
 }
 
 void layer_prefill(dial_b200_engine* e, LayerW& L, void* hidden, int M, int session, int p0,
