@@ -130,6 +130,7 @@ cudaError_t attn_prefill_launch(const AttnPrefillArgs& a, int act, cudaStream_t 
                              : cudaLaunchKernelEx(&cfg, kv_append_kernel<__half>, a);
     if (e != cudaSuccess) return e;
   }
+  if (attn_prefill_tc_supported(a, act)) return attn_prefill_tc_launch(a, s);
   // Causal attention: row t attends to positions <= p0+t.
   int32_t* pos = a.rows_scratch;
   int32_t* sid = pos + a.M;

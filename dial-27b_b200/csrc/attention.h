@@ -69,7 +69,14 @@ struct AttnPrefillArgs {
   void* out;                   // [M][q_heads*head_dim]
   int out_ld;
   int* status;
+  // tensor-core path (bf16, M >= 64): rotated queries [M][q_heads*head_dim]
+  // scratch and the KV pool's page count; null / 0 keep the CUDA-core path
+  void* q_rot;
+  int num_blocks;
 };
+
+bool attn_prefill_tc_supported(const AttnPrefillArgs& a, int act);
+cudaError_t attn_prefill_tc_launch(const AttnPrefillArgs& a, cudaStream_t s);
 
 cudaError_t attn_prefill_launch(const AttnPrefillArgs& a, int act, cudaStream_t s, bool pdl);
 

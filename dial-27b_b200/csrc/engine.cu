@@ -260,6 +260,7 @@ GemvTuning g_tuning() {
   if (const char* v = std::getenv("DIAL_B200_STEP_KERNEL")) t.step_kernel = std::atoi(v) != 0;
   if (const char* v = std::getenv("DIAL_B200_GEMM_MIN_ROWS")) t.gemm_min_rows = std::atoi(v);
   if (const char* v = std::getenv("DIAL_B200_ATTN_MIN_SPLIT")) t.attn_min_split = std::atoi(v);
+  if (const char* v = std::getenv("DIAL_B200_ATTN_TC")) t.attn_tc = std::atoi(v) != 0;
   return t;
 }
 
@@ -661,6 +662,10 @@ void layer_prefill(dial_b200_engine* e, LayerW& L, void* hidden, int M, int sess
   a.out = e->attn.p;
   a.out_ld = e->QH * e->D;
   a.status = e->status;
+  if (g_tuning().attn_tc) {
+    a.q_rot = e->gemm_scratch.p;  // free between the QKV and o_proj GEMMs
+    a.num_blocks = e->cfg.max_sessions * e->max_blocks;
+  }
   DIAL_CUDA(attn_prefill_launch(a, e->cfg.act, s, g_tuning().pdl));
   run_linear(L.o, e->attn.p, e->QH * e->D, nullptr, eps, hidden, e->H, M, kEpiResidual, s, e->status,
              gs);

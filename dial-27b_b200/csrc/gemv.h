@@ -40,6 +40,7 @@ struct GemvTuning {
   bool step_kernel = false;  // whole decode step as one persistent kernel when supported
   int gemm_min_rows = 64;    // rows from which W8A16 linears take the tcgen05 GEMM (0 = never)
   int attn_min_split = 0;    // decode attention: context tokens per split at least (0 = 16)
+  bool attn_tc = true;       // prefill attention on the tensor cores when supported
 };
 
 // act: 0 = bf16, 1 = f16.  Launches ceil(M/8) kernels on `stream`.
