@@ -539,6 +539,60 @@ def run_ragged32(args) -> dict:
             "positions_advanced": bool(np.all(pos == lengths + args.warmup + args.steps))}
 
 
+def run_quant27b(args, fmt_name: str) -> dict:
+    """BASELINE config 5 on one GPU: the 27B-class dense decoder (64 layers,
+    hidden 5120, 40 q / 8 kv heads, FFN 21504) with FP8 block-128 or NVFP4
+    linears, prefill of 4096 seeded tokens (TTFT) then bs1 greedy decode."""
+    import torch
+
+    import dial_b200
+
+    torch.cuda.set_device(0)
+    fmt = getattr(dial_b200, fmt_name)
+    n_prompt, n_gen = 4096, 256
+    cfg = dial_b200.Config.dense_27b(max_seq_len=n_prompt + n_gen + 64, max_sessions=1,
+                                     max_tokens=n_prompt, linear_fmt=fmt)
+    eng = dial_b200.Engine(cfg, device=0)
+    eng.load_synthetic(seed=0)
+    prompt = _prompt_tokens(cfg.vocab_size, n_prompt)
+    ttfts = []
+    for i in range(args.warmup + args.steps):
+        first, ttft, _ = eng.generate(prompt, 1)
+        if i >= args.warmup:
+            ttfts.append(ttft)
+    ttft = statistics.median(ttfts)
+    eng.loop_prepare([int(first[0])], [0], [n_prompt])
+    eng.loop_run(1, 8)
+    torch.cuda.synchronize()
+    stream = eng.stream
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(0) as clk:
+        ev0.record(stream)
+        eng.loop_run(1, n_gen - 8)
+        ev1.record(stream)
+        ev1.synchronize()
+    dec_ms = ev0.elapsed_time(ev1) / (n_gen - 8)
+    status = dial_b200.device_status()
+    w_bytes = sum(eng.linear_bytes(0, w, 1) for w in range(4)) * cfg.num_hidden_layers + \
+        eng.linear_bytes(0, 4, 1)
+    peaks = load_peaks()
+    gbs = w_bytes / (dec_ms * 1e-3) / 1e9
+    tag = "fp8-block128" if fmt == dial_b200.FMT_FP8_BLOCK128 else "nvfp4"
+    return {"metric": f"decode tok/s (bs1, 27B-class dense, {tag})", "value": 1000.0 / dec_ms,
+            "unit": "tok/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": dec_ms, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": f"dense27b-{tag}-prefill4096-decode256", "layers": 64,
+                       "hidden": 5120, "heads": "40q/8kv", "ffn": 21504, "prompt_len": n_prompt,
+                       "gen_tokens": n_gen, "parallelism": "single GPU",
+                       "l2": "inputs larger than L2"},
+            "ttft_ms": ttft * 1e3, "prefill_tok_s": n_prompt / ttft,
+            "roofline": {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac": gbs / peaks["hbm_gbs"], "bytes_per_token": w_bytes,
+                         "traffic": None, "kernel": "whole decode step (weights only)"},
+            "clocks": clk.summary(), "device_status": status}
+
+
 def _prompt_tokens(vocab: int, n: int = PROMPT_LEN):
     import numpy as np
 
@@ -564,9 +618,11 @@ def main():
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="decode", choices=["decode", "prefill2048", "ragged32"],
+    ap.add_argument("--workload", default="decode",
+                    choices=["decode", "prefill2048", "ragged32", "fp8_27b", "nvfp4_27b"],
                     help="decode (BASELINE config 1, the headline), prefill2048 (config 3 on one "
-                         "GPU), ragged32 (config 4 on one GPU)")
+                         "GPU), ragged32 (config 4 on one GPU), fp8_27b / nvfp4_27b (config 5 on "
+                         "one GPU)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -574,7 +630,13 @@ def main():
         run_reference(args)
         return
     if args.workload != "decode":
-        r = run_prefill2048(args) if args.workload == "prefill2048" else run_ragged32(args)
+        if args.workload == "prefill2048":
+            r = run_prefill2048(args)
+        elif args.workload == "ragged32":
+            r = run_ragged32(args)
+        else:
+            r = run_quant27b(args, "FMT_FP8_BLOCK128" if args.workload == "fp8_27b"
+                             else "FMT_NVFP4_G16")
         r["gpu_launches"] = None
         print(json.dumps(r), flush=True)
         return

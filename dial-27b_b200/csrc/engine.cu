@@ -242,6 +242,45 @@ void build_w8a16_from_device_dense(Linear& L, const void* w_dev, int src_dtype, 
   DIAL_CUDA(cudaStreamSynchronize(s));
 }
 
+// FP8 block-128 or NVFP4 from a dense bf16 device weight [N, K] (synthetic
+// models of the 27B-class configuration), quantized on the device.
+void build_quant_from_device_bf16(Linear& L, int fmt, const uint16_t* w_dev, int act, int64_t N,
+                                  int64_t K, int swiglu, cudaStream_t s) {
+  geometry(L, fmt, N, K, swiglu);
+  L.act = act;
+  alloc_tiles(L);
+  if (fmt == DIAL_FMT_FP8_BLOCK128) {
+    const int64_t nbr = (N + 127) / 128, nbc = (K + 127) / 128;
+    const int ld = static_cast<int>((nbc + 3) / 4 * 4);
+    DevBuf codes(static_cast<size_t>(N * K));
+    L.blk_scale.alloc(static_cast<size_t>(nbr * ld) * sizeof(float));
+    DIAL_CUDA(cudaMemsetAsync(L.blk_scale.p, 0, L.blk_scale.bytes, s));
+    DIAL_CUDA(quantize_fp8_block128_dev(w_dev, static_cast<int>(N), static_cast<int>(K),
+                                        codes.as<uint8_t>(), L.blk_scale.as<float>(), ld, s));
+    DIAL_CUDA(tile_codes(codes.as<uint8_t>(), K, L.d, L.tiles.as<uint8_t>(), s));
+    L.d.blk_scale = L.blk_scale.as<float>();
+    L.d.blk_ld = ld;
+    L.resident = N * K + nbr * nbc * 4;
+  } else if (fmt == DIAL_FMT_NVFP4_G16) {
+    DIAL_CHECK(K % 16 == 0, "NVFP4 needs in_dim %% 16 == 0 (got %lld)", (long long)K);
+    DevBuf packed(static_cast<size_t>(N * K / 2)), sc(static_cast<size_t>(N * K / 16)), amax(16);
+    DIAL_CUDA(quantize_nvfp4_dev(w_dev, N * K, packed.as<uint8_t>(), sc.as<uint8_t>(),
+                                 amax.as<unsigned>(), s));
+    DIAL_CUDA(tile_codes(packed.as<uint8_t>(), K / 2, L.d, L.tiles.as<uint8_t>(), s));
+    DIAL_CUDA(tile_nvfp4_scales(sc.as<uint8_t>(), K / 16, L.d, L.tiles.as<uint8_t>(), s));
+    unsigned bits = 0;
+    DIAL_CUDA(cudaMemcpyAsync(&bits, amax.p, 4, cudaMemcpyDeviceToHost, s));
+    DIAL_CUDA(cudaStreamSynchronize(s));
+    float am = 0.f;
+    std::memcpy(&am, &bits, 4);
+    L.d.global_scale = am > 0.f ? static_cast<float>(static_cast<double>(am) / 6.0 / 448.0) : 1.f;
+    L.resident = N * K / 2 + N * K / 16 + 4;
+  } else {
+    DIAL_CHECK(false, "device quantizer for format %d not available", fmt);
+  }
+  DIAL_CUDA(cudaStreamSynchronize(s));
+}
+
 void build_dense_from_device(Linear& L, const void* w_dev, int act, int64_t N, int64_t K,
                              cudaStream_t s) {
   geometry(L, DIAL_FMT_DENSE, N, K, 0);
@@ -534,8 +573,16 @@ uint64_t layer_stream(int l, int part) { return (static_cast<uint64_t>(l + 1) <<
 
 void engine_load_synthetic(dial_b200_engine* e, uint64_t seed, const uint16_t* table_host) {
   DIAL_CHECK(table_host != nullptr, "normal table is null");
-  DIAL_CHECK(e->cfg.linear_fmt == DIAL_FMT_W8A16_ROW,
-             "synthetic load supports the W8A16 format (engine uses %d)", e->cfg.linear_fmt);
+  const int fmt = e->cfg.linear_fmt;
+  DIAL_CHECK(fmt == DIAL_FMT_W8A16_ROW || fmt == DIAL_FMT_FP8_BLOCK128 || fmt == DIAL_FMT_NVFP4_G16,
+             "synthetic load supports W8A16, FP8 block-128 and NVFP4 (engine uses %d)", fmt);
+  // dense bf16 weight -> this engine's linear format
+  auto build = [&](Linear& L, const uint16_t* w, int64_t N, int64_t K, int swiglu) {
+    if (fmt == DIAL_FMT_W8A16_ROW)
+      build_w8a16_from_device_dense(L, w, kSrcBf16, e->cfg.act, N, K, swiglu, e->stream);
+    else
+      build_quant_from_device_bf16(L, fmt, w, e->cfg.act, N, K, swiglu, e->stream);
+  };
   cudaStream_t s = e->stream;
   DevBuf table(65536 * 2);
   DIAL_CUDA(cudaMemcpy(table.p, table_host, table.bytes, cudaMemcpyHostToDevice));
@@ -554,15 +601,15 @@ void engine_load_synthetic(dial_b200_engine* e, uint64_t seed, const uint16_t* t
     DIAL_CUDA(synth_table_fill(t, nq, seed, layer_stream(l, kPq), 0, tb, s));
     DIAL_CUDA(synth_table_fill(t + nq, nk, seed, layer_stream(l, kPk), 0, tb, s));
     DIAL_CUDA(synth_table_fill(t + nq + nk, nk, seed, layer_stream(l, kPv), 0, tb, s));
-    build_w8a16_from_device_dense(L.qkv, t, kSrcBf16, act, e->QKV, H, 0, s);
+    build(L.qkv, t, e->QKV, H, 0);
     DIAL_CUDA(synth_table_fill(t, static_cast<int64_t>(H) * QH * D, seed, layer_stream(l, kPo), 0, tb, s));
-    build_w8a16_from_device_dense(L.o, t, kSrcBf16, act, H, QH * D, 0, s);
+    build(L.o, t, H, QH * D, 0);
     const int64_t ng = static_cast<int64_t>(I) * H;
     DIAL_CUDA(synth_table_fill(t, ng, seed, layer_stream(l, kPgate), 0, tb, s));
     DIAL_CUDA(synth_table_fill(t + ng, ng, seed, layer_stream(l, kPup), 0, tb, s));
-    build_w8a16_from_device_dense(L.gate_up, t, kSrcBf16, act, 2 * I, H, 1, s);
+    build(L.gate_up, t, 2 * I, H, 1);
     DIAL_CUDA(synth_table_fill(t, static_cast<int64_t>(H) * I, seed, layer_stream(l, kPdown), 0, tb, s));
-    build_w8a16_from_device_dense(L.down, t, kSrcBf16, act, H, I, 0, s);
+    build(L.down, t, H, I, 0);
     fill_ones(L.input_norm, H, s, act);
     fill_ones(L.post_norm, H, s, act);
     fill_ones(L.q_norm, D, s, act);

@@ -1,4 +1,4 @@
-// Prefill W8A16 linear (M >= 64 tokens) on the 5th-generation tensor cores.
+// Prefill W8A16 / FP8 linear (M >= 64 tokens) on the 5th-generation tensor cores.
 //
 // Replaces the reference's prefill kernel dial_w8a16_prefill_f16
 // (dial-core/src/models/qwen3_vl/worker_w8a16.rs:186-224, a 16x16 shared-memory
@@ -12,7 +12,8 @@
 //    would not cover the SMs).  Warp 0 streams the
 //    int8 weight chunks (1-D bulk copies) and the f16 activation tile (2-D
 //    TMA, 128-byte swizzle) into a 3-5 stage ring; warps 4-11 turn the int8
-//    bytes into f16 (exact: PRMT into the 0x6400 exponent + HSUB2) written in
+//    bytes into f16 (exact: PRMT into the 0x6400 exponent + HSUB2; e4m3 codes
+//    by the hardware cvt, times the 128x128 block scale when there is one) written in
 //    the same 128-byte-swizzled K-major layout (2-4 stage ring); warp 1 issues
 //    tcgen05.mma.kind::f16 (two M=128 halves sharing the activation tile,
 //    N=256, K=16, f32 accumulate in TMEM) and frees each stage with
@@ -116,7 +117,7 @@ template <typename Act, bool NORM>
 __global__ void __launch_bounds__(256) prep_kernel(const GemmArgs a) {
   using AT = ActTraits<Act>;
   constexpr bool SCALE = std::is_same<Act, __nv_bfloat16>::value;
-  constexpr int NT = 256, VEC = 6;
+  constexpr int NT = 256, VEC = 12;  // rows up to 24576 columns (27B-class down_proj: 21504)
   __shared__ float red[16];
   const int m = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int K = a.w.K, Kp = a.w.K_pad, nv = K / 8;
@@ -195,7 +196,7 @@ __global__ void __launch_bounds__(256) prep_kernel(const GemmArgs a) {
 }
 
 // ------------------------------------------------------------------ gemm
-template <typename Act, int EPI, int BM_, int BN_>
+template <typename Act, int FMT, int EPI, int BM_, int BN_>
 __global__ void __launch_bounds__(kThreads, 1)
     w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmap, const GemmArgs a) {
   using AT = ActTraits<Act>;
@@ -313,8 +314,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int row = within / TPR, part = within % TPR;
     const int r = c * 16 + row;           // row of the block
     const int h = r >> 7, rh = r & 127;   // MMA half and row inside it
+    // FP8 block-128: this thread's 128-row scale block (original row order;
+    // the fused gate/up tile holds gate rows 8t.. in rows 0-7, up rows I+8t..)
+    const float* bsc_row = nullptr;
+    if constexpr (FMT == kFmtFp8Block128) {
+      const int n = blk * BM + r, t = n >> 4, tr = n & 15;
+      const int orig = !a.w.swiglu ? n : (tr < 8 ? 8 * t + tr : a.w.N / 2 + 8 * t + tr - 8);
+      bsc_row = a.w.blk_scale + static_cast<size_t>(orig / 128) * a.w.blk_ld;
+    }
     for (int kb = 0; kb < C; ++kb) {
       const int s = kb % STAGES, sa_i = kb % ASTAGES;
+      float bscale = 1.f;
+      if constexpr (FMT == kFmtFp8Block128) bscale = __ldg(bsc_row + (kb >> 1));
       if (!mbar_wait(&full[s], static_cast<uint32_t>(kb / STAGES) & 1u, a.status,
                      kStatusGemmWait))
         break;
@@ -336,10 +347,28 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t w0 = (&wv[i >> 1].x)[(i & 1) * 2];
         const uint32_t w1 = (&wv[i >> 1].x)[(i & 1) * 2 + 1];
         uint4 o;
-        o.x = i8_lo_pair(w0);
-        o.y = i8_hi_pair(w0);
-        o.z = i8_lo_pair(w1);
-        o.w = i8_hi_pair(w1);
+        if constexpr (FMT == kFmtW8A16Row) {
+          o.x = i8_lo_pair(w0);
+          o.y = i8_hi_pair(w0);
+          o.z = i8_lo_pair(w1);
+          o.w = i8_hi_pair(w1);
+        } else {
+          o.x = e4m3x2_to_f16x2(static_cast<uint16_t>(w0 & 0xffffu));
+          o.y = e4m3x2_to_f16x2(static_cast<uint16_t>(w0 >> 16));
+          o.z = e4m3x2_to_f16x2(static_cast<uint16_t>(w1 & 0xffffu));
+          o.w = e4m3x2_to_f16x2(static_cast<uint16_t>(w1 >> 16));
+          if constexpr (FMT == kFmtFp8Block128) {
+            // the 128 x 128 block scale varies along K, so it is applied here
+            // (e4m3 * scale rounded to f16; relative error <= 2^-11)
+            uint32_t* ow = &o.x;
+#pragma unroll
+            for (int q2 = 0; q2 < 4; ++q2) {
+              const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&ow[q2]));
+              const __half2 hs = __floats2half2_rn(f.x * bscale, f.y * bscale);
+              ow[q2] = *reinterpret_cast<const uint32_t*>(&hs);
+            }
+          }
+        }
         *reinterpret_cast<uint4*>(arow + ((j ^ (rh & 7)) << 4)) = o;
       }
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -409,10 +438,10 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
-template <typename Act, int EPI, int BM, int BN>
+template <typename Act, int FMT, int EPI, int BM, int BN>
 cudaError_t launch_gemm(const CUtensorMap& map, const GemmArgs& a, cudaStream_t s) {
   using G = Cfg<BM, BN>;
-  auto kern = w8a16_gemm_kernel<Act, EPI, BM, BN>;
+  auto kern = w8a16_gemm_kernel<Act, FMT, EPI, BM, BN>;
   cudaError_t e =
       cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, G::SMEM_BYTES);
   if (e != cudaSuccess) return e;
@@ -432,6 +461,23 @@ bool use_big_tiles(const GemmArgs& a) {
   return fits && 2 * static_cast<long long>((a.M + 255) / 256) * (a.w.T / 16) >= sms;
 }
 
+template <typename Act, int FMT>
+cudaError_t launch_fmt(const CUtensorMap& map, const GemmArgs& a, int epi, bool big,
+                       cudaStream_t s) {
+  switch (epi) {
+    case kEpiStore:
+      return big ? launch_gemm<Act, FMT, kEpiStore, 256, 256>(map, a, s)
+                 : launch_gemm<Act, FMT, kEpiStore, 128, 128>(map, a, s);
+    case kEpiResidual:
+      return big ? launch_gemm<Act, FMT, kEpiResidual, 256, 256>(map, a, s)
+                 : launch_gemm<Act, FMT, kEpiResidual, 128, 128>(map, a, s);
+    case kEpiSwiglu:
+      return big ? launch_gemm<Act, FMT, kEpiSwiglu, 256, 256>(map, a, s)
+                 : launch_gemm<Act, FMT, kEpiSwiglu, 128, 128>(map, a, s);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
 template <typename Act>
 cudaError_t launch_act(const CUtensorMap& map, const GemmArgs& a, int epi, bool big,
                        cudaStream_t s) {
@@ -441,16 +487,10 @@ cudaError_t launch_act(const CUtensorMap& map, const GemmArgs& a, int epi, bool 
     prep_kernel<Act, false><<<a.M, 256, 0, s>>>(a);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  switch (epi) {
-    case kEpiStore:
-      return big ? launch_gemm<Act, kEpiStore, 256, 256>(map, a, s)
-                 : launch_gemm<Act, kEpiStore, 128, 128>(map, a, s);
-    case kEpiResidual:
-      return big ? launch_gemm<Act, kEpiResidual, 256, 256>(map, a, s)
-                 : launch_gemm<Act, kEpiResidual, 128, 128>(map, a, s);
-    case kEpiSwiglu:
-      return big ? launch_gemm<Act, kEpiSwiglu, 256, 256>(map, a, s)
-                 : launch_gemm<Act, kEpiSwiglu, 128, 128>(map, a, s);
+  switch (a.w.fmt) {
+    case kFmtW8A16Row: return launch_fmt<Act, kFmtW8A16Row>(map, a, epi, big, s);
+    case kFmtFp8Row: return launch_fmt<Act, kFmtFp8Row>(map, a, epi, big, s);
+    case kFmtFp8Block128: return launch_fmt<Act, kFmtFp8Block128>(map, a, epi, big, s);
     default: return cudaErrorInvalidValue;
   }
 }
@@ -458,8 +498,11 @@ cudaError_t launch_act(const CUtensorMap& map, const GemmArgs& a, int epi, bool 
 }  // namespace
 
 bool gemm_w8a16_supported(const DevQLinear& w) {
-  return w.fmt == kFmtW8A16Row && w.T % 8 == 0 && w.K % 8 == 0 && w.K <= 6 * 8 * 256 &&
-         w.row_scale != nullptr && (w.swiglu ? (w.N / 2) % 64 == 0 : w.N % 128 == 0);
+  const bool scales = (w.fmt == kFmtW8A16Row || w.fmt == kFmtFp8Row) ? w.row_scale != nullptr
+                     : w.fmt == kFmtFp8Block128                     ? w.blk_scale != nullptr
+                                                                    : false;
+  return scales && w.T % 8 == 0 && w.K % 8 == 0 && w.K <= 12 * 8 * 256 &&
+         (w.swiglu ? (w.N / 2) % 64 == 0 : w.N % 128 == 0);
 }
 
 size_t gemm_scratch_bytes(int rows, int k_pad) {

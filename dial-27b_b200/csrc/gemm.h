@@ -23,8 +23,9 @@ struct GemmArgs {
   int* status;
 };
 
-// True when the weight can take the tensor-core path: W8A16, 128-row blocks
-// (N % 128 == 0, or 64 gate + 64 up rows for the fused gate/up layout).
+// True when the weight can take the tensor-core path: W8A16 or FP8 (row or
+// 128x128 block scales), 128-row blocks (N % 128 == 0, or 64 gate + 64 up
+// rows for the fused gate/up layout).
 bool gemm_w8a16_supported(const DevQLinear& w);
 
 // Scratch bytes for `rows` rows (xh + xexp), 256-byte aligned pieces.

@@ -3,6 +3,8 @@
 // generators used for benchmark weights.
 #include <cstdint>
 
+#include <cuda_fp8.h>
+
 #include "common.cuh"
 #include "layout.h"
 
@@ -175,6 +177,96 @@ __global__ void fill_u16_kernel(uint16_t* out, int64_t n, uint16_t v) {
   if (i < n) out[i] = v;
 }
 
+// ------------------------------------------------- synthetic FP8 / NVFP4
+// e4m3 code of v: round to nearest even, saturating at 448, +0 for zero.
+__device__ __forceinline__ uint8_t to_e4m3(float v) {
+  const uint8_t c = static_cast<uint8_t>(__nv_cvt_float_to_fp8(v, __NV_SATFINITE, __NV_E4M3));
+  return c == 0x80 ? 0 : c;
+}
+__device__ __forceinline__ float e4m3_value(uint8_t c) {
+  const __half_raw h = __nv_cvt_fp8_to_halfraw(static_cast<__nv_fp8_storage_t>(c), __NV_E4M3);
+  return __half2float(__half(h));
+}
+// e2m1 code of v: the nearest of {0, .5, 1, 1.5, 2, 3, 4, 6} (|v| clamped to 6),
+// ties to the smaller magnitude, sign bit 0x8 unless the code is zero.
+__device__ __forceinline__ uint8_t to_e2m1(float v) {
+  const float vals[8] = {0.f, 0.5f, 1.f, 1.5f, 2.f, 3.f, 4.f, 6.f};
+  const float mag = fminf(fabsf(v), 6.f);
+  uint8_t best = 0;
+  float bd = fabsf(mag - vals[0]);
+#pragma unroll
+  for (int i = 1; i < 8; ++i) {
+    const float d = fabsf(mag - vals[i]);
+    if (d < bd) {
+      bd = d;
+      best = static_cast<uint8_t>(i);
+    }
+  }
+  return (v < 0.f && best != 0) ? static_cast<uint8_t>(best | 0x8) : best;
+}
+
+__device__ __forceinline__ float bf16_at(const uint16_t* w, int64_t i) {
+  return __uint_as_float(static_cast<uint32_t>(w[i]) << 16);
+}
+
+// One CTA per 128x128 block: scale = blockmax / 448 (1 when zero), codes = e4m3(w / scale).
+__global__ void fp8_block_quant_kernel(const uint16_t* __restrict__ w, int N, int K,
+                                       uint8_t* __restrict__ codes, float* __restrict__ scales,
+                                       int ld) {
+  __shared__ float red[8];
+  const int r0 = blockIdx.y * 128, c0 = blockIdx.x * 128;
+  const int rows = min(128, N - r0), cols = min(128, K - c0);
+  float am = 0.f;
+  for (int i = threadIdx.x; i < rows * cols; i += blockDim.x)
+    am = fmaxf(am, fabsf(bf16_at(w, static_cast<int64_t>(r0 + i / cols) * K + c0 + i % cols)));
+  am = warp_max(am);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = am;
+  __syncthreads();
+  am = 0.f;
+  for (int i = 0; i < static_cast<int>(blockDim.x >> 5); ++i) am = fmaxf(am, red[i]);
+  const float sc = am > 0.f ? __fdiv_rn(am, 448.f) : 1.f;
+  if (threadIdx.x == 0) scales[static_cast<size_t>(blockIdx.y) * ld + blockIdx.x] = sc;
+  for (int i = threadIdx.x; i < rows * cols; i += blockDim.x) {
+    const int64_t idx = static_cast<int64_t>(r0 + i / cols) * K + c0 + i % cols;
+    codes[idx] = to_e4m3(__fdiv_rn(bf16_at(w, idx), sc));
+  }
+}
+
+__global__ void absmax_kernel(const uint16_t* __restrict__ w, int64_t n, unsigned* out) {
+  float am = 0.f;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    am = fmaxf(am, fabsf(bf16_at(w, i)));
+  am = warp_max(am);
+  if ((threadIdx.x & 31) == 0) atomicMax(out, __float_as_uint(am));  // non-negative floats
+}
+
+// One thread per 16-element group: e4m3 group scale of groupmax / 6 / global,
+// e2m1 codes of w / (scale * global), two per byte (low nibble first).
+__global__ void nvfp4_quant_kernel(const uint16_t* __restrict__ w, int64_t groups,
+                                   const unsigned* __restrict__ amax_bits, uint8_t* __restrict__ packed,
+                                   uint8_t* __restrict__ sc) {
+  const int64_t g = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (g >= groups) return;
+  const float amax = __uint_as_float(*amax_bits);
+  // amax / 6 / 448 in double, rounded once to f32 (the oracle computes it in Python floats)
+  const float gs = amax > 0.f ? static_cast<float>(static_cast<double>(amax) / 6.0 / 448.0) : 1.f;
+  float v[16], gm = 0.f;
+#pragma unroll
+  for (int e = 0; e < 16; ++e) {
+    v[e] = bf16_at(w, g * 16 + e);
+    gm = fmaxf(gm, fabsf(v[e]));
+  }
+  const uint8_t code = to_e4m3(__fdiv_rn(__fdiv_rn(gm, 6.f), gs));
+  sc[g] = code;
+  float sdec = e4m3_value(code) * gs;
+  if (sdec == 0.f) sdec = 1.f;
+#pragma unroll
+  for (int e = 0; e < 16; e += 2)
+    packed[g * 8 + e / 2] = static_cast<uint8_t>(to_e2m1(__fdiv_rn(v[e], sdec)) |
+                                                 (to_e2m1(__fdiv_rn(v[e + 1], sdec)) << 4));
+}
+
 inline unsigned blocks_for(int64_t n, int bs) { return static_cast<unsigned>((n + bs - 1) / bs); }
 
 }  // namespace
@@ -232,6 +324,23 @@ cudaError_t synth_tokens(int32_t* out, int64_t n, uint64_t seed, uint32_t vocab,
 cudaError_t fill_u16(uint16_t* out, int64_t n, uint16_t v, cudaStream_t s) {
   if (n <= 0) return cudaSuccess;
   fill_u16_kernel<<<blocks_for(n, 256), 256, 0, s>>>(out, n, v);
+  return cudaGetLastError();
+}
+
+cudaError_t quantize_fp8_block128_dev(const uint16_t* w_bf16, int N, int K, uint8_t* codes,
+                                      float* scales, int ld, cudaStream_t s) {
+  const dim3 grid((K + 127) / 128, (N + 127) / 128);
+  fp8_block_quant_kernel<<<grid, 256, 0, s>>>(w_bf16, N, K, codes, scales, ld);
+  return cudaGetLastError();
+}
+
+cudaError_t quantize_nvfp4_dev(const uint16_t* w_bf16, int64_t n, uint8_t* packed, uint8_t* sc,
+                               unsigned* amax_bits, cudaStream_t s) {
+  if (n % 16) return cudaErrorInvalidValue;
+  cudaError_t e = cudaMemsetAsync(amax_bits, 0, sizeof(unsigned), s);
+  if (e != cudaSuccess) return e;
+  absmax_kernel<<<1184, 256, 0, s>>>(w_bf16, n, amax_bits);
+  nvfp4_quant_kernel<<<blocks_for(n / 16, 256), 256, 0, s>>>(w_bf16, n / 16, amax_bits, packed, sc);
   return cudaGetLastError();
 }
 

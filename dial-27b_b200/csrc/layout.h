@@ -25,4 +25,14 @@ cudaError_t synth_table_fill(uint16_t* out, int64_t n, uint64_t seed, uint64_t s
 cudaError_t synth_tokens(int32_t* out, int64_t n, uint64_t seed, uint32_t vocab, cudaStream_t s);
 cudaError_t fill_u16(uint16_t* out, int64_t n, uint16_t v, cudaStream_t s);
 
+// Synthetic-weight quantizers on the device (bf16 [N][K] in, the rules of
+// the CPU oracle's quantize_fp8_block128 / quantize_nvfp4):
+//  * FP8 e4m3 codes [N][K] + f32 scales [ceil(N/128)][ld] of blockmax/448;
+//  * NVFP4: e2m1 pairs [n/2] + e4m3 group scales [n/16]; the f32 global scale
+//    amax/6/448 is derived from *amax_bits (written here, read back by the host).
+cudaError_t quantize_fp8_block128_dev(const uint16_t* w_bf16, int N, int K, uint8_t* codes,
+                                      float* scales, int ld, cudaStream_t s);
+cudaError_t quantize_nvfp4_dev(const uint16_t* w_bf16, int64_t n, uint8_t* packed, uint8_t* sc,
+                               unsigned* amax_bits, cudaStream_t s);
+
 }  // namespace dialb200

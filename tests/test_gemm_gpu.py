@@ -122,3 +122,38 @@ def test_layer_prefill_on_tensor_cores(cuda, gemv_only):
     assert_hidden_close(outs[1], ref)
     # the two paths sum in different orders; each is held to the oracle's bound
     assert_hidden_close(outs[0], outs[1])
+
+
+@pytest.mark.parametrize("K,N,M", [(5120, 1024, 64), (1024, 384, 200), (4096, 6144, 96)])
+def test_gemm_fp8_block128_vs_oracle(cuda, K, N, M):
+    """FP8 e4m3 with 128x128 block scales on the tensor
+    cores: the block scale is folded into the f16 operand (relative error
+    <= 2^-11 per weight), so the bound is max |d| <= 2^-7 max|y| + 1e-3 and
+    98% of outputs within 1 bf16 ulp (measured 98.3% at K=5120)."""
+    from dial_b200 import CudaQuantLinear
+
+    rng = np.random.default_rng(K + N + M)
+    w = rng.standard_normal((N, K)).astype(np.float32) * 0.02
+    codes, scales = O.quantize_fp8_block128(w)
+    x = O.bf16_round(rng.standard_normal((M, K)).astype(np.float32))
+    lin = CudaQuantLinear.fp8_block128(codes, scales, K, N)
+    got = lin.forward(_bf16(x, cuda)).float().cpu().numpy()
+    assert_bf16_close(got, O.fp8_block_linear(x, codes, scales, K, N, "bf16"), frac_ulp=0.98)
+
+
+@pytest.mark.parametrize("M", [64, 150])
+def test_gemm_fp8_row_vs_oracle(cuda, M):
+    """FP8 e4m3 with per-row scales (cuda_quant.rs:58-65), f16 activations as
+    the reference's FP8 path: exact f16 operands, row scale in the epilogue."""
+    from dial_b200 import CudaQuantLinear
+
+    K, N = 1024, 512
+    rng = np.random.default_rng(M)
+    w = rng.standard_normal((N, K)).astype(np.float32) * 0.02
+    row_scale = (np.abs(w).max(axis=1) / 448.0).astype(np.float32)
+    codes = O.f32_to_e4m3(w / row_scale[:, None])
+    x = O.f16_round(rng.standard_normal((M, K)).astype(np.float32))
+    lin = CudaQuantLinear.fp8(codes, row_scale, K, N)
+    got = lin.forward(_f16(x, cuda)).float().cpu().numpy()
+    ref = O.fp8_linear(x, codes, row_scale, K, N, "f16")
+    assert np.max(np.abs(got - ref)) <= 2 ** -9 * np.max(np.abs(ref)) + 1e-3
