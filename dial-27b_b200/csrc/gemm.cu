@@ -32,27 +32,33 @@
 namespace dialb200 {
 namespace {
 
-constexpr int BK = 64;   // K per ring stage (one 1 KB int8 chunk per 16 rows)
 constexpr int kThreads = 384;
 constexpr int kStatusGemmWait = 0x401;
 
 // Tile configurations: 256 weight rows (two M=128 MMAs sharing the activation
-// tile) x 256 tokens for large grids, 128 x 128 when that would leave SMs idle.
-template <int BM_, int BN_>
+// tile) x 256 tokens for large grids, 128 x 128 when that would leave SMs idle;
+// K per stage is one weight chunk: 64 (int8 / e4m3) or 128 (NVFP4, 1152-byte
+// chunks with their group scales).  Operand tiles are K-major with 64-column
+// (128-byte) swizzle atoms: A [half][atom][128 rows][128 B], B [atom][BN][128 B].
+template <int BM_, int BN_, int BK_ = 64>
 struct Cfg {
   static constexpr int BM = BM_;  // weight rows per CTA
   static constexpr int BN = BN_;  // tokens per CTA: the MMA N
-  static constexpr int STAGES = BM == 256 ? 3 : 5;   // load ring: activations + int8 chunks
-  static constexpr int ASTAGES = BM == 256 ? 2 : 4;  // dequantized-weight ring
-  static constexpr int A_BYTES = BM * BK * 2;
+  static constexpr int BK = BK_;  // K per ring stage
+  static constexpr int NATOM = BK / 64;
+  static constexpr int CHUNK = BK == 128 ? 1152 : 1024;  // bytes per 16-row weight chunk
+  static constexpr int STAGES = (BM == 256 || BK == 128) ? 3 : 5;   // load ring
+  static constexpr int ASTAGES = (BM == 256 || BK == 128) ? 2 : 4;  // dequantized-weight ring
   static constexpr int A_HALF = 128 * BK * 2;  // one 128-row MMA operand
+  static constexpr int A_BYTES = BM * BK * 2;
+  static constexpr int B_ATOM = BN * 128;
   static constexpr int B_BYTES = BN * BK * 2;
-  static constexpr int RAW_BYTES = BM * BK;
+  static constexpr int RAW_BYTES = (BM / 16) * CHUNK;
   static constexpr int OFF_A = 0;
   static constexpr int OFF_B = OFF_A + ASTAGES * A_BYTES;
   static constexpr int OFF_RAW = OFF_B + STAGES * B_BYTES;
   // barriers: full, lfree [STAGES]; aready, afree [ASTAGES]; accfull
-  static constexpr int OFF_BAR = OFF_RAW + STAGES * RAW_BYTES;
+  static constexpr int OFF_BAR = (OFF_RAW + STAGES * RAW_BYTES + 15) / 16 * 16;
   static constexpr int OFF_TMEM = OFF_BAR + (2 * STAGES + 2 * ASTAGES + 1) * 8;
   static constexpr int OFF_XEXP = OFF_TMEM + 16;
   static constexpr int SMEM_BYTES = OFF_XEXP + BN * 4 + 1024;  // + room to align to 1024
@@ -196,12 +202,13 @@ __global__ void __launch_bounds__(256) prep_kernel(const GemmArgs a) {
 }
 
 // ------------------------------------------------------------------ gemm
-template <typename Act, int FMT, int EPI, int BM_, int BN_>
+template <typename Act, int FMT, int EPI, int BM_, int BN_, int BK_>
 __global__ void __launch_bounds__(kThreads, 1)
     w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmap, const GemmArgs a) {
   using AT = ActTraits<Act>;
-  using G = Cfg<BM_, BN_>;
-  constexpr int BM = G::BM, BN = G::BN, STAGES = G::STAGES, ASTAGES = G::ASTAGES;
+  using G = Cfg<BM_, BN_, BK_>;
+  constexpr int BM = G::BM, BN = G::BN, BK = G::BK, STAGES = G::STAGES, ASTAGES = G::ASTAGES;
+  constexpr int CHUNK = G::CHUNK, NATOM = G::NATOM, B_ATOM = G::B_ATOM;
   constexpr int A_BYTES = G::A_BYTES, A_HALF = G::A_HALF, B_BYTES = G::B_BYTES;
   constexpr int RAW_BYTES = G::RAW_BYTES, OFF_A = G::OFF_A, OFF_B = G::OFF_B;
   constexpr int OFF_RAW = G::OFF_RAW, OFF_BAR = G::OFF_BAR, OFF_TMEM = G::OFF_TMEM;
@@ -260,12 +267,15 @@ __global__ void __launch_bounds__(kThreads, 1)
                        kStatusGemmWait))
           break;
         mbar_arrive_expect_tx(&full[s], B_BYTES + RAW_BYTES);
-        tma_load_2d(smem + OFF_B + s * B_BYTES, &tmap, kb * BK, tok0, &full[s]);
+#pragma unroll
+        for (int at = 0; at < NATOM; ++at)
+          tma_load_2d(smem + OFF_B + s * B_BYTES + at * B_ATOM, &tmap, kb * BK + at * 64, tok0,
+                      &full[s]);
         uint8_t* raw = smem + OFF_RAW + s * RAW_BYTES;
 #pragma unroll
         for (int c = 0; c < BM / 16; ++c) {
           const size_t t = static_cast<size_t>(blk) * (BM / 16) + c;
-          bulk_g2s(raw + c * 1024, a.w.tiles + (t * C + kb) * 1024, 1024, &full[s]);
+          bulk_g2s(raw + c * CHUNK, a.w.tiles + (t * C + kb) * CHUNK, CHUNK, &full[s]);
         }
       }
       // every copy issued must land before the CTA retires
@@ -291,10 +301,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int k16 = 0; k16 < BK / 16; ++k16) {
           const uint32_t acc = (kb | k16) != 0 ? 1u : 0u;
-          const uint64_t db = sw128_desc(sb + k16 * 32);
-          tc_mma(tmem, sw128_desc(sa + k16 * 32), db, G::kIdesc, acc);  // rows 0..127
+          const uint32_t ka = (k16 >> 2) * 16384 + (k16 & 3) * 32;  // atom, 16-col step
+          const uint64_t db = sw128_desc(sb + (k16 >> 2) * B_ATOM + (k16 & 3) * 32);
+          tc_mma(tmem, sw128_desc(sa + ka), db, G::kIdesc, acc);  // rows 0..127
           if constexpr (BM == 256)  // rows 128..255 into the second accumulator
-            tc_mma(tmem + BN, sw128_desc(sa + A_HALF + k16 * 32), db, G::kIdesc, acc);
+            tc_mma(tmem + BN, sw128_desc(sa + A_HALF + ka), db, G::kIdesc, acc);
         }
         tc_commit(&afree[sa_i]);
         tc_commit(&lfree[s]);
@@ -305,6 +316,55 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp >= 4) {
     // ------------------------------------------------------------ dequant
+    if constexpr (FMT == kFmtNvfp4G16) {
+      // 128 rows x 128 K per stage: thread dt takes row dt/2, K half dt%2 =
+      // 32 nibble bytes (four 16-value groups) and its four e4m3 group scales;
+      // e2m1 * e4m3 is exact in f16 (the f32 global scale is in the epilogue)
+      static_assert(BM == 128 && BK == 128, "NVFP4 tiles are 128 x 128 K");
+      const int dt = tid - 128;
+      const int r = dt >> 1, part = dt & 1;
+      const int c = r >> 4, rr = r & 15;
+      for (int kb = 0; kb < C; ++kb) {
+        const int s = kb % STAGES, sa_i = kb % ASTAGES;
+        if (!mbar_wait(&full[s], static_cast<uint32_t>(kb / STAGES) & 1u, a.status,
+                       kStatusGemmWait))
+          break;
+        const uint8_t* ch = smem + OFF_RAW + s * RAW_BYTES + c * CHUNK;
+        const uint4 n0 = *reinterpret_cast<const uint4*>(ch + rr * 64 + part * 32);
+        const uint4 n1 = *reinterpret_cast<const uint4*>(ch + rr * 64 + part * 32 + 16);
+        const uint32_t scw = *reinterpret_cast<const uint32_t*>(ch + 1024 + rr * 8 + part * 4);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&lfree[s]);
+        if (kb >= ASTAGES &&
+            !mbar_wait(&afree[sa_i], static_cast<uint32_t>(kb / ASTAGES - 1) & 1u, a.status,
+                       kStatusGemmWait))
+          break;
+        const uint32_t s01 = e4m3x2_to_f16x2(static_cast<uint16_t>(scw & 0xffffu));
+        const uint32_t s23 = e4m3x2_to_f16x2(static_cast<uint16_t>(scw >> 16));
+        const __half2 sc2[4] = {__low2half2(*reinterpret_cast<const __half2*>(&s01)),
+                                __high2half2(*reinterpret_cast<const __half2*>(&s01)),
+                                __low2half2(*reinterpret_cast<const __half2*>(&s23)),
+                                __high2half2(*reinterpret_cast<const __half2*>(&s23))};
+        const uint32_t wd[8] = {n0.x, n0.y, n0.z, n0.w, n1.x, n1.y, n1.z, n1.w};
+        uint8_t* arow = smem + OFF_A + sa_i * A_BYTES + part * 16384 + (r >> 3) * 1024 +
+                        (r & 7) * 128;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {  // word i = 8 values = one 16-byte output chunk
+          uint32_t o4[4];
+          e2m1x8_to_f16x2x4(wd[i], o4);
+#pragma unroll
+          for (int q2 = 0; q2 < 4; ++q2) {
+            const __half2 hv = __hmul2(*reinterpret_cast<const __half2*>(&o4[q2]), sc2[i >> 1]);
+            o4[q2] = *reinterpret_cast<const uint32_t*>(&hv);
+          }
+          *reinterpret_cast<uint4*>(arow + ((i ^ (r & 7)) << 4)) =
+              make_uint4(o4[0], o4[1], o4[2], o4[3]);
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&aready[sa_i]);
+      }
+    } else {
     // thread dt converts BPT bytes: part `part` of row `row` of 16-row chunk c
     constexpr int BPT = BM / 4;        // 64 (BM 256) or 32 (BM 128) bytes
     constexpr int TPR = 64 / BPT;      // threads per 64-byte row
@@ -330,7 +390,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                      kStatusGemmWait))
         break;
       const uint4* src = reinterpret_cast<const uint4*>(smem + OFF_RAW + s * RAW_BYTES +
-                                                        c * 1024 + row * 64 + part * BPT);
+                                                        c * CHUNK + row * 64 + part * BPT);
       uint4 wv[NV];
 #pragma unroll
       for (int i = 0; i < NV; ++i) wv[i] = src[i];
@@ -375,6 +435,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&aready[sa_i]);
     }
+    }
 
     // ---------------------------------------------------------- epilogue
     // the whole warp takes the same branch (tcgen05.ld is warp-collective)
@@ -385,7 +446,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const int q = warp & 3;          // TMEM lane quarter this warp may read
       const int rr = hh * 128 + 32 * q + lane;  // row of the block
-      const float rs = a.w.row_scale ? a.w.row_scale[static_cast<size_t>(blk) * BM + rr] : 1.f;
+      float rs = a.w.row_scale ? a.w.row_scale[static_cast<size_t>(blk) * BM + rr] : 1.f;
+      if constexpr (FMT == kFmtNvfp4G16) rs *= a.w.global_scale;
       const int n = blk * BM + rr;
       const int tr = rr & 15;  // row inside the 16-row tile
       const int jcol = (blk * (BM / 16) + (rr >> 4)) * 8 + (tr & 7);  // SwiGLU output column
@@ -438,10 +500,10 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
-template <typename Act, int FMT, int EPI, int BM, int BN>
+template <typename Act, int FMT, int EPI, int BM, int BN, int BK = 64>
 cudaError_t launch_gemm(const CUtensorMap& map, const GemmArgs& a, cudaStream_t s) {
-  using G = Cfg<BM, BN>;
-  auto kern = w8a16_gemm_kernel<Act, FMT, EPI, BM, BN>;
+  using G = Cfg<BM, BN, BK>;
+  auto kern = w8a16_gemm_kernel<Act, FMT, EPI, BM, BN, BK>;
   cudaError_t e =
       cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, G::SMEM_BYTES);
   if (e != cudaSuccess) return e;
@@ -464,17 +526,26 @@ bool use_big_tiles(const GemmArgs& a) {
 template <typename Act, int FMT>
 cudaError_t launch_fmt(const CUtensorMap& map, const GemmArgs& a, int epi, bool big,
                        cudaStream_t s) {
-  switch (epi) {
-    case kEpiStore:
-      return big ? launch_gemm<Act, FMT, kEpiStore, 256, 256>(map, a, s)
-                 : launch_gemm<Act, FMT, kEpiStore, 128, 128>(map, a, s);
-    case kEpiResidual:
-      return big ? launch_gemm<Act, FMT, kEpiResidual, 256, 256>(map, a, s)
-                 : launch_gemm<Act, FMT, kEpiResidual, 128, 128>(map, a, s);
-    case kEpiSwiglu:
-      return big ? launch_gemm<Act, FMT, kEpiSwiglu, 256, 256>(map, a, s)
-                 : launch_gemm<Act, FMT, kEpiSwiglu, 128, 128>(map, a, s);
-    default: return cudaErrorInvalidValue;
+  if constexpr (FMT == kFmtNvfp4G16) {
+    switch (epi) {
+      case kEpiStore: return launch_gemm<Act, FMT, kEpiStore, 128, 128, 128>(map, a, s);
+      case kEpiResidual: return launch_gemm<Act, FMT, kEpiResidual, 128, 128, 128>(map, a, s);
+      case kEpiSwiglu: return launch_gemm<Act, FMT, kEpiSwiglu, 128, 128, 128>(map, a, s);
+      default: return cudaErrorInvalidValue;
+    }
+  } else {
+    switch (epi) {
+      case kEpiStore:
+        return big ? launch_gemm<Act, FMT, kEpiStore, 256, 256>(map, a, s)
+                   : launch_gemm<Act, FMT, kEpiStore, 128, 128>(map, a, s);
+      case kEpiResidual:
+        return big ? launch_gemm<Act, FMT, kEpiResidual, 256, 256>(map, a, s)
+                   : launch_gemm<Act, FMT, kEpiResidual, 128, 128>(map, a, s);
+      case kEpiSwiglu:
+        return big ? launch_gemm<Act, FMT, kEpiSwiglu, 256, 256>(map, a, s)
+                   : launch_gemm<Act, FMT, kEpiSwiglu, 128, 128>(map, a, s);
+      default: return cudaErrorInvalidValue;
+    }
   }
 }
 
@@ -491,6 +562,7 @@ cudaError_t launch_act(const CUtensorMap& map, const GemmArgs& a, int epi, bool 
     case kFmtW8A16Row: return launch_fmt<Act, kFmtW8A16Row>(map, a, epi, big, s);
     case kFmtFp8Row: return launch_fmt<Act, kFmtFp8Row>(map, a, epi, big, s);
     case kFmtFp8Block128: return launch_fmt<Act, kFmtFp8Block128>(map, a, epi, big, s);
+    case kFmtNvfp4G16: return launch_fmt<Act, kFmtNvfp4G16>(map, a, epi, false, s);
     default: return cudaErrorInvalidValue;
   }
 }
@@ -500,7 +572,7 @@ cudaError_t launch_act(const CUtensorMap& map, const GemmArgs& a, int epi, bool 
 bool gemm_w8a16_supported(const DevQLinear& w) {
   const bool scales = (w.fmt == kFmtW8A16Row || w.fmt == kFmtFp8Row) ? w.row_scale != nullptr
                      : w.fmt == kFmtFp8Block128                     ? w.blk_scale != nullptr
-                                                                    : false;
+                                                                    : w.fmt == kFmtNvfp4G16;
   return scales && w.T % 8 == 0 && w.K % 8 == 0 && w.K <= 12 * 8 * 256 &&
          (w.swiglu ? (w.N / 2) % 64 == 0 : w.N % 128 == 0);
 }
@@ -522,8 +594,8 @@ cudaError_t gemm_w8a16_launch(const GemmArgs& a, int act, int epi, cudaStream_t 
   CUtensorMap map;
   const cuuint64_t dims[2] = {static_cast<cuuint64_t>(a.w.K_pad), static_cast<cuuint64_t>(a.M)};
   const cuuint64_t strides[1] = {static_cast<cuuint64_t>(a.w.K_pad) * 2};
-  const bool big = use_big_tiles(a);
-  const cuuint32_t box[2] = {BK, big ? 256u : 128u};
+  const bool big = a.w.fmt != kFmtNvfp4G16 && use_big_tiles(a);
+  const cuuint32_t box[2] = {64, big ? 256u : 128u};
   const cuuint32_t estr[2] = {1, 1};
   if (enc(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, a.xh, dims, strides, box, estr,
           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,

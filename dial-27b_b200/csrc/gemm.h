@@ -23,9 +23,10 @@ struct GemmArgs {
   int* status;
 };
 
-// True when the weight can take the tensor-core path: W8A16 or FP8 (row or
-// 128x128 block scales), 128-row blocks (N % 128 == 0, or 64 gate + 64 up
-// rows for the fused gate/up layout).
+// True when the weight can take the tensor-core path: W8A16, FP8 (row or
+// 128x128 block scales) or NVFP4 (e4m3 scale per 16 inputs, f32 global
+// scale), 128-row blocks (N % 128 == 0, or 64 gate + 64 up rows for the
+// fused gate/up layout), K <= 24576.
 bool gemm_w8a16_supported(const DevQLinear& w);
 
 // Scratch bytes for `rows` rows (xh + xexp), 256-byte aligned pieces.

@@ -157,3 +157,35 @@ def test_gemm_fp8_row_vs_oracle(cuda, M):
     got = lin.forward(_f16(x, cuda)).float().cpu().numpy()
     ref = O.fp8_linear(x, codes, row_scale, K, N, "f16")
     assert np.max(np.abs(got - ref)) <= 2 ** -9 * np.max(np.abs(ref)) + 1e-3
+
+
+@pytest.mark.parametrize("K,N,M", [(1024, 512, 64), (4096, 1024, 200), (5120, 256, 130)])
+def test_gemm_nvfp4_vs_oracle(cuda, K, N, M):
+    """NVFP4 (e2m1 codes, e4m3 scale per 16 inputs, f32 global scale;
+    cuda_quant.rs:67-100) on the tensor cores: e2m1 x e4m3 is exact in f16,
+    the global scale is applied in the f32 epilogue, so the bound is the
+    W8A16 one (f32 accumulation order only)."""
+    from dial_b200 import CudaQuantLinear
+
+    rng = np.random.default_rng(K + 3 * N + M)
+    w = rng.standard_normal((N, K)).astype(np.float32) * 0.02
+    packed, sc, gs = O.quantize_nvfp4(w)
+    x = O.bf16_round(rng.standard_normal((M, K)).astype(np.float32))
+    lin = CudaQuantLinear.nvfp4(packed, sc, gs, K, N, act=torch.bfloat16)
+    got = lin.forward(_bf16(x, cuda)).float().cpu().numpy()
+    assert_bf16_close(got, O.nvfp4_linear(x, packed, sc, gs, K, N, "bf16"))
+
+
+def test_gemm_nvfp4_matches_gemv(cuda, gemv_only):
+    from dial_b200 import CudaQuantLinear
+
+    rng = np.random.default_rng(4)
+    K, N, M = 2048, 768, 96
+    w = rng.standard_normal((N, K)).astype(np.float32) * 0.05
+    packed, sc, gs = O.quantize_nvfp4(w)
+    lin = CudaQuantLinear.nvfp4(packed, sc, gs, K, N, act=torch.bfloat16)
+    xt = _bf16(O.bf16_round(rng.standard_normal((M, K)).astype(np.float32)), cuda)
+    tc = lin.forward(xt).float().cpu().numpy()
+    with gemv_only:
+        gv = lin.forward(xt).float().cpu().numpy()
+    assert_bf16_close(tc, gv)
