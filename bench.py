@@ -484,6 +484,8 @@ def run_prefill2048(args) -> dict:
             "prefill_tok_s": n_prompt / ttft, "decode_tok_s": 1000.0 / dec_ms,
             "decode_ms_per_token": dec_ms, "clocks": clk.summary(), "device_status": status,
             "linear_tflop_per_prefill_approx": flops / 1e12,
+            "gpu_launches": eng.prefill_kernel_count(n_prompt) * args.steps,
+            "decode_gpu_launches_per_token": eng.step_kernel_count(1),
             "e2e": {"value": ttft * 1e3, "unit": "ms", "h2d_bytes_per_step": 4 * n_prompt,
                     "d2h_bytes_per_step": 4}}
 
@@ -536,6 +538,7 @@ def run_ragged32(args) -> dict:
             "hbm": {"bytes_per_iteration": kv_bytes + w_bytes, "achieved_gbs": gbs,
                     "frac": gbs / peaks["hbm_gbs"], "peak": peaks["hbm_gbs"]},
             "clocks": clk.summary(), "device_status": status,
+            "gpu_launches": eng.step_kernel_count(n_sess) * args.steps,
             "positions_advanced": bool(np.all(pos == lengths + args.warmup + args.steps))}
 
 
@@ -590,7 +593,9 @@ def run_quant27b(args, fmt_name: str) -> dict:
             "roofline": {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                          "frac": gbs / peaks["hbm_gbs"], "bytes_per_token": w_bytes,
                          "traffic": None, "kernel": "whole decode step (weights only)"},
-            "clocks": clk.summary(), "device_status": status}
+            "clocks": clk.summary(), "device_status": status,
+            "gpu_launches": eng.step_kernel_count(1) * (n_gen - 8),
+            "prefill_gpu_launches": eng.prefill_kernel_count(n_prompt)}
 
 
 def _prompt_tokens(vocab: int, n: int = PROMPT_LEN):
@@ -637,7 +642,6 @@ def main():
         else:
             r = run_quant27b(args, "FMT_FP8_BLOCK128" if args.workload == "fp8_27b"
                              else "FMT_NVFP4_G16")
-        r["gpu_launches"] = None
         print(json.dumps(r), flush=True)
         return
     world = int(os.environ.get("WORLD_SIZE", "1"))

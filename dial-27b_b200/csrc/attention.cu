@@ -28,10 +28,9 @@ constexpr int kD = kHeadDim;
 template <typename Act, int NREP>
 __global__ void __launch_bounds__(NREP * 32) attn_decode_kernel(const AttnDecodeArgs a) {
   pdl_launch_dependents();
-  pdl_wait();
   __shared__ AttnItemSmem sm;
-  attn_item<Act, NREP>(a, blockIdx.z, blockIdx.x, blockIdx.y, threadIdx.x >> 5, threadIdx.x & 31,
-                       sm, 1);
+  attn_item<Act, NREP, true>(a, blockIdx.z, blockIdx.x, blockIdx.y, threadIdx.x >> 5,
+                             threadIdx.x & 31, sm, 1);
 }
 
 // Prefill KV append: token t of the session at position p0+t.  One warp per

@@ -45,6 +45,11 @@ struct AttnDecodeArgs {
   float* part_ml;            // [M][q_heads][splits][2]
   int* counters;             // [M][kv_heads], zero on entry, left zero on exit
   int* status;
+  // 1: sid, pos, the block table and the KV pages of positions < pos[m] are
+  // complete before the launch (nothing a programmatically overlapped
+  // predecessor writes), so the kernel reads them before griddepcontrol.wait
+  // and waits only for q / k / v.  0: everything is read after the wait.
+  int rows_ready;
 };
 
 // Scratch bytes needed for (M, splits).

@@ -110,14 +110,19 @@ struct AttnItemSmem {
 };
 
 // Process item (m, kvh, split) of `a` with NREP warps; `r` = this warp's
-// index in the group, `bar_id` a named barrier owned by the group.
-template <typename Act, int NREP>
+// index in the group, `bar_id` a named barrier owned by the group.  PDL: the
+// item executes griddepcontrol.wait itself, after the reads that a.rows_ready
+// allows before it (block ids, the span's first K/V page, norm weights and
+// RoPE rows); an item with nothing to do then exits without waiting.
+template <typename Act, int NREP, bool PDL = false>
 __device__ void attn_item(const AttnDecodeArgs& a, int m, int kvh, int split, int r, int lane,
                           AttnItemSmem& sm, int bar_id) {
   using AT = ActTraits<Act>;
   const int QH = a.sh.q_heads, KVH = a.sh.kv_heads;
   const int h = kvh * NREP + r;
   auto group_sync = [&]() { named_bar_sync(bar_id, NREP * 32); };
+  const bool early = PDL && a.rows_ready != 0;
+  if (PDL && !early) pdl_wait();
 
   const int sid = a.sid[m];
   int pos = a.pos[m];
@@ -148,10 +153,12 @@ __device__ void attn_item(const AttnDecodeArgs& a, int m, int kvh, int split, in
   // id of the span's first page, q (and the new k/v), norm weights, cos/sin.
   const int blk_first = bt[tok0 / kPageTokens];
   float q[4], kn[4] = {0.f, 0.f, 0.f, 0.f}, vn[4] = {0.f, 0.f, 0.f, 0.f};
-  load4_cg(qkv + h * kHeadDim + lane * 4, q);
-  if (do_kv) {
-    load4_cg(qkv + (QH + kvh) * kHeadDim + lane * 4, kn);
-    load4_cg(qkv + (QH + KVH + kvh) * kHeadDim + lane * 4, vn);
+  if (!early) {
+    load4_cg(qkv + h * kHeadDim + lane * 4, q);
+    if (do_kv) {
+      load4_cg(qkv + (QH + kvh) * kHeadDim + lane * 4, kn);
+      load4_cg(qkv + (QH + KVH + kvh) * kHeadDim + lane * 4, vn);
+    }
   }
   float qw[4], kw[4], cs[4], sn[4];
   load4(reinterpret_cast<const Act*>(a.q_norm_w) + lane * 4, qw);
@@ -167,6 +174,16 @@ __device__ void attn_item(const AttnDecodeArgs& a, int m, int kvh, int split, in
     for (int j = 0; j < kPageTokens; ++j) {
       kr[j] = *reinterpret_cast<const uint2*>(kpool + base + j * kHeadDim);
       vr[j] = *reinterpret_cast<const uint2*>(vpool + base + j * kHeadDim);
+    }
+  }
+  if (early) {
+    // the row pos[m] of this page is the new token: it is taken from q/k/v
+    // below, never from the (not yet written) page
+    pdl_wait();
+    load4_cg(qkv + h * kHeadDim + lane * 4, q);
+    if (do_kv) {
+      load4_cg(qkv + (QH + kvh) * kHeadDim + lane * 4, kn);
+      load4_cg(qkv + (QH + KVH + kvh) * kHeadDim + lane * 4, vn);
     }
   }
 

@@ -669,6 +669,9 @@ AttnDecodeArgs decode_attn_args(dial_b200_engine* e, LayerW& L, int M) {
   a.counters = e->counters.as<int>();
   a.status = e->status;
   a.min_split_tokens = g_tuning().attn_min_split;
+  // every caller of layer_decode starts from completed sessions, positions
+  // and KV: a graph launch (root node), or an eager call after a host sync
+  a.rows_ready = 1;
   return a;
 }
 
@@ -1513,15 +1516,66 @@ int dial_b200_session_fill_random(dial_b200_engine* eng, int32_t session, int64_
   });
 }
 
+namespace {
+
+int64_t kernel_nodes(cudaGraph_t g) {
+  size_t n = 0;
+  DIAL_CUDA(cudaGraphGetNodes(g, nullptr, &n));
+  std::vector<cudaGraphNode_t> nodes(n);
+  DIAL_CUDA(cudaGraphGetNodes(g, nodes.data(), &n));
+  int64_t k = 0;
+  for (size_t i = 0; i < n; ++i) {
+    cudaGraphNodeType t;
+    DIAL_CUDA(cudaGraphNodeGetType(nodes[i], &t));
+    if (t == cudaGraphNodeTypeKernel) ++k;
+  }
+  return k;
+}
+
+}  // namespace
+
 int64_t dial_b200_step_kernel_count(dial_b200_engine* eng, int64_t rows) {
   if (!eng || rows < 1) return -1;
   try {
-    if (step_kernel_usable(eng, static_cast<int>(rows))) return 1;
+    DIAL_CUDA(cudaSetDevice(eng->device));
+    require_full_model(eng);
+    DIAL_CHECK(rows <= eng->max_rows_decode && rows <= 256, "rows out of range");
+    return kernel_nodes(get_graph(eng, static_cast<int>(rows), true)->g);
   } catch (...) {
+    return -1;
   }
-  const int64_t groups = (rows + 7) / 8;
-  const int64_t per_layer = 4 * groups + 1;
-  return 1 + eng->cfg.num_layers * per_layer + groups + 1;
+}
+
+int64_t dial_b200_prefill_kernel_count(dial_b200_engine* eng, int64_t n_prompt) {
+  if (!eng || n_prompt < 1) return -1;
+  try {
+    DIAL_CUDA(cudaSetDevice(eng->device));
+    require_full_model(eng);
+    DIAL_CHECK(n_prompt <= eng->cfg.max_tokens && n_prompt <= eng->cfg.max_seq_len,
+               "prompt length out of range");
+    // capture (never launched) the device work of dial_b200_generate's
+    // prefill: embed, every layer at positions [0, n_prompt) of session 0, head
+    cudaStream_t s = eng->stream;
+    DIAL_CUDA(cudaStreamSynchronize(s));
+    Graph g;
+    DIAL_CUDA(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
+    try {
+      DIAL_CUDA(embed_launch(eng->embed.p, eng->tok_in.as<int32_t>(), static_cast<int>(n_prompt),
+                             eng->V, eng->H, eng->hidden.p, eng->H, eng->status, s, false));
+      for (int l = 0; l < eng->cfg.num_layers; ++l)
+        layer_prefill(eng, eng->layers[l], eng->hidden.p, static_cast<int>(n_prompt), 0, 0, s);
+      head_forward(eng, eng->hidden.p, 1, nullptr, eng->tok_out.as<int32_t>(), s);
+    } catch (...) {
+      cudaGraph_t tmp = nullptr;
+      cudaStreamEndCapture(s, &tmp);
+      if (tmp) cudaGraphDestroy(tmp);
+      throw;
+    }
+    DIAL_CUDA(cudaStreamEndCapture(s, &g.g));
+    return kernel_nodes(g.g);
+  } catch (...) {
+    return -1;
+  }
 }
 
 int dial_b200_engine_linear_replay(dial_b200_engine* eng, int layer, int which, int64_t rows,

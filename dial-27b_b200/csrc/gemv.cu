@@ -193,6 +193,14 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const GemvArgs a, con
   if constexpr (EPI == kEpiArgmax) {
     if (threadIdx.x < kMaxM) skey[threadIdx.x] = 0ull;
   }
+  if constexpr (NORM) {
+    // the RMSNorm weight is constant: bring it into L1 before the wait so
+    // that staging after it touches only the activations in L2
+    const char* nw = reinterpret_cast<const char*>(a.norm_w);
+    for (int off = threadIdx.x * 128; off < a.w.K * static_cast<int>(sizeof(Act));
+         off += kNW * 32 * 128)
+      asm volatile("prefetch.global.L1 [%0];" ::"l"(nw + off));
+  }
   pdl_wait();
   stage_x<Act, XT, NORM, kScaleX, kNW>(a, xs, p.xs_stride, xexp, scratch);
   named_bar_sync(1, kNW * 32);

@@ -112,6 +112,7 @@ _SIGS = {
     "dial_b200_engine_stream": (_vp, [_vp]),
     "dial_b200_session_fill_random": (C.c_int, [_vp, _i32, _i64, _u64, _vp, *_err]),
     "dial_b200_step_kernel_count": (_i64, [_vp, _i64]),
+    "dial_b200_prefill_kernel_count": (_i64, [_vp, _i64]),
     "dial_b200_engine_linear_replay": (C.c_int, [_vp, C.c_int, C.c_int, _i64, _i64, *_err]),
     "dial_b200_engine_linear_bytes": (_i64, [_vp, C.c_int, C.c_int, _i64]),
 }

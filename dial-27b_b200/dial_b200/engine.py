@@ -280,6 +280,9 @@ class Engine:
     def step_kernel_count(self, rows: int) -> int:
         return int(lib.dial_b200_step_kernel_count(self._h, rows))
 
+    def prefill_kernel_count(self, n_prompt: int) -> int:
+        return int(lib.dial_b200_prefill_kernel_count(self._h, n_prompt))
+
     def linear_replay(self, layer: int, which: int, rows: int, iters: int):
         call("dial_b200_engine_linear_replay", self._h, layer, which, rows, iters)
 

@@ -300,9 +300,15 @@ int dial_b200_session_fill_random(dial_b200_engine* eng, int32_t session, int64_
                                   uint64_t seed, const uint16_t* normal_table_bits, char* err,
                                   size_t err_size);
 
-/* Number of kernels one device-loop decode step launches for `rows` rows
- * (1 when the persistent step kernel runs the step). */
+/* Number of kernels one device-loop decode step launches for `rows` rows,
+ * counted as the kernel nodes of the captured step graph (1 when the
+ * persistent step kernel runs the step); -1 on error. */
 int64_t dial_b200_step_kernel_count(dial_b200_engine* eng, int64_t rows);
+
+/* Number of kernels dial_b200_generate launches for a prompt of `n_prompt`
+ * tokens up to the first token (embed, the prefill layers, the head), counted
+ * from a capture of that work that is never launched; -1 on error. */
+int64_t dial_b200_prefill_kernel_count(dial_b200_engine* eng, int64_t n_prompt);
 
 /* Measurement hook: launch one owned layer's linear (`which` as in
  * set_linear, with the epilogue the decode step uses) `iters` times back to

@@ -189,6 +189,26 @@ def test_decode_step_graph_matches_eager(cuda):
     assert toks == out.tolist()
 
 
+def test_kernel_counts_from_captured_graphs(cuda):
+    """The launch counts the bench reports are the kernel nodes of captured
+    work: decode = embed + 5 per layer (QKV, attention, o, gate/up, down) +
+    head + token advance at one row; counting a prefill launches nothing and
+    leaves generation unchanged."""
+    import dial_b200
+
+    cfg = small_cfg(layers=2, vocab=1024)
+    eng = engine_for(cfg, dial_b200, max_sessions=2)
+    eng.load_synthetic(seed=3)
+    prompt = list(range(3, 70))
+    out, _, _ = eng.generate(prompt, 4, session=0)
+    assert eng.step_kernel_count(1) == 1 + 5 * cfg.layers + 1 + 1
+    n_pf = eng.prefill_kernel_count(len(prompt))
+    assert n_pf >= 1 + 5 * cfg.layers + 1
+    out2, _, _ = eng.generate(prompt, 4, session=1)
+    assert out2.tolist() == out.tolist()
+    assert dial_b200.device_status() == 0
+
+
 def test_layer_forward_rejects_bad_requests(cuda):
     import dial_b200
 
