@@ -33,6 +33,17 @@ __global__ void __launch_bounds__(NREP * 32) attn_decode_kernel(const AttnDecode
                              threadIdx.x & 31, sm, 1);
 }
 
+// Cluster form: the CL splits of a (row, kv head) that share a cluster merge
+// their partials over distributed shared memory.
+template <typename Act, int NREP, int CL>
+__global__ void __launch_bounds__(NREP * 32) attn_decode_cluster_kernel(const AttnDecodeArgs a) {
+  pdl_launch_dependents();
+  __shared__ AttnItemSmem sm;
+  __shared__ AttnClusterSmem<NREP> cs;
+  attn_item<Act, NREP, true, CL>(a, blockIdx.z, blockIdx.x, blockIdx.y, threadIdx.x >> 5,
+                                 threadIdx.x & 31, sm, 1, &cs);
+}
+
 // Prefill KV append: token t of the session at position p0+t.  One warp per
 // (token, kv head) writes the normed+roped K and the raw V into the pages.
 template <typename Act>
@@ -70,8 +81,47 @@ __global__ void iota_pos_kernel(int32_t* pos, int32_t* sid, int M, int p0) {
   }
 }
 
+// Launch of the cluster form with CL splits per cluster; false when this
+// device cannot hold such a cluster (the caller then takes the plain form).
+template <typename Act, int NREP, int CL>
+bool launch_cluster(const AttnDecodeArgs& a, cudaStream_t s, bool pdl, cudaError_t& err) {
+  auto kern = attn_decode_cluster_kernel<Act, NREP, CL>;
+  static int usable = -1;  // per instantiation: checked once per process
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(a.sh.kv_heads, a.splits, a.M);
+  cfg.blockDim = dim3(NREP * 32);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = CL;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  cfg.attrs = attr;
+  if (usable < 0) {
+    usable = 0;
+    bool ok = CL <= 8 ||
+              cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) ==
+                  cudaSuccess;
+    int n = 0;
+    cfg.numAttrs = 1;
+    ok = ok && cudaOccupancyMaxActiveClusters(&n, kern, &cfg) == cudaSuccess;
+    if (!ok) cudaGetLastError();  // a refused size is an answer, not an error to keep
+    usable = ok && n >= 1 ? 1 : 0;
+  }
+  if (!usable) return false;
+  cfg.numAttrs = 2;
+  err = cudaLaunchKernelEx(&cfg, kern, a);
+  return true;
+}
+
 template <typename Act, int NREP>
 cudaError_t launch_decode_t(const AttnDecodeArgs& a, cudaStream_t s, bool pdl) {
+  // splits of a (row, kv head) merged inside a cluster when they tile it
+  cudaError_t err = cudaSuccess;
+  if (a.splits % 16 == 0 && launch_cluster<Act, NREP, 16>(a, s, pdl, err)) return err;
+  if (a.splits % 8 == 0 && launch_cluster<Act, NREP, 8>(a, s, pdl, err)) return err;
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(a.sh.kv_heads, a.splits, a.M);
   cfg.blockDim = dim3(NREP * 32);

@@ -109,14 +109,121 @@ struct AttnItemSmem {
   int last;
 };
 
+// Per-CTA partials of the cluster combine, read by the cluster's rank-0 CTA
+// through distributed shared memory (16-byte vector stores and loads).
+template <int NREP>
+struct __align__(16) AttnClusterSmem {
+  float o[NREP][kHeadDim];
+  float ml[NREP][2];
+};
+
+__device__ __forceinline__ uint32_t cluster_map(const void* p, int rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+  return r;
+}
+
+__device__ __forceinline__ float ld_dsmem_f32(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ float4 ld_dsmem_v4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(addr)
+               : "memory");
+  return v;
+}
+
+// Every thread of every CTA of the cluster (shared-memory writes before it
+// are visible to the cluster after it).
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
+                   : "memory");
+}
+
+// Combine of S_parts partial rows (m, l, acc) of (row m, kv head) through the
+// scratch buffer: partial idx is stored, the last arrival on the (row, kv
+// head) counter merges all of them, writes the output and resets the counter.
+template <typename Act, int NREP, typename Sync>
+__device__ void attn_global_combine(const AttnDecodeArgs& a, int m, int kvh, int h, int r,
+                                    int lane, AttnItemSmem& sm, Sync group_sync, int S_parts,
+                                    int idx, const float (&acc)[4], float mrun, float lrun,
+                                    Act* out) {
+  const int QH = a.sh.q_heads, KVH = a.sh.kv_heads;
+  // partial rows are laid out with the allocation stride a.splits
+  const size_t prow = (static_cast<size_t>(m) * QH + h) * a.splits;
+  __stcg(reinterpret_cast<float4*>(a.part_o + (prow + idx) * kHeadDim + lane * 4),
+         make_float4(acc[0], acc[1], acc[2], acc[3]));
+  if (lane == 0) {
+    __stcg(a.part_ml + (prow + idx) * 2, mrun);
+    __stcg(a.part_ml + (prow + idx) * 2 + 1, lrun);
+  }
+  group_sync();
+  if (r == 0 && lane == 0) {
+    __threadfence();
+    const int old = atomicAdd(a.counters + m * KVH + kvh, 1);
+    sm.last = (old == S_parts - 1);
+  }
+  group_sync();
+  const bool last = sm.last != 0;
+  if (last) {
+    __threadfence();
+    // lane s2 < S_parts holds partial s2's (m, l); weights are broadcast by shuffles
+    float ms_l = -INFINITY, ls_l = 0.f;
+    if (lane < S_parts) {
+      ms_l = __ldcg(a.part_ml + (prow + lane) * 2);
+      ls_l = __ldcg(a.part_ml + (prow + lane) * 2 + 1);
+    }
+    const float M = warp_max(ms_l);
+    const float w_l = (lane < S_parts && ms_l != -INFINITY) ? expf(ms_l - M) : 0.f;
+    const float L = warp_sum(w_l * ls_l);
+    float o[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int s0 = 0; s0 < S_parts; s0 += 8) {
+      float4 po[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        po[u] = (s0 + u < S_parts)
+                    ? __ldcg(reinterpret_cast<const float4*>(a.part_o + (prow + s0 + u) * kHeadDim + lane * 4))
+                    : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const float w = __shfl_sync(0xffffffffu, w_l, (s0 + u) & 31);
+        if (s0 + u < S_parts) {
+          o[0] = fmaf(w, po[u].x, o[0]);
+          o[1] = fmaf(w, po[u].y, o[1]);
+          o[2] = fmaf(w, po[u].z, o[2]);
+          o[3] = fmaf(w, po[u].w, o[3]);
+        }
+      }
+    }
+    const float inv = L > 0.f ? 1.f / L : 0.f;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) o[e] *= inv;
+    store4(out, o);
+  }
+  group_sync();
+  if (last && r == 0 && lane == 0) a.counters[m * KVH + kvh] = 0;
+}
+
 // Process item (m, kvh, split) of `a` with NREP warps; `r` = this warp's
 // index in the group, `bar_id` a named barrier owned by the group.  PDL: the
 // item executes griddepcontrol.wait itself, after the reads that a.rows_ready
 // allows before it (block ids, the span's first K/V page, norm weights and
 // RoPE rows); an item with nothing to do then exits without waiting.
-template <typename Act, int NREP, bool PDL = false>
+//
+// CL > 0: the CTAs of item splits [c*CL, (c+1)*CL) form one thread-block
+// cluster; each keeps its partial in `cs` and the cluster's rank-0 CTA merges
+// the active ones over distributed shared memory (one cluster covering all
+// active splits writes the output directly; otherwise the cluster partials
+// take the scratch-buffer combine).  Splits past the active count in an
+// active cluster only join the two cluster barriers.
+template <typename Act, int NREP, bool PDL = false, int CL = 0>
 __device__ void attn_item(const AttnDecodeArgs& a, int m, int kvh, int split, int r, int lane,
-                          AttnItemSmem& sm, int bar_id) {
+                          AttnItemSmem& sm, int bar_id, AttnClusterSmem<NREP>* csm = nullptr) {
   using AT = ActTraits<Act>;
   const int QH = a.sh.q_heads, KVH = a.sh.kv_heads;
   const int h = kvh * NREP + r;
@@ -136,10 +243,16 @@ __device__ void attn_item(const AttnDecodeArgs& a, int m, int kvh, int split, in
   // Splits actually used by this row: short contexts skip the partial/combine
   // round trip.  Uniform over the group, so every warp returns together.
   const int S = active_splits(ctx, a.splits, a.min_split_tokens);
-  if (split >= S) return;
+  bool active = true;
+  if constexpr (CL > 0) {
+    if (split / CL * CL >= S) return;  // the whole cluster is idle: uniform over it
+    active = split < S;
+  } else {
+    if (split >= S) return;
+  }
   const int span = ((ctx + S - 1) / S + kPageTokens - 1) / kPageTokens * kPageTokens;
   const int tok0 = split * span;
-  const int tok1 = min(ctx, tok0 + span);
+  const int tok1 = active ? min(ctx, tok0 + span) : tok0;
   const bool owner = tok0 <= pos && pos < tok1;
 
   const Act* qkv = reinterpret_cast<const Act*>(a.qkv) + static_cast<size_t>(m) * a.qkv_ld;
@@ -151,7 +264,7 @@ __device__ void attn_item(const AttnDecodeArgs& a, int m, int kvh, int split, in
 
   // Issue every load that does not depend on another one first: the block
   // id of the span's first page, q (and the new k/v), norm weights, cos/sin.
-  const int blk_first = bt[tok0 / kPageTokens];
+  const int blk_first = active ? bt[tok0 / kPageTokens] : 0;
   float q[4], kn[4] = {0.f, 0.f, 0.f, 0.f}, vn[4] = {0.f, 0.f, 0.f, 0.f};
   if (!early) {
     load4_cg(qkv + h * kHeadDim + lane * 4, q);
@@ -167,7 +280,7 @@ __device__ void attn_item(const AttnDecodeArgs& a, int m, int kvh, int split, in
   load4(sin_row + (lane & 15) * 4, sn);
   // first page's K/V (depends only on the block id)
   uint2 kr[kPageTokens], vr[kPageTokens];
-  {
+  if (active) {
     const size_t base =
         (static_cast<size_t>(blk_first) * KVH + kvh) * kPageTokens * kHeadDim + lane * 4;
 #pragma unroll
@@ -284,6 +397,49 @@ __device__ void attn_item(const AttnDecodeArgs& a, int m, int kvh, int split, in
 
   Act* out =
       reinterpret_cast<Act*>(a.out) + static_cast<size_t>(m) * a.out_ld + h * kHeadDim + lane * 4;
+  if constexpr (CL > 0) {
+    if (active) {
+      *reinterpret_cast<float4*>(&csm->o[r][lane * 4]) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+      if (lane == 0) {
+        csm->ml[r][0] = mrun;
+        csm->ml[r][1] = lrun;
+      }
+    }
+    cluster_sync_all();
+    if (split % CL == 0) {
+      // warp r merges query head h over the cluster's active splits
+      const int nact = min(S, split + CL) - split;
+      float ms_l = -INFINITY, ls_l = 0.f;
+      if (lane < nact) {
+        const uint32_t pm = cluster_map(&csm->ml[r][0], lane);
+        ms_l = ld_dsmem_f32(pm);
+        ls_l = ld_dsmem_f32(pm + 4);
+      }
+      const float Mx = warp_max(ms_l);
+      const float w_l = (lane < nact && ms_l != -INFINITY) ? expf(ms_l - Mx) : 0.f;
+      const float L = warp_sum(w_l * ls_l);
+      float o[4] = {0.f, 0.f, 0.f, 0.f};
+      for (int s2 = 0; s2 < nact; ++s2) {
+        const float w = __shfl_sync(0xffffffffu, w_l, s2);
+        const float4 po = ld_dsmem_v4(cluster_map(&csm->o[r][lane * 4], s2));
+        o[0] = fmaf(w, po.x, o[0]);
+        o[1] = fmaf(w, po.y, o[1]);
+        o[2] = fmaf(w, po.z, o[2]);
+        o[3] = fmaf(w, po.w, o[3]);
+      }
+      if (S <= CL) {
+        const float inv = L > 0.f ? 1.f / L : 0.f;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) o[e] *= inv;
+        store4(out, o);
+      } else {
+        attn_global_combine<Act, NREP>(a, m, kvh, h, r, lane, sm, group_sync, (S + CL - 1) / CL,
+                                       split / CL, o, Mx, L, out);
+      }
+    }
+    cluster_sync_all();  // peers keep their partials until rank 0 has read them
+    return;
+  }
   if (S == 1) {
     float o[4];
     const float inv = lrun > 0.f ? 1.f / lrun : 0.f;
@@ -294,59 +450,8 @@ __device__ void attn_item(const AttnDecodeArgs& a, int m, int kvh, int split, in
     return;
   }
 
-  // partial rows are laid out with the allocation stride a.splits
-  const size_t prow = (static_cast<size_t>(m) * QH + h) * a.splits;
-  __stcg(reinterpret_cast<float4*>(a.part_o + (prow + split) * kHeadDim + lane * 4),
-         make_float4(acc[0], acc[1], acc[2], acc[3]));
-  if (lane == 0) {
-    __stcg(a.part_ml + (prow + split) * 2, mrun);
-    __stcg(a.part_ml + (prow + split) * 2 + 1, lrun);
-  }
-  group_sync();
-  if (r == 0 && lane == 0) {
-    __threadfence();
-    const int old = atomicAdd(a.counters + m * KVH + kvh, 1);
-    sm.last = (old == S - 1);
-  }
-  group_sync();
-  const bool last = sm.last != 0;
-  if (last) {
-    __threadfence();
-    // lane s2 < S holds split s2's (m, l); weights are broadcast by shuffles
-    float ms_l = -INFINITY, ls_l = 0.f;
-    if (lane < S) {
-      ms_l = __ldcg(a.part_ml + (prow + lane) * 2);
-      ls_l = __ldcg(a.part_ml + (prow + lane) * 2 + 1);
-    }
-    const float M = warp_max(ms_l);
-    const float w_l = (lane < S && ms_l != -INFINITY) ? expf(ms_l - M) : 0.f;
-    const float L = warp_sum(w_l * ls_l);
-    float o[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int s0 = 0; s0 < S; s0 += 8) {
-      float4 po[8];
-#pragma unroll
-      for (int u = 0; u < 8; ++u)
-        po[u] = (s0 + u < S)
-                    ? __ldcg(reinterpret_cast<const float4*>(a.part_o + (prow + s0 + u) * kHeadDim + lane * 4))
-                    : make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const float w = __shfl_sync(0xffffffffu, w_l, (s0 + u) & 31);
-        if (s0 + u < S) {
-          o[0] = fmaf(w, po[u].x, o[0]);
-          o[1] = fmaf(w, po[u].y, o[1]);
-          o[2] = fmaf(w, po[u].z, o[2]);
-          o[3] = fmaf(w, po[u].w, o[3]);
-        }
-      }
-    }
-    const float inv = L > 0.f ? 1.f / L : 0.f;
-#pragma unroll
-    for (int e = 0; e < 4; ++e) o[e] *= inv;
-    store4(out, o);
-  }
-  group_sync();
-  if (last && r == 0 && lane == 0) a.counters[m * KVH + kvh] = 0;
+  attn_global_combine<Act, NREP>(a, m, kvh, h, r, lane, sm, group_sync, S, split, acc, mrun,
+                                 lrun, out);
 }
 
 }  // namespace dialb200

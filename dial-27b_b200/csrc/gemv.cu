@@ -7,10 +7,12 @@
 //   dial_nvfp4_decode_f16   dial-core/src/models/qwen3_8/cuda_quant.rs:67-100
 // plus the dense candle Linear used for the lm_head (qwen3_vl.rs:1325-1335).
 //
-// Design (one CTA per SM, 8 consumer warps + 1 producer warp):
+// Design (one CTA per SM, 16 consumer warps + 1 producer warp):
 //  * The producer streams the CTA's contiguous range of 16-row weight tiles
 //    through a shared-memory ring with 1-D bulk async copies (TMA engine),
-//    16 chunks (16-18 KB) per stage, completion tracked on mbarriers.  It
+//    32 chunks (32-36 KB) per stage, completion tracked on mbarriers; each
+//    consumer warp takes two chunks of a stage (16 warps keep enough
+//    independent dequant + MMA chains in flight to follow the copies).  It
 //    starts before griddepcontrol.wait, so weight streaming overlaps the tail
 //    of the previous kernel (programmatic dependent launch).
 //  * Activations are staged once per CTA in shared memory as f16 (with a
@@ -30,9 +32,9 @@
 namespace dialb200 {
 namespace {
 
-constexpr int kNW = 8;                      // consumer warps
+constexpr int kNW = 16;                     // consumer warps
 constexpr int kThreads = (kNW + 1) * 32;    // + producer warp
-constexpr int kStageChunks = 16;
+constexpr int kStageChunks = 32;                // two per consumer warp
 constexpr int kMaxSlots = 16;
 constexpr int kMaxM = 8;
 constexpr int kSmemBudget = 232448;         // 227 KB opt-in per CTA
@@ -150,6 +152,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const GemvArgs a, con
                           a.w.blk_scale + static_cast<size_t>(hi0) * a.w.blk_ld, row_bytes * nhi,
                           sbar);
       }
+      // weights are read once per pass: evict them first so that activations,
+      // norm weights and the KV cache stay in L2 between layers
+      const uint64_t pol = l2_evict_first_policy();
       long long it = 0;
       int slot = 0;         // ring position and fill round, advanced incrementally
       uint32_t round = 0;
@@ -165,8 +170,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const GemvArgs a, con
           const int nch = min(kStageChunks, C - s * kStageChunks);
           const uint32_t bytes = static_cast<uint32_t>(nch * CB);
           mbar_arrive_expect_tx(&full[slot], bytes);
-          bulk_g2s(ring + static_cast<size_t>(slot) * kStageBytes,
-                   src + static_cast<size_t>(s) * kStageChunks * CB, bytes, &full[slot]);
+          bulk_g2s_hint(ring + static_cast<size_t>(slot) * kStageBytes,
+                        src + static_cast<size_t>(s) * kStageChunks * CB, bytes, &full[slot], pol);
           if (++slot == NS) {
             slot = 0;
             ++round;
