@@ -109,6 +109,9 @@ struct AttnItemSmem {
   int last;
 };
 
+// Largest cluster: rank 0 issues all of its peers' loads at once.
+constexpr int kMaxClusterLoads = 16;
+
 // Per-CTA partials of the cluster combine, read by the cluster's rank-0 CTA
 // through distributed shared memory (16-byte vector stores and loads).
 template <int NREP>
@@ -265,6 +268,7 @@ __device__ void attn_item(const AttnDecodeArgs& a, int m, int kvh, int split, in
   // Issue every load that does not depend on another one first: the block
   // id of the span's first page, q (and the new k/v), norm weights, cos/sin.
   const int blk_first = active ? bt[tok0 / kPageTokens] : 0;
+  const int blk_pos = do_kv ? bt[pos / kPageTokens] : 0;
   float q[4], kn[4] = {0.f, 0.f, 0.f, 0.f}, vn[4] = {0.f, 0.f, 0.f, 0.f};
   if (!early) {
     load4_cg(qkv + h * kHeadDim + lane * 4, q);
@@ -308,12 +312,18 @@ __device__ void attn_item(const AttnDecodeArgs& a, int m, int kvh, int split, in
       sm.kn[lane * 4 + e] = kn[e];
       sm.vn[lane * 4 + e] = vn[e];
     }
-    const int blk = bt[pos / kPageTokens];
-    const size_t off = ((static_cast<size_t>(blk) * KVH + kvh) * kPageTokens + (pos % kPageTokens)) *
-                           kHeadDim + lane * 4;
-    store4(kpool + off, kn);
-    store4(vpool + off, vn);
   }
+  // The new token's K/V reach the pages last (no later read in this launch
+  // needs them): no fence or barrier release below waits for these stores.
+  auto append_kv = [&]() {
+    if (do_kv) {
+      const size_t off =
+          ((static_cast<size_t>(blk_pos) * KVH + kvh) * kPageTokens + (pos % kPageTokens)) *
+              kHeadDim + lane * 4;
+      store4(kpool + off, kn);
+      store4(vpool + off, vn);
+    }
+  };
   group_sync();
 
   const float scale = AT::round(1.0f / sqrtf(static_cast<float>(kHeadDim)));
@@ -406,7 +416,10 @@ __device__ void attn_item(const AttnDecodeArgs& a, int m, int kvh, int split, in
       }
     }
     cluster_sync_all();
-    if (split % CL == 0) {
+    const bool leader = split % CL == 0;
+    float o[4] = {0.f, 0.f, 0.f, 0.f};
+    float Mx = -INFINITY, L = 0.f;
+    if (leader) {
       // warp r merges query head h over the cluster's active splits
       const int nact = min(S, split + CL) - split;
       float ms_l = -INFINITY, ls_l = 0.f;
@@ -415,18 +428,27 @@ __device__ void attn_item(const AttnDecodeArgs& a, int m, int kvh, int split, in
         ms_l = ld_dsmem_f32(pm);
         ls_l = ld_dsmem_f32(pm + 4);
       }
-      const float Mx = warp_max(ms_l);
+      Mx = warp_max(ms_l);
       const float w_l = (lane < nact && ms_l != -INFINITY) ? expf(ms_l - Mx) : 0.f;
-      const float L = warp_sum(w_l * ls_l);
-      float o[4] = {0.f, 0.f, 0.f, 0.f};
-      for (int s2 = 0; s2 < nact; ++s2) {
-        const float w = __shfl_sync(0xffffffffu, w_l, s2);
-        const float4 po = ld_dsmem_v4(cluster_map(&csm->o[r][lane * 4], s2));
-        o[0] = fmaf(w, po.x, o[0]);
-        o[1] = fmaf(w, po.y, o[1]);
-        o[2] = fmaf(w, po.z, o[2]);
-        o[3] = fmaf(w, po.w, o[3]);
+      L = warp_sum(w_l * ls_l);
+      float4 po[kMaxClusterLoads];
+#pragma unroll
+      for (int u = 0; u < kMaxClusterLoads; ++u)
+        po[u] = u < nact ? ld_dsmem_v4(cluster_map(&csm->o[r][lane * 4], u))
+                         : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int u = 0; u < kMaxClusterLoads; ++u) {
+        const float w = __shfl_sync(0xffffffffu, w_l, u);
+        o[0] = fmaf(w, po[u].x, o[0]);
+        o[1] = fmaf(w, po[u].y, o[1]);
+        o[2] = fmaf(w, po[u].z, o[2]);
+        o[3] = fmaf(w, po[u].w, o[3]);
       }
+    }
+    // peers keep their partials until rank 0 has read them; the stores come
+    // after, so neither barrier waits on a global write
+    cluster_sync_all();
+    if (leader) {
       if (S <= CL) {
         const float inv = L > 0.f ? 1.f / L : 0.f;
 #pragma unroll
@@ -437,7 +459,7 @@ __device__ void attn_item(const AttnDecodeArgs& a, int m, int kvh, int split, in
                                        split / CL, o, Mx, L, out);
       }
     }
-    cluster_sync_all();  // peers keep their partials until rank 0 has read them
+    append_kv();
     return;
   }
   if (S == 1) {
@@ -446,12 +468,14 @@ __device__ void attn_item(const AttnDecodeArgs& a, int m, int kvh, int split, in
 #pragma unroll
     for (int e = 0; e < 4; ++e) o[e] = acc[e] * inv;
     store4(out, o);
+    append_kv();
     group_sync();  // kn/vn reuse by the group's next item
     return;
   }
 
   attn_global_combine<Act, NREP>(a, m, kvh, h, r, lane, sm, group_sync, S, split, acc, mrun,
                                  lrun, out);
+  append_kv();
 }
 
 }  // namespace dialb200
