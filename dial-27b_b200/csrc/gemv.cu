@@ -38,6 +38,7 @@ constexpr int kStageChunks = 32;                // two per consumer warp
 constexpr int kMaxSlots = 16;
 constexpr int kMaxM = 8;
 constexpr int kSmemBudget = 232448;         // 227 KB opt-in per CTA
+constexpr int kMiscFlag = 32, kMiscKeys = 64, kMiscScratch = 128;  // offsets in the misc area
 
 struct SmemPlan {
   int ring_off, x_off, red_off, misc_off, bsc_off, bar_off, total;
@@ -68,7 +69,9 @@ __host__ inline SmemPlan make_plan(const DevQLinear& w, int M, int grid, int slo
   p.xs_stride = w.K_pad + 8;
   const int x_bytes = ((M * p.xs_stride * 2) + 127) / 128 * 128;
   const int red_bytes = 2 * kNW * 32 * 4 * 4;
-  const int misc_bytes = 256;
+  // misc: xexp [kMaxM] ints | argmax flag | argmax keys [kMaxM] | staging
+  // scratch [2][kNW] floats (block reduction of the activation statistics)
+  const int misc_bytes = kMiscScratch + 2 * kNW * 4;
   int bsc_bytes = 0;
   if (w.fmt == kFmtFp8Block128) {
     // worst case over CTAs: tiles per CTA <= ceil(T/grid)
@@ -113,7 +116,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const GemvArgs a, con
   XT* xs = reinterpret_cast<XT*>(smem + p.x_off);
   float* red = reinterpret_cast<float*>(smem + p.red_off);
   int* xexp = reinterpret_cast<int*>(smem + p.misc_off);
-  float* scratch = reinterpret_cast<float*>(smem + p.misc_off + 64);
+  float* scratch = reinterpret_cast<float*>(smem + p.misc_off + kMiscScratch);
   float* bsc = reinterpret_cast<float*>(smem + p.bsc_off);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + p.bar_off);
   uint64_t* empty = full + kMaxSlots;
@@ -193,8 +196,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const GemvArgs a, con
   }
 
   // -------------------------------------------------------------- consumers
-  int* sflag = reinterpret_cast<int*>(smem + p.misc_off + 128);
-  unsigned long long* skey = reinterpret_cast<unsigned long long*>(smem + p.misc_off + 192);
+  int* sflag = reinterpret_cast<int*>(smem + p.misc_off + kMiscFlag);
+  unsigned long long* skey = reinterpret_cast<unsigned long long*>(smem + p.misc_off + kMiscKeys);
   if constexpr (EPI == kEpiArgmax) {
     if (threadIdx.x < kMaxM) skey[threadIdx.x] = 0ull;
   }
@@ -258,19 +261,23 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const GemvArgs a, con
       const uint8_t* st = ring + static_cast<size_t>(slot) * kStageBytes;
       if (ok) {
         if constexpr (FMT == kFmtFp8Block128) {
-          float tmp[4] = {0.f, 0.f, 0.f, 0.f};
+          // only a warp with a chunk in this stage reads a block scale: the
+          // others' column index is past the scales this CTA loaded
+          if (warp * 2 < nch) {
+            float tmp[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-          for (int j = 0; j < 2; ++j) {
-            const int ch = warp * 2 + j;
-            if (ch < nch) chunk_mma<FMT, XT>(st + ch * CB, s * kStageChunks + ch, xrow, lane, tmp);
+            for (int j = 0; j < 2; ++j) {
+              const int ch = warp * 2 + j;
+              if (ch < nch) chunk_mma<FMT, XT>(st + ch * CB, s * kStageChunks + ch, xrow, lane, tmp);
+            }
+            const int kb = (s * kStageChunks + warp * 2) / 2;
+            const float slo = bsc[rb_lo * a.w.blk_ld + kb];
+            const float shi = bsc[rb_hi * a.w.blk_ld + kb];
+            acc[0] = fmaf(tmp[0], slo, acc[0]);
+            acc[1] = fmaf(tmp[1], slo, acc[1]);
+            acc[2] = fmaf(tmp[2], shi, acc[2]);
+            acc[3] = fmaf(tmp[3], shi, acc[3]);
           }
-          const int kb = (s * kStageChunks + warp * 2) / 2;
-          const float slo = bsc[rb_lo * a.w.blk_ld + kb];
-          const float shi = bsc[rb_hi * a.w.blk_ld + kb];
-          acc[0] = fmaf(tmp[0], slo, acc[0]);
-          acc[1] = fmaf(tmp[1], slo, acc[1]);
-          acc[2] = fmaf(tmp[2], shi, acc[2]);
-          acc[3] = fmaf(tmp[3], shi, acc[3]);
         } else {
           const int ch0 = warp * 2, ch1 = warp * 2 + 1;
           if constexpr (FMT == kFmtW8A16Row || FMT == kFmtFp8Row) {
