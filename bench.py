@@ -38,7 +38,7 @@ PROMPT_LEN = 128
 WORKLOAD = "qwen3-8b-w8a16-bs1-decode"
 # DRAM bytes (read + write) of one launch of the W8A16 GEMV on the fused gate/up weight
 # (N=24576, K=4096, M=1), from an `ncu --set full` capture of the same kernel and weight shape
-# with the store epilogue (summary: profiles/gemv_w8a16_gate_up_m1.md).
+# with the store epilogue.
 GATE_UP_TRAFFIC_BYTES = 100_804_864 + 3_187_968
 GATE_UP_TRAFFIC_SOURCE = "ncu dram__bytes_read+write, gemv_kernel<bf16,W8A16,store> N=24576 K=4096 M=1"
 
