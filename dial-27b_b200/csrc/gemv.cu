@@ -32,9 +32,10 @@
 namespace dialb200 {
 namespace {
 
-constexpr int kNW = 16;                     // consumer warps
-constexpr int kThreads = (kNW + 1) * 32;    // + producer warp
-constexpr int kStageChunks = 32;                // two per consumer warp
+// Consumer warps per CTA (template NW): 16, with 32-chunk stages, while the
+// staged activation rows leave room for them; 8, with 16-chunk stages, when
+// more rows per launch fit that way (each launch re-streams the weights).
+// Every consumer warp takes two chunks of a stage.
 constexpr int kMaxSlots = 16;
 constexpr int kMaxM = 8;
 constexpr int kSmemBudget = 232448;         // 227 KB opt-in per CTA
@@ -63,15 +64,15 @@ __host__ __device__ inline void bsc_rows(const DevQLinear& w, int t0, int t1, in
   }
 }
 
-__host__ inline SmemPlan make_plan(const DevQLinear& w, int M, int grid, int slots_req) {
+__host__ inline SmemPlan make_plan(const DevQLinear& w, int M, int grid, int slots_req, int nw) {
   SmemPlan p{};
-  const int stage = kStageChunks * fmt_chunk_bytes(w.fmt);
+  const int stage = 2 * nw * fmt_chunk_bytes(w.fmt);
   p.xs_stride = w.K_pad + 8;
   const int x_bytes = ((M * p.xs_stride * 2) + 127) / 128 * 128;
-  const int red_bytes = 2 * kNW * 32 * 4 * 4;
+  const int red_bytes = 2 * nw * 32 * 4 * 4;
   // misc: xexp [kMaxM] ints | argmax flag | argmax keys [kMaxM] | staging
-  // scratch [2][kNW] floats (block reduction of the activation statistics)
-  const int misc_bytes = kMiscScratch + 2 * kNW * 4;
+  // scratch [2][nw] floats (block reduction of the activation statistics)
+  const int misc_bytes = kMiscScratch + 2 * nw * 4;
   int bsc_bytes = 0;
   if (w.fmt == kFmtFp8Block128) {
     // worst case over CTAs: tiles per CTA <= ceil(T/grid)
@@ -99,12 +100,31 @@ __host__ inline SmemPlan make_plan(const DevQLinear& w, int M, int grid, int slo
   return p;
 }
 
+// Consumer warps and rows per launch for M rows: rows per launch up to kMaxM,
+// fewer when the staged activations would leave the weight ring under 4
+// stages; 16 warps unless 8 warps need fewer launches.
+__host__ inline void gemv_shape(const DevQLinear& w, int M, int& nw, int& group) {
+  const int pgrid = std::max(1, std::min(w.T, 148));
+  auto rows = [&](int n) {
+    int g = kMaxM;
+    while (g > 1 && make_plan(w, g, pgrid, 0, n).slots < 4) g >>= 1;
+    return g;
+  };
+  const int g16 = rows(16), g8 = rows(8);
+  const int l16 = (M + g16 - 1) / g16, l8 = (M + g8 - 1) / g8;
+  nw = l16 <= l8 ? 16 : 8;
+  group = nw == 16 ? g16 : g8;
+}
+
 template <int FMT>
 struct XType { using T = __half; };
 
 // ------------------------------------------------------------------ kernel
-template <typename Act, int FMT, int EPI, bool NORM>
-__global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const GemvArgs a, const SmemPlan p) {
+template <typename Act, int FMT, int EPI, bool NORM, int NW>
+__global__ void __launch_bounds__((NW + 1) * 32, 1)
+    gemv_kernel(const GemvArgs a, const SmemPlan p) {
+  constexpr int kNW = NW;                   // consumer warps
+  constexpr int kStageChunks = 2 * NW;      // two per consumer warp
   using AT = ActTraits<Act>;
   using XT = typename std::conditional<FMT == kFmtDense, Act, __half>::type;
   constexpr bool kScaleX = (FMT != kFmtDense) && std::is_same<Act, __nv_bfloat16>::value;
@@ -383,7 +403,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const GemvArgs a, con
   }
 }
 
-template <typename Act, int FMT, int EPI, bool NORM>
+template <typename Act, int FMT, int EPI, bool NORM, int NW>
 cudaError_t launch_one(const GemvArgs& a, int slots_req, int grid_req, cudaStream_t stream,
                        bool pdl) {
   int dev = 0, sms = 0;
@@ -391,9 +411,9 @@ cudaError_t launch_one(const GemvArgs& a, int slots_req, int grid_req, cudaStrea
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   int grid = grid_req > 0 ? grid_req : sms;
   if (grid > a.w.T) grid = a.w.T;
-  const SmemPlan p = make_plan(a.w, a.M, grid, slots_req);
+  const SmemPlan p = make_plan(a.w, a.M, grid, slots_req, NW);
   if (p.slots < 2) return cudaErrorInvalidConfiguration;
-  auto kern = gemv_kernel<Act, FMT, EPI, NORM>;
+  auto kern = gemv_kernel<Act, FMT, EPI, NORM, NW>;
   cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          kSmemBudget);
   if (err != cudaSuccess) return err;
@@ -403,7 +423,7 @@ cudaError_t launch_one(const GemvArgs& a, int slots_req, int grid_req, cudaStrea
   if (err != cudaSuccess) return err;
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(grid);
-  cfg.blockDim = dim3(kThreads);
+  cfg.blockDim = dim3((NW + 1) * 32);
   cfg.dynamicSmemBytes = p.total;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
@@ -414,37 +434,43 @@ cudaError_t launch_one(const GemvArgs& a, int slots_req, int grid_req, cudaStrea
   return cudaLaunchKernelEx(&cfg, kern, a, p);
 }
 
+template <typename Act, int FMT, int EPI, bool NORM>
+cudaError_t launch_nw(const GemvArgs& a, int nw, int slots, int grid, cudaStream_t s, bool pdl) {
+  return nw == 16 ? launch_one<Act, FMT, EPI, NORM, 16>(a, slots, grid, s, pdl)
+                  : launch_one<Act, FMT, EPI, NORM, 8>(a, slots, grid, s, pdl);
+}
+
 template <typename Act, int FMT>
-cudaError_t dispatch_epi(const GemvArgs& a, int epi, bool norm, int slots, int grid,
+cudaError_t dispatch_epi(const GemvArgs& a, int epi, bool norm, int nw, int slots, int grid,
                          cudaStream_t s, bool pdl) {
   if (epi == kEpiArgmax) {
     if constexpr (FMT == kFmtDense || FMT == kFmtW8A16Row)
-      return norm ? launch_one<Act, FMT, kEpiArgmax, true>(a, slots, grid, s, pdl)
-                  : launch_one<Act, FMT, kEpiArgmax, false>(a, slots, grid, s, pdl);
+      return norm ? launch_nw<Act, FMT, kEpiArgmax, true>(a, nw, slots, grid, s, pdl)
+                  : launch_nw<Act, FMT, kEpiArgmax, false>(a, nw, slots, grid, s, pdl);
     return cudaErrorInvalidValue;
   }
   if (epi == kEpiStore)
-    return norm ? launch_one<Act, FMT, kEpiStore, true>(a, slots, grid, s, pdl)
-                : launch_one<Act, FMT, kEpiStore, false>(a, slots, grid, s, pdl);
+    return norm ? launch_nw<Act, FMT, kEpiStore, true>(a, nw, slots, grid, s, pdl)
+                : launch_nw<Act, FMT, kEpiStore, false>(a, nw, slots, grid, s, pdl);
   if (epi == kEpiResidual)
-    return norm ? launch_one<Act, FMT, kEpiResidual, true>(a, slots, grid, s, pdl)
-                : launch_one<Act, FMT, kEpiResidual, false>(a, slots, grid, s, pdl);
+    return norm ? launch_nw<Act, FMT, kEpiResidual, true>(a, nw, slots, grid, s, pdl)
+                : launch_nw<Act, FMT, kEpiResidual, false>(a, nw, slots, grid, s, pdl);
   if (epi == kEpiSwiglu)
-    return norm ? launch_one<Act, FMT, kEpiSwiglu, true>(a, slots, grid, s, pdl)
-                : launch_one<Act, FMT, kEpiSwiglu, false>(a, slots, grid, s, pdl);
+    return norm ? launch_nw<Act, FMT, kEpiSwiglu, true>(a, nw, slots, grid, s, pdl)
+                : launch_nw<Act, FMT, kEpiSwiglu, false>(a, nw, slots, grid, s, pdl);
   return cudaErrorInvalidValue;
 }
 
 template <typename Act>
-cudaError_t dispatch_fmt(const GemvArgs& a, int epi, bool norm, int slots, int grid,
+cudaError_t dispatch_fmt(const GemvArgs& a, int epi, bool norm, int nw, int slots, int grid,
                          cudaStream_t s, bool pdl) {
   switch (a.w.fmt) {
-    case kFmtW8A16Row: return dispatch_epi<Act, kFmtW8A16Row>(a, epi, norm, slots, grid, s, pdl);
+    case kFmtW8A16Row: return dispatch_epi<Act, kFmtW8A16Row>(a, epi, norm, nw, slots, grid, s, pdl);
     case kFmtFp8Block128:
-      return dispatch_epi<Act, kFmtFp8Block128>(a, epi, norm, slots, grid, s, pdl);
-    case kFmtFp8Row: return dispatch_epi<Act, kFmtFp8Row>(a, epi, norm, slots, grid, s, pdl);
-    case kFmtNvfp4G16: return dispatch_epi<Act, kFmtNvfp4G16>(a, epi, norm, slots, grid, s, pdl);
-    case kFmtDense: return dispatch_epi<Act, kFmtDense>(a, epi, norm, slots, grid, s, pdl);
+      return dispatch_epi<Act, kFmtFp8Block128>(a, epi, norm, nw, slots, grid, s, pdl);
+    case kFmtFp8Row: return dispatch_epi<Act, kFmtFp8Row>(a, epi, norm, nw, slots, grid, s, pdl);
+    case kFmtNvfp4G16: return dispatch_epi<Act, kFmtNvfp4G16>(a, epi, norm, nw, slots, grid, s, pdl);
+    case kFmtDense: return dispatch_epi<Act, kFmtDense>(a, epi, norm, nw, slots, grid, s, pdl);
     default: return cudaErrorInvalidValue;
   }
 }
@@ -457,12 +483,10 @@ cudaError_t gemv_launch(const GemvArgs& args, int act, int epi, bool norm, cudaS
   if (epi == kEpiSwiglu && !args.w.swiglu) return cudaErrorInvalidValue;
   GemvArgs a = args;
   const size_t esz = 2;
-  // Rows per launch: up to kMaxM, fewer when the staged activations would
-  // leave the weight ring under 4 stages.  Each group re-streams W.
+  int nw = 16, group = 1;
+  gemv_shape(args.w, args.M, nw, group);
   const int pgrid = std::max(1, std::min(args.w.T, 148));
-  int group = kMaxM;
-  while (group > 1 && make_plan(args.w, group, pgrid, 0).slots < 4) group >>= 1;
-  if (make_plan(args.w, group, pgrid, 0).slots < 2) return cudaErrorInvalidConfiguration;
+  if (make_plan(args.w, group, pgrid, 0, nw).slots < 2) return cudaErrorInvalidConfiguration;
   for (int r0 = 0; r0 < args.M; r0 += group) {
     a.M = std::min(group, args.M - r0);
     a.x = static_cast<const char*>(args.x) + static_cast<size_t>(r0) * args.x_ld * esz;
@@ -474,17 +498,19 @@ cudaError_t gemv_launch(const GemvArgs& args, int act, int epi, bool norm, cudaS
       a.amax_count = args.amax_count + r0;
       a.amax_tok = args.amax_tok + r0;
     }
-    cudaError_t e = act == 0 ? dispatch_fmt<__nv_bfloat16>(a, epi, norm, tune.slots, tune.grid,
-                                                           stream, tune.pdl)
-                             : dispatch_fmt<__half>(a, epi, norm, tune.slots, tune.grid, stream,
-                                                    tune.pdl);
+    cudaError_t e = act == 0 ? dispatch_fmt<__nv_bfloat16>(a, epi, norm, nw, tune.slots,
+                                                           tune.grid, stream, tune.pdl)
+                             : dispatch_fmt<__half>(a, epi, norm, nw, tune.slots, tune.grid,
+                                                    stream, tune.pdl);
     if (e != cudaSuccess) return e;
   }
   return cudaSuccess;
 }
 
 int gemv_smem_bytes(const DevQLinear& w, int M, int grid, int slots) {
-  return make_plan(w, std::min(M, kMaxM), grid, slots).total;
+  int nw = 16, group = 1;
+  gemv_shape(w, M, nw, group);
+  return make_plan(w, std::min(M, group), grid, slots, nw).total;
 }
 
 }  // namespace dialb200
