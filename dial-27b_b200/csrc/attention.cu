@@ -44,6 +44,36 @@ __global__ void __launch_bounds__(NREP * 32) attn_decode_cluster_kernel(const At
                                  threadIdx.x & 31, sm, 1, &cs);
 }
 
+// Ring form (optionally clustered, CL > 0): NREP query warps + one producer
+// warp that streams each split's K/V pages through a shared-memory ring.
+constexpr int kRingPages = 4;
+constexpr int kRingBytes = kRingPages * 2 * kPageBytes;
+
+template <typename Act, int NREP, int CL>
+__global__ void __launch_bounds__((NREP + 1) * 32) attn_decode_ring_kernel(const AttnDecodeArgs a) {
+  pdl_launch_dependents();
+  __shared__ AttnItemSmem sm;
+  __shared__ AttnClusterSmem<NREP> cs;  // partials of the cluster merge (CL > 0)
+  __shared__ uint64_t bars[2 * kRingPages];
+  extern __shared__ __align__(128) uint8_t ring[];  // kRingBytes
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kRingPages; ++i) {
+      mbar_init(&bars[i], 1);                   // full: the producer's expect_tx
+      mbar_init(&bars[kRingPages + i], NREP);   // empty: one arrival per query warp
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (warp == NREP) {
+    attn_ring_producer<CL, kRingPages>(a, blockIdx.z, blockIdx.x, blockIdx.y, lane, ring, bars,
+                                       bars + kRingPages);
+    return;
+  }
+  attn_item<Act, NREP, true, CL, kRingPages>(a, blockIdx.z, blockIdx.x, blockIdx.y, warp, lane, sm,
+                                             1, &cs, ring, bars, bars + kRingPages);
+}
+
 // Prefill KV append: token t of the session at position p0+t.  One warp per
 // (token, kv head) writes the normed+roped K and the raw V into the pages.
 template <typename Act>
@@ -83,13 +113,14 @@ __global__ void iota_pos_kernel(int32_t* pos, int32_t* sid, int M, int p0) {
 
 // Launch of the cluster form with CL splits per cluster; false when this
 // device cannot hold such a cluster (the caller then takes the plain form).
-template <typename Act, int NREP, int CL>
+template <typename Act, int NREP, int CL, bool RING>
 bool launch_cluster(const AttnDecodeArgs& a, cudaStream_t s, bool pdl, cudaError_t& err) {
-  auto kern = attn_decode_cluster_kernel<Act, NREP, CL>;
+  auto kern = RING ? attn_decode_ring_kernel<Act, NREP, CL> : attn_decode_cluster_kernel<Act, NREP, CL>;
   static int usable = -1;  // per instantiation: checked once per process
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(a.sh.kv_heads, a.splits, a.M);
-  cfg.blockDim = dim3(NREP * 32);
+  cfg.blockDim = dim3((NREP + (RING ? 1 : 0)) * 32);
+  cfg.dynamicSmemBytes = RING ? kRingBytes : 0;
   cfg.stream = s;
   cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -120,18 +151,25 @@ template <typename Act, int NREP>
 cudaError_t launch_decode_t(const AttnDecodeArgs& a, cudaStream_t s, bool pdl) {
   // splits of a (row, kv head) merged inside a cluster when they tile it
   cudaError_t err = cudaSuccess;
-  if (a.splits % 16 == 0 && launch_cluster<Act, NREP, 16>(a, s, pdl, err)) return err;
-  if (a.splits % 8 == 0 && launch_cluster<Act, NREP, 8>(a, s, pdl, err)) return err;
+  if (a.page_ring) {
+    if (a.splits % 16 == 0 && launch_cluster<Act, NREP, 16, true>(a, s, pdl, err)) return err;
+    if (a.splits % 8 == 0 && launch_cluster<Act, NREP, 8, true>(a, s, pdl, err)) return err;
+  } else {
+    if (a.splits % 16 == 0 && launch_cluster<Act, NREP, 16, false>(a, s, pdl, err)) return err;
+    if (a.splits % 8 == 0 && launch_cluster<Act, NREP, 8, false>(a, s, pdl, err)) return err;
+  }
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(a.sh.kv_heads, a.splits, a.M);
-  cfg.blockDim = dim3(NREP * 32);
+  cfg.blockDim = dim3((NREP + (a.page_ring ? 1 : 0)) * 32);
+  cfg.dynamicSmemBytes = a.page_ring ? kRingBytes : 0;
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, attn_decode_kernel<Act, NREP>, a);
+  return a.page_ring ? cudaLaunchKernelEx(&cfg, attn_decode_ring_kernel<Act, NREP, 0>, a)
+                     : cudaLaunchKernelEx(&cfg, attn_decode_kernel<Act, NREP>, a);
 }
 
 template <typename Act>

@@ -50,6 +50,9 @@ struct AttnDecodeArgs {
   // predecessor writes), so the kernel reads them before griddepcontrol.wait
   // and waits only for q / k / v.  0: everything is read after the wait.
   int rows_ready;
+  // 1: a producer warp streams each split's K/V pages through a shared-memory
+  // ring (bulk copies); 0: every query warp loads its pages into registers.
+  int page_ring;
 };
 
 // Scratch bytes needed for (M, splits).

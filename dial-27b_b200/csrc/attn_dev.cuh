@@ -148,6 +148,78 @@ __device__ __forceinline__ void cluster_sync_all() {
                    : "memory");
 }
 
+// Bytes of one page of one kv head (K or V): 16 tokens x 128 dims x 2 B.
+constexpr int kPageBytes = kPageTokens * kHeadDim * 2;
+
+// Producer warp of the ring form of attn_item: lane 0 streams the span's K
+// and V pages of (row m, kv head, split) into the ring with bulk copies and
+// waits (bounded) for them all to land; the warp then joins the cluster
+// barriers of the query warps.  With a.rows_ready it reads the session,
+// position and block table and issues the copies before griddepcontrol.wait
+// (the page holding the new position is read stale; its new row is taken
+// from q/k/v by the query warps).  Geometry as in attn_item.
+template <int CL, int RING>
+__device__ void attn_ring_producer(const AttnDecodeArgs& a, int m, int kvh, int split, int lane,
+                                   uint8_t* ring, uint64_t* rfull, uint64_t* rempty) {
+  if (a.rows_ready == 0) pdl_wait();
+  const int sid = a.sid[m];
+  int pos = a.pos[m];
+  if (pos < 0 || pos >= a.sh.max_pos || pos / kPageTokens >= a.sh.max_blocks) pos = 0;
+  const int ctx = pos + 1;
+  const int S = active_splits(ctx, a.splits, a.min_split_tokens);
+  bool active = true;
+  if constexpr (CL > 0) {
+    if (split / CL * CL >= S) return;
+    active = split < S;
+  } else {
+    if (split >= S) return;
+  }
+  const int span = ((ctx + S - 1) / S + kPageTokens - 1) / kPageTokens * kPageTokens;
+  const int tok0 = split * span;
+  const int tok1 = active ? min(ctx, tok0 + span) : tok0;
+  if (tok1 > tok0) {
+    const int KVH = a.sh.kv_heads;
+    const int32_t* bt = a.block_table + static_cast<size_t>(sid) * a.sh.max_blocks;
+    const uint8_t* kpool = static_cast<const uint8_t*>(a.kv.k);
+    const uint8_t* vpool = static_cast<const uint8_t*>(a.kv.v);
+    const int pg_first = tok0 / kPageTokens;
+    const int npages = (tok1 - tok0 + kPageTokens - 1) / kPageTokens;
+    // the warp loads the block ids 32 at a time; lane 0 issues the copies
+    int issued = 0, bt_lane = 0;
+    bool ok = true;
+    for (int pg = 0; pg < npages && ok; ++pg) {
+      if ((pg & 31) == 0) bt_lane = pg + lane < npages ? bt[pg_first + pg + lane] : 0;
+      const int blk = __shfl_sync(0xffffffffu, bt_lane, pg & 31);
+      if (lane == 0) {
+        const int slot = pg % RING;
+        if (pg >= RING && !mbar_wait(&rempty[slot], static_cast<uint32_t>(pg / RING - 1) & 1u,
+                                     a.status, kStatusAttnRing)) {
+          ok = false;
+        } else {
+          const size_t off = (static_cast<size_t>(blk) * KVH + kvh) * kPageBytes;
+          mbar_arrive_expect_tx(&rfull[slot], 2 * kPageBytes);
+          bulk_g2s(ring + slot * (2 * kPageBytes), kpool + off, kPageBytes, &rfull[slot]);
+          bulk_g2s(ring + slot * (2 * kPageBytes) + kPageBytes, vpool + off, kPageBytes,
+                   &rfull[slot]);
+          ++issued;
+        }
+      }
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+    }
+    // copies in flight must land before the CTA retires
+    if (lane == 0)
+      for (int pg = issued > RING ? issued - RING : 0; pg < issued; ++pg)
+        if (!mbar_wait(&rfull[pg % RING], static_cast<uint32_t>(pg / RING) & 1u, a.status,
+                       kStatusAttnRing))
+          break;
+  }
+  __syncwarp();
+  if constexpr (CL > 0) {
+    cluster_sync_all();  // the query warps' partial exchange
+    cluster_sync_all();
+  }
+}
+
 // Combine of S_parts partial rows (m, l, acc) of (row m, kv head) through the
 // scratch buffer: partial idx is stored, the last arrival on the (row, kv
 // head) counter merges all of them, writes the output and resets the counter.
@@ -224,9 +296,16 @@ __device__ void attn_global_combine(const AttnDecodeArgs& a, int m, int kvh, int
 // active splits writes the output directly; otherwise the cluster partials
 // take the scratch-buffer combine).  Splits past the active count in an
 // active cluster only join the two cluster barriers.
-template <typename Act, int NREP, bool PDL = false, int CL = 0>
+//
+// RING > 0: the span's pages come from a shared-memory ring of RING pages
+// (K page then V page, 4 KB each; full[] / empty[] mbarriers) that the
+// CTA's producer warp fills (attn_ring_producer); the query warps read each
+// page from shared memory and release its slot.
+template <typename Act, int NREP, bool PDL = false, int CL = 0, int RING = 0>
 __device__ void attn_item(const AttnDecodeArgs& a, int m, int kvh, int split, int r, int lane,
-                          AttnItemSmem& sm, int bar_id, AttnClusterSmem<NREP>* csm = nullptr) {
+                          AttnItemSmem& sm, int bar_id, AttnClusterSmem<NREP>* csm = nullptr,
+                          const uint8_t* ring = nullptr, uint64_t* rfull = nullptr,
+                          uint64_t* rempty = nullptr) {
   using AT = ActTraits<Act>;
   const int QH = a.sh.q_heads, KVH = a.sh.kv_heads;
   const int h = kvh * NREP + r;
@@ -267,7 +346,12 @@ __device__ void attn_item(const AttnDecodeArgs& a, int m, int kvh, int split, in
 
   // Issue every load that does not depend on another one first: the block
   // id of the span's first page, q (and the new k/v), norm weights, cos/sin.
-  const int blk_first = active ? bt[tok0 / kPageTokens] : 0;
+  const int blk_first = (RING == 0 && active) ? bt[tok0 / kPageTokens] : 0;
+  // the other block ids of the span's first 32 pages (register form)
+  const int bt_lane0 =
+      (RING == 0 && active && lane < (tok1 - tok0 + kPageTokens - 1) / kPageTokens)
+          ? bt[tok0 / kPageTokens + lane]
+          : 0;
   const int blk_pos = do_kv ? bt[pos / kPageTokens] : 0;
   float q[4], kn[4] = {0.f, 0.f, 0.f, 0.f}, vn[4] = {0.f, 0.f, 0.f, 0.f};
   if (!early) {
@@ -284,7 +368,7 @@ __device__ void attn_item(const AttnDecodeArgs& a, int m, int kvh, int split, in
   load4(sin_row + (lane & 15) * 4, sn);
   // first page's K/V (depends only on the block id)
   uint2 kr[kPageTokens], vr[kPageTokens];
-  if (active) {
+  if (RING == 0 && active) {
     const size_t base =
         (static_cast<size_t>(blk_first) * KVH + kvh) * kPageTokens * kHeadDim + lane * 4;
 #pragma unroll
@@ -331,9 +415,28 @@ __device__ void attn_item(const AttnDecodeArgs& a, int m, int kvh, int split, in
   const int my_tok = ((lane >> 4) & 1) * 8 + ((lane >> 3) & 1) * 4 + ((lane >> 2) & 1) * 2 +
                      ((lane >> 1) & 1);
 
-  for (int b0 = tok0; b0 < tok1; b0 += kPageTokens) {
-    if (b0 != tok0) {
-      const int blk = bt[b0 / kPageTokens];
+  // block ids of the span's pages, 32 at a time: lane l holds page (32i + l)
+  const int pg_first = tok0 / kPageTokens;
+  const int npg = (tok1 - tok0 + kPageTokens - 1) / kPageTokens;
+  int bt_lane = bt_lane0;
+  for (int b0 = tok0, pg = 0; b0 < tok1; b0 += kPageTokens, ++pg) {
+    if (RING == 0 && (pg & 31) == 0 && pg > 0)
+      bt_lane = pg + lane < npg ? bt[pg_first + pg + lane] : 0;
+    if constexpr (RING > 0) {
+      // the page's K/V rows (lane: dims 4*lane.. of every token) from the ring
+      const int slot = pg % RING;
+      mbar_wait(&rfull[slot], static_cast<uint32_t>(pg / RING) & 1u, a.status, kStatusAttnRing);
+      const uint8_t* kp = ring + slot * (2 * kPageBytes);
+      const uint8_t* vp = kp + kPageBytes;
+#pragma unroll
+      for (int j = 0; j < kPageTokens; ++j) {
+        kr[j] = *reinterpret_cast<const uint2*>(kp + j * kHeadDim * 2 + lane * 8);
+        vr[j] = *reinterpret_cast<const uint2*>(vp + j * kHeadDim * 2 + lane * 8);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&rempty[slot]);
+    } else if (b0 != tok0) {
+      const int blk = __shfl_sync(0xffffffffu, bt_lane, pg & 31);
       const size_t base = (static_cast<size_t>(blk) * KVH + kvh) * kPageTokens * kHeadDim + lane * 4;
 #pragma unroll
       for (int j = 0; j < kPageTokens; ++j) {

@@ -25,6 +25,7 @@ enum DevStatus : int {
   kStatusDrainTimeout = 0x103,      // in-flight copies did not land during error drain
   kStatusBadArgs = 0x104,
   kStatusAttnCounter = 0x201,
+  kStatusAttnRing = 0x202,          // decode-attention page ring wait timed out
 };
 
 // Wall-clock bound (ns) on any spin-wait; well above any legitimate wait.

@@ -300,6 +300,7 @@ GemvTuning g_tuning() {
   if (const char* v = std::getenv("DIAL_B200_GEMM_MIN_ROWS")) t.gemm_min_rows = std::atoi(v);
   if (const char* v = std::getenv("DIAL_B200_ATTN_MIN_SPLIT")) t.attn_min_split = std::atoi(v);
   if (const char* v = std::getenv("DIAL_B200_ATTN_TC")) t.attn_tc = std::atoi(v) != 0;
+  if (const char* v = std::getenv("DIAL_B200_ATTN_RING")) t.attn_ring = std::atoi(v) != 0;
   return t;
 }
 
@@ -672,6 +673,9 @@ AttnDecodeArgs decode_attn_args(dial_b200_engine* e, LayerW& L, int M) {
   // every caller of layer_decode starts from completed sessions, positions
   // and KV: a graph launch (root node), or an eager call after a host sync
   a.rows_ready = 1;
+  // the page ring pays at one or few rows (long contexts); with many rows
+  // the register form packs more CTAs per SM
+  a.page_ring = g_tuning().attn_ring && M <= 4 ? 1 : 0;
   return a;
 }
 
@@ -1158,6 +1162,7 @@ int dial_b200_attention_decode(const dial_b200_attn_shape* sh, const void* qkv, 
       a.counters = reinterpret_cast<int*>(a.part_ml + prow * 2);
     }
     a.status = device_status_word();
+    a.page_ring = 1;
     DIAL_CUDA(attn_decode_launch(a, sh->act, static_cast<cudaStream_t>(stream), false));
   });
 }

@@ -38,9 +38,10 @@ struct GemvTuning {
   int grid = 0;    // CTAs (0 = one per SM)
   bool pdl = true; // programmatic dependent launch
   bool step_kernel = false;  // whole decode step as one persistent kernel when supported
-  int gemm_min_rows = 64;    // rows from which W8A16 linears take the tcgen05 GEMM (0 = never)
+  int gemm_min_rows = 16;    // rows from which linears take the tcgen05 GEMM (0 = never)
   int attn_min_split = 0;    // decode attention: context tokens per split at least (0 = 16)
   bool attn_tc = true;       // prefill attention on the tensor cores when supported
+  bool attn_ring = true;     // decode attention pages through a shared-memory ring
 };
 
 // act: 0 = bf16, 1 = f16.  Launches ceil(M/8) kernels on `stream`.

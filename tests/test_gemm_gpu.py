@@ -1,4 +1,4 @@
-"""Prefill W8A16 linear on the tensor cores (tcgen05 GEMM, M >= 64 rows)
+"""Prefill W8A16 linear on the tensor cores (tcgen05 GEMM, M >= 16 rows)
 against the oracle's dequant + matmul (worker_w8a16.rs:186-224 semantics:
 y = act(s[n] * sum_k q[n, k] x[m, k])) and against the decode GEMV path."""
 
