@@ -200,6 +200,7 @@ def run_single(args) -> dict:
     eng.load_synthetic(seed=0)
     sys.path.insert(0, str(ROOT / "oracle"))
     prompt = _prompt_tokens(cfg.vocab_size)
+    eng.generate(prompt, 1)  # first call: lazy kernel loading, tensor-map set-up
     first, ttft, _ = eng.generate(prompt, 1)
     stream = eng.stream
     pos = PROMPT_LEN

@@ -33,6 +33,7 @@ namespace dialb200 {
 namespace {
 
 constexpr int kThreads = 384;
+constexpr int kEpiPartial = 8;  // split-K: scaled f32 partial sums into GemmArgs::part
 constexpr int kStatusGemmWait = 0x401;
 
 // Tile configurations: 256 weight rows (two M=128 MMAs sharing the activation
@@ -227,7 +228,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int tok0 = blockIdx.x * BN;
   const int blk = blockIdx.y;  // 256-row block = tiles [16 blk, 16 blk + 16)
-  const int C = a.w.C;         // k-steps (BK = one chunk)
+  // k-steps (BK = one chunk) of this split: [KB0, KB0 + NK) of the row's C
+  const int KB0 = static_cast<int>(static_cast<long long>(a.w.C) * blockIdx.z / gridDim.z);
+  const int NK =
+      static_cast<int>(static_cast<long long>(a.w.C) * (blockIdx.z + 1) / gridDim.z) - KB0;
+  const int C = a.w.C;
 
   if (tid == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -259,11 +264,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
-      int kb = 0;
-      for (; kb < C; ++kb) {
-        const int s = kb % STAGES;
-        if (kb >= STAGES &&
-            !mbar_wait(&lfree[s], static_cast<uint32_t>(kb / STAGES - 1) & 1u, a.status,
+      int it = 0;
+      for (; it < NK; ++it) {
+        const int kb = KB0 + it, s = it % STAGES;
+        if (it >= STAGES &&
+            !mbar_wait(&lfree[s], static_cast<uint32_t>(it / STAGES - 1) & 1u, a.status,
                        kStatusGemmWait))
           break;
         mbar_arrive_expect_tx(&full[s], B_BYTES + RAW_BYTES);
@@ -279,7 +284,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       // every copy issued must land before the CTA retires
-      for (int j = kb > STAGES ? kb - STAGES : 0; j < kb; ++j)
+      for (int j = it > STAGES ? it - STAGES : 0; j < it; ++j)
         if (!mbar_wait(&full[j % STAGES], static_cast<uint32_t>(j / STAGES) & 1u, a.status,
                        kStatusGemmWait))
           break;
@@ -287,12 +292,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA
     if (lane == 0) {
-      for (int kb = 0; kb < C; ++kb) {
-        const int s = kb % STAGES, sa_i = kb % ASTAGES;
-        if (!mbar_wait(&aready[sa_i], static_cast<uint32_t>(kb / ASTAGES) & 1u, a.status,
+      for (int it = 0; it < NK; ++it) {
+        const int s = it % STAGES, sa_i = it % ASTAGES;
+        if (!mbar_wait(&aready[sa_i], static_cast<uint32_t>(it / ASTAGES) & 1u, a.status,
                        kStatusGemmWait))
           break;
-        if (!mbar_wait(&full[s], static_cast<uint32_t>(kb / STAGES) & 1u, a.status,
+        if (!mbar_wait(&full[s], static_cast<uint32_t>(it / STAGES) & 1u, a.status,
                        kStatusGemmWait))
           break;
         tc_fence_after();
@@ -300,7 +305,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t sb = smem_u32(smem + OFF_B + s * B_BYTES);
 #pragma unroll
         for (int k16 = 0; k16 < BK / 16; ++k16) {
-          const uint32_t acc = (kb | k16) != 0 ? 1u : 0u;
+          const uint32_t acc = (it | k16) != 0 ? 1u : 0u;
           const uint32_t ka = (k16 >> 2) * 16384 + (k16 & 3) * 32;  // atom, 16-col step
           const uint64_t db = sw128_desc(sb + (k16 >> 2) * B_ATOM + (k16 & 3) * 32);
           tc_mma(tmem, sw128_desc(sa + ka), db, G::kIdesc, acc);  // rows 0..127
@@ -324,9 +329,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int dt = tid - 128;
       const int r = dt >> 1, part = dt & 1;
       const int c = r >> 4, rr = r & 15;
-      for (int kb = 0; kb < C; ++kb) {
-        const int s = kb % STAGES, sa_i = kb % ASTAGES;
-        if (!mbar_wait(&full[s], static_cast<uint32_t>(kb / STAGES) & 1u, a.status,
+      for (int it = 0; it < NK; ++it) {
+        const int s = it % STAGES, sa_i = it % ASTAGES;
+        if (!mbar_wait(&full[s], static_cast<uint32_t>(it / STAGES) & 1u, a.status,
                        kStatusGemmWait))
           break;
         const uint8_t* ch = smem + OFF_RAW + s * RAW_BYTES + c * CHUNK;
@@ -335,8 +340,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t scw = *reinterpret_cast<const uint32_t*>(ch + 1024 + rr * 8 + part * 4);
         __syncwarp();
         if (lane == 0) mbar_arrive(&lfree[s]);
-        if (kb >= ASTAGES &&
-            !mbar_wait(&afree[sa_i], static_cast<uint32_t>(kb / ASTAGES - 1) & 1u, a.status,
+        if (it >= ASTAGES &&
+            !mbar_wait(&afree[sa_i], static_cast<uint32_t>(it / ASTAGES - 1) & 1u, a.status,
                        kStatusGemmWait))
           break;
         const uint32_t s01 = e4m3x2_to_f16x2(static_cast<uint16_t>(scw & 0xffffu));
@@ -382,11 +387,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int orig = !a.w.swiglu ? n : (tr < 8 ? 8 * t + tr : a.w.N / 2 + 8 * t + tr - 8);
       bsc_row = a.w.blk_scale + static_cast<size_t>(orig / 128) * a.w.blk_ld;
     }
-    for (int kb = 0; kb < C; ++kb) {
-      const int s = kb % STAGES, sa_i = kb % ASTAGES;
+    for (int it = 0; it < NK; ++it) {
+      const int kb = KB0 + it, s = it % STAGES, sa_i = it % ASTAGES;
       float bscale = 1.f;
       if constexpr (FMT == kFmtFp8Block128) bscale = __ldg(bsc_row + (kb >> 1));
-      if (!mbar_wait(&full[s], static_cast<uint32_t>(kb / STAGES) & 1u, a.status,
+      if (!mbar_wait(&full[s], static_cast<uint32_t>(it / STAGES) & 1u, a.status,
                      kStatusGemmWait))
         break;
       const uint4* src = reinterpret_cast<const uint4*>(smem + OFF_RAW + s * RAW_BYTES +
@@ -396,8 +401,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int i = 0; i < NV; ++i) wv[i] = src[i];
       __syncwarp();
       if (lane == 0) mbar_arrive(&lfree[s]);  // raw bytes are in registers
-      if (kb >= ASTAGES &&
-          !mbar_wait(&afree[sa_i], static_cast<uint32_t>(kb / ASTAGES - 1) & 1u, a.status,
+      if (it >= ASTAGES &&
+          !mbar_wait(&afree[sa_i], static_cast<uint32_t>(it / ASTAGES - 1) & 1u, a.status,
                      kStatusGemmWait))
         break;
       uint8_t* arow = smem + OFF_A + sa_i * A_BYTES + h * A_HALF + (rh >> 3) * 1024 + (rh & 7) * 128;
@@ -457,6 +462,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int jj = 0; jj < 16; ++jj) {
           const int tk = cb * 16 + jj, tok = tok0 + tk;
+          if constexpr (EPI == kEpiPartial) {
+            // this split's scaled partial sum, rounded once the splits are added
+            if (tok < a.M && n < a.w.N)
+              a.part[(static_cast<size_t>(blockIdx.z) * a.M + tok) * a.w.N + n] =
+                  __uint_as_float(v[jj]) * (exp2i(sxexp[tk]) * rs);
+            continue;
+          }
           const float y = AT::round(__uint_as_float(v[jj]) * (exp2i(sxexp[tk]) * rs));
           if constexpr (EPI == kEpiSwiglu) {
             const float yu = __shfl_down_sync(0xffffffffu, y, 8);
@@ -501,26 +513,86 @@ EncodeTiledFn encode_fn() {
 }
 
 template <typename Act, int FMT, int EPI, int BM, int BN, int BK = 64>
-cudaError_t launch_gemm(const CUtensorMap& map, const GemmArgs& a, cudaStream_t s) {
+cudaError_t launch_gemm(const CUtensorMap& map, const GemmArgs& a, cudaStream_t s, int ks = 1) {
   using G = Cfg<BM, BN, BK>;
   auto kern = w8a16_gemm_kernel<Act, FMT, EPI, BM, BN, BK>;
   cudaError_t e =
       cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, G::SMEM_BYTES);
   if (e != cudaSuccess) return e;
-  const dim3 grid((a.M + BN - 1) / BN, a.w.T / (BM / 16));
+  const dim3 grid((a.M + BN - 1) / BN, a.w.T / (BM / 16), ks);
   kern<<<grid, kThreads, G::SMEM_BYTES, s>>>(map, a);
   return cudaGetLastError();
 }
 
-// 256 x 256 tiles when they give at least half the SMs a CTA (measured: a
-// half-empty wave of the larger tile still beats 3+ waves of 128 x 128),
-// else 128 x 128.
-bool use_big_tiles(const GemmArgs& a) {
+// Split-K epilogue: out = epilogue(act(sum over the ks partials, in split
+// order)); one thread per output element (SwiGLU: per gate/up pair).
+template <typename Act, int EPI>
+__global__ void splitk_finalize_kernel(const GemmArgs a, int ks) {
+  using AT = ActTraits<Act>;
+  const int N = a.w.N;
+  const int cols = EPI == kEpiSwiglu ? N / 2 : N;
+  const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (idx >= static_cast<long long>(a.M) * cols) return;
+  const int tok = static_cast<int>(idx / cols), j = static_cast<int>(idx % cols);
+  auto total = [&](int n) {
+    float y = 0.f;
+    for (int z = 0; z < ks; ++z) y += a.part[(static_cast<size_t>(z) * a.M + tok) * N + n];
+    return AT::round(y);
+  };
+  Act* o = reinterpret_cast<Act*>(a.out) + static_cast<size_t>(tok) * a.out_ld + j;
+  if constexpr (EPI == kEpiSwiglu) {
+    // fused gate/up rows: tile t holds gate rows 8t.. in rows 0-7, up rows in 8-15
+    const int t = j >> 3, tr = j & 7;
+    *o = AT::from_f(silu_mul_ref<Act>(total(16 * t + tr), total(16 * t + 8 + tr)));
+  } else if constexpr (EPI == kEpiResidual) {
+    *o = AT::from_f(total(j) + AT::to_f(*o));
+  } else {
+    *o = AT::from_f(total(j));
+  }
+}
+
+template <typename Act, int FMT, int BK>
+cudaError_t launch_split(const CUtensorMap& map, const GemmArgs& a, int epi, int ks,
+                         cudaStream_t s) {
+  cudaError_t e = launch_gemm<Act, FMT, kEpiPartial, 128, 128, BK>(map, a, s, ks);
+  if (e != cudaSuccess) return e;
+  const long long n = static_cast<long long>(a.M) * (epi == kEpiSwiglu ? a.w.N / 2 : a.w.N);
+  const int blocks = static_cast<int>((n + 255) / 256);
+  switch (epi) {
+    case kEpiStore: splitk_finalize_kernel<Act, kEpiStore><<<blocks, 256, 0, s>>>(a, ks); break;
+    case kEpiResidual: splitk_finalize_kernel<Act, kEpiResidual><<<blocks, 256, 0, s>>>(a, ks); break;
+    case kEpiSwiglu: splitk_finalize_kernel<Act, kEpiSwiglu><<<blocks, 256, 0, s>>>(a, ks); break;
+    default: return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
+int sm_count() {
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  return sms;
+}
+
+// 256 x 256 tiles when they give at least half the SMs a CTA (measured: a
+// half-empty wave of the larger tile still beats 3+ waves of 128 x 128),
+// else 128 x 128.  Calls of at most 128 rows (one token tile either way)
+// take 128 x 128 tiles, filled up by split-K where the caller allows it.
+bool use_big_tiles(const GemmArgs& a) {
+  if (a.M <= 128) return false;
   const bool fits = a.w.T % 16 == 0 && (a.w.swiglu ? (a.w.N / 2) % 128 == 0 : a.w.N % 256 == 0);
-  return fits && 2 * static_cast<long long>((a.M + 255) / 256) * (a.w.T / 16) >= sms;
+  return fits && 2 * static_cast<long long>((a.M + 255) / 256) * (a.w.T / 16) >= sm_count();
+}
+
+// K splits for a 128 x 128-tile launch: as many as keep the grid within the
+// SMs (at most 8, at least 4 k-steps each, partials within the workspace).
+int k_splits(const GemmArgs& a) {
+  if (!a.part) return 1;
+  const long long base = static_cast<long long>((a.M + 127) / 128) * (a.w.T / 8);
+  int ks = static_cast<int>(std::min<long long>(8, sm_count() / std::max(1ll, base)));
+  ks = std::min(ks, a.w.C / 4);
+  while (ks > 1 && static_cast<size_t>(ks) * a.M * a.w.N * 4 > a.part_bytes) --ks;
+  return std::max(ks, 1);
 }
 
 template <typename Act, int FMT>
@@ -550,7 +622,7 @@ cudaError_t launch_fmt(const CUtensorMap& map, const GemmArgs& a, int epi, bool 
 }
 
 template <typename Act>
-cudaError_t launch_act(const CUtensorMap& map, const GemmArgs& a, int epi, bool big,
+cudaError_t launch_act(const CUtensorMap& map, const GemmArgs& a, int epi, bool big, int ks,
                        cudaStream_t s) {
   if (a.norm_w)
     prep_kernel<Act, true><<<a.M, 256, 0, s>>>(a);
@@ -558,6 +630,15 @@ cudaError_t launch_act(const CUtensorMap& map, const GemmArgs& a, int epi, bool 
     prep_kernel<Act, false><<<a.M, 256, 0, s>>>(a);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
+  if (ks > 1) {
+    switch (a.w.fmt) {
+      case kFmtW8A16Row: return launch_split<Act, kFmtW8A16Row, 64>(map, a, epi, ks, s);
+      case kFmtFp8Row: return launch_split<Act, kFmtFp8Row, 64>(map, a, epi, ks, s);
+      case kFmtFp8Block128: return launch_split<Act, kFmtFp8Block128, 64>(map, a, epi, ks, s);
+      case kFmtNvfp4G16: return launch_split<Act, kFmtNvfp4G16, 128>(map, a, epi, ks, s);
+      default: return cudaErrorInvalidValue;
+    }
+  }
   switch (a.w.fmt) {
     case kFmtW8A16Row: return launch_fmt<Act, kFmtW8A16Row>(map, a, epi, big, s);
     case kFmtFp8Row: return launch_fmt<Act, kFmtFp8Row>(map, a, epi, big, s);
@@ -601,8 +682,9 @@ cudaError_t gemm_w8a16_launch(const GemmArgs& a, int act, int epi, cudaStream_t 
           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
     return cudaErrorInvalidValue;
-  return act == 0 ? launch_act<__nv_bfloat16>(map, a, epi, big, s)
-                  : launch_act<__half>(map, a, epi, big, s);
+  const int ks = big ? 1 : k_splits(a);
+  return act == 0 ? launch_act<__nv_bfloat16>(map, a, epi, big, ks, s)
+                  : launch_act<__half>(map, a, epi, big, ks, s);
 }
 
 }  // namespace dialb200

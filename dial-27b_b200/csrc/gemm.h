@@ -21,6 +21,12 @@ struct GemmArgs {
   __half* xh;           // scratch [M][w.K_pad]: staged f16 activations
   int* xexp;            // scratch [M]: per-row power-of-two pre-scale
   int* status;
+  // Optional split-K workspace (f32): when given and a launch would leave
+  // most SMs idle, K is cut into splits whose partial sums land here
+  // ([split][M][N]) and a second kernel adds them in split order and applies
+  // the epilogue.  Null: one pass over K.
+  float* part;
+  size_t part_bytes;
 };
 
 // True when the weight can take the tensor-core path: W8A16, FP8 (row or

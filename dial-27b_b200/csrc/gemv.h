@@ -41,7 +41,7 @@ struct GemvTuning {
   int gemm_min_rows = 16;    // rows from which linears take the tcgen05 GEMM (0 = never)
   int attn_min_split = 0;    // decode attention: context tokens per split at least (0 = 16)
   bool attn_tc = true;       // prefill attention on the tensor cores when supported
-  bool attn_ring = true;     // decode attention pages through a shared-memory ring
+  bool attn_ring = false;    // decode attention pages through a shared-memory ring (opt-in)
 };
 
 // act: 0 = bf16, 1 = f16.  Launches ceil(M/8) kernels on `stream`.

@@ -46,12 +46,17 @@ def _oracle_model(cfg, seed, fmt):
 
 
 @pytest.mark.parametrize("fmt_name", ["FMT_FP8_BLOCK128", "FMT_NVFP4_G16"])
-@pytest.mark.parametrize("n_prompt", [9, 80])
-def test_synthetic_quantised_model_matches_oracle(cuda, fmt_name, n_prompt):
+@pytest.mark.parametrize("n_prompt,wide", [(9, False), (80, False), (40, True)])
+def test_synthetic_quantised_model_matches_oracle(cuda, fmt_name, n_prompt, wide):
+    """The wide case (hidden 1024, FFN 2048, 40 rows) runs its projections as
+    split-K tensor-core GEMMs (few 128-row tiles, K long enough to cut)."""
     import dial_b200
 
     fmt = getattr(dial_b200, fmt_name)
-    cfg = small_cfg(hidden=256, inter=512, heads=2, kv_heads=1, layers=2, vocab=1000)
+    if wide:
+        cfg = small_cfg(hidden=1024, inter=2048, heads=8, kv_heads=2, layers=1, vocab=1000)
+    else:
+        cfg = small_cfg(hidden=256, inter=512, heads=2, kv_heads=1, layers=2, vocab=1000)
     dcfg = dial_b200.Config(hidden_size=cfg.hidden, intermediate_size=cfg.inter,
                             vocab_size=cfg.vocab, num_hidden_layers=cfg.layers,
                             num_attention_heads=cfg.heads, num_key_value_heads=cfg.kv_heads,
