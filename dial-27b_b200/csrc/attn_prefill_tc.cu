@@ -292,11 +292,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int i = 0; i < kKB; ++i) bm = fmaxf(bm, s[i]);
       const float m_new = fmaxf(m_run, bm);
-      const float alpha = (m_run == -INFINITY) ? 0.f : expf(m_run - m_new);
+      // exponentials through the hardware exp2 (__expf): its relative error
+      // (about 1e-6 here) is far below the bf16 rounding P receives
+      const float alpha = (m_run == -INFINITY) ? 0.f : __expf(m_run - m_new);
       float psum = 0.f;
 #pragma unroll
       for (int i = 0; i < kKB; ++i) {
-        const float p = (m_new == -INFINITY) ? 0.f : expf(s[i] - m_new);
+        const float p = (m_new == -INFINITY) ? 0.f : __expf(s[i] - m_new);
         s[i] = p;
         psum += p;
       }
@@ -312,15 +314,17 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         fence_after();
-        // unconditional: tcgen05.ld/st are warp-collective (.sync.aligned), so
-        // no lane may skip them; alpha is 1 for rows whose max did not move
+        // tcgen05.ld/st are warp-collective (.sync.aligned): the whole warp
+        // rescales its 32 rows, or none does when no row's max moved (alpha 1)
+        if (__any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll
-        for (int cb = 0; cb < kHeadDim / 16; ++cb) {
-          uint32_t v[16];
-          ld16(tO + lane_off + cb * 16, v);
+          for (int cb = 0; cb < kHeadDim / 16; ++cb) {
+            uint32_t v[16];
+            ld16(tO + lane_off + cb * 16, v);
 #pragma unroll
-          for (int e = 0; e < 16; ++e) v[e] = __float_as_uint(__uint_as_float(v[e]) * alpha);
-          st16(tO + lane_off + cb * 16, v);
+            for (int e = 0; e < 16; ++e) v[e] = __float_as_uint(__uint_as_float(v[e]) * alpha);
+            st16(tO + lane_off + cb * 16, v);
+          }
         }
       }
       // P row r as bf16 into the K-major swizzled tile: 16-byte chunk c holds keys 8c..8c+7
