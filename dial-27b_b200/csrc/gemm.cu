@@ -120,8 +120,71 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
 
 // ------------------------------------------------------------------ prep
 // Row m of x -> xh[m][0..Kp) as f16 * 2^-xexp[m] (RMSNorm first when norm_w).
+// One warp per row (8 rows per CTA): a first pass over the row takes the sum
+// of squares and the bound of the staged values (warp reductions only), the
+// second re-reads the row (an L2 hit) and writes it converted.
+constexpr int kPrepRows = 8;
+
 template <typename Act, bool NORM>
-__global__ void __launch_bounds__(256) prep_kernel(const GemmArgs a) {
+__global__ void __launch_bounds__(kPrepRows * 32) prep_kernel(const GemmArgs a) {
+  using AT = ActTraits<Act>;
+  constexpr bool SCALE = std::is_same<Act, __nv_bfloat16>::value;
+  const int lane = threadIdx.x & 31;
+  const int m = blockIdx.x * kPrepRows + (threadIdx.x >> 5);
+  if (m >= a.M) return;
+  const int K = a.w.K, Kp = a.w.K_pad, nv = K / 8;
+  const uint4* xr =
+      reinterpret_cast<const uint4*>(reinterpret_cast<const Act*>(a.x) + static_cast<size_t>(m) * a.x_ld);
+  const uint4* wr = reinterpret_cast<const uint4*>(a.norm_w);
+  float ss = 0.f, am = 0.f;
+#pragma unroll 4
+  for (int i = lane; i < nv; i += 32) {
+    float xf[8], wf[8];
+    unpack8<Act>(__ldcg(xr + i), xf);  // written by the previous kernel: read through L2
+    if (NORM) unpack8<Act>(__ldg(wr + i), wf);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      ss = fmaf(xf[e], xf[e], ss);
+      am = fmaxf(am, fabsf(NORM ? xf[e] * wf[e] : xf[e]));
+    }
+  }
+  ss = warp_sum(ss);
+  am = warp_max(am);
+  float rms = 1.f;
+  if (NORM) rms = AT::round(__fsqrt_rn(__fdiv_rn(ss, static_cast<float>(K)) + a.eps));
+  int e = 0;
+  if (SCALE) {
+    const float bound = NORM ? __fdiv_rn(am, rms) * 1.02f : am;
+    if (bound >= 16384.f) e = ilogbf(bound) - 13;
+  }
+  const float sc = exp2i(-e);
+  __half* orow = a.xh + static_cast<size_t>(m) * Kp;
+#pragma unroll 4
+  for (int i = lane; i < nv; i += 32) {
+    float xf[8], wf[8];
+    unpack8<Act>(__ldcg(xr + i), xf);
+    if (NORM) unpack8<Act>(__ldg(wr + i), wf);
+    uint4 o;
+    __half* h = reinterpret_cast<__half*>(&o);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      float v = xf[q];
+      if (NORM) {
+        v = AT::round(__fdiv_rn(v, rms));
+        v = AT::round(v * wf[q]);
+      }
+      h[q] = __float2half_rn(v * sc);
+    }
+    *reinterpret_cast<uint4*>(orow + static_cast<size_t>(i) * 8) = o;
+  }
+  for (int k = K + lane; k < Kp; k += 32) orow[k] = __float2half_rn(0.f);
+  if (lane == 0) a.xexp[m] = e;
+}
+
+// The same with one CTA of 256 threads per row: more loads in flight per row
+// for calls of few rows.
+template <typename Act, bool NORM>
+__global__ void __launch_bounds__(256) prep_row_kernel(const GemmArgs a) {
   using AT = ActTraits<Act>;
   constexpr bool SCALE = std::is_same<Act, __nv_bfloat16>::value;
   constexpr int NT = 256, VEC = 12;  // rows up to 24576 columns (27B-class down_proj: 21504)
@@ -624,10 +687,17 @@ cudaError_t launch_fmt(const CUtensorMap& map, const GemmArgs& a, int epi, bool 
 template <typename Act>
 cudaError_t launch_act(const CUtensorMap& map, const GemmArgs& a, int epi, bool big, int ks,
                        cudaStream_t s) {
-  if (a.norm_w)
-    prep_kernel<Act, true><<<a.M, 256, 0, s>>>(a);
-  else
-    prep_kernel<Act, false><<<a.M, 256, 0, s>>>(a);
+  const int prep_blocks = (a.M + kPrepRows - 1) / kPrepRows;
+  if (a.M < 256) {  // few rows: a CTA per row keeps more of each row's loads in flight
+    if (a.norm_w)
+      prep_row_kernel<Act, true><<<a.M, 256, 0, s>>>(a);
+    else
+      prep_row_kernel<Act, false><<<a.M, 256, 0, s>>>(a);
+  } else if (a.norm_w) {
+    prep_kernel<Act, true><<<prep_blocks, kPrepRows * 32, 0, s>>>(a);
+  } else {
+    prep_kernel<Act, false><<<prep_blocks, kPrepRows * 32, 0, s>>>(a);
+  }
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   if (ks > 1) {
