@@ -32,14 +32,17 @@ namespace {
 
 constexpr int kQ = 128;       // queries per CTA
 constexpr int kKB = 128;      // keys per block
-constexpr int kThreads = 192;
+// warps 0-3 and 6-9: softmax (two per 32-row TMEM lane quarter, one per
+// 64-key half of each block); warp 4: loads; warp 5: MMA
+constexpr int kThreads = 320;
 constexpr int TILE = 128 * 128 * 2;     // one 128 x 128 bf16 tile (two 64-column halves)
 constexpr int HALF = 128 * 64 * 2;      // one 64-column half: [128 rows][128 B]
 constexpr int OFF_Q = 0;
 constexpr int OFF_K = OFF_Q + TILE;           // [2] key tiles
 constexpr int OFF_V = OFF_K + 2 * TILE;       // [2] value tiles
 constexpr int OFF_P = OFF_V + 2 * TILE;       // probabilities
-constexpr int OFF_BAR = OFF_P + TILE;
+constexpr int OFF_XCH = OFF_P + TILE;        // row max exchange [2 parities][2 halves][128]
+constexpr int OFF_BAR = OFF_XCH + 2 * 2 * 128 * 4;
 // qbar, kvfull[2], kvfree[2], sbar, pready, obar, fin
 constexpr int NBAR = 9;
 constexpr int OFF_TMEM = OFF_BAR + NBAR * 8;
@@ -168,7 +171,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&kvfree[b], 1);
     }
     mbar_init(sbar, 1);
-    mbar_init(pready, kQ);
+    mbar_init(pready, 2 * kQ);  // every softmax thread of both halves
     mbar_init(obar, 1);
     mbar_init(fin, 1);
     fence_mbar_init();
@@ -261,13 +264,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ---------------------------------------------- softmax + epilogue
-    const int r = tid;  // query row of the block = TMEM lane
+    // two warps per 32 query rows (the TMEM lane quarter warp % 4 they may
+    // read): half 0 takes keys / output dims 0-63 of every block, half 1 64-127
+    const int quarter = warp & 3, half = warp >= 6 ? 1 : 0;
+    const int r = quarter * 32 + lane;  // query row of the block = TMEM lane
     const int qi = q0 + r;
     const int qpos = a.p0 + qi;
     const float scale = AT::round(1.0f / sqrtf(static_cast<float>(kHeadDim)));
-    const uint32_t lane_off = static_cast<uint32_t>(32 * warp) << 16;
-    float m_run = -INFINITY, l_run = 0.f;
+    const uint32_t lane_off = static_cast<uint32_t>(32 * quarter) << 16;
+    float* xch = reinterpret_cast<float*>(smem + OFF_XCH);  // [parity][half][row]
+    auto pair_sync = [&]() { named_bar_sync(1 + quarter, 64); };
+    float m_run = -INFINITY, l_run = 0.f;  // l_run: this half's share of the row sum
     bool ok = true;
+    int exchanged = 0;  // pair barriers passed; both warps of a pair pass nkb + 1
     for (int j = 0; j < nkb; ++j) {
       const bool okw = __all_sync(0xffffffffu, ok && mbar_wait(sbar, static_cast<uint32_t>(j) & 1u,
                                                                a.status, kStatusAttnTc));
@@ -276,28 +285,36 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       fence_after();
-      float s[kKB];
+      constexpr int KH = kKB / 2;  // keys of this half
+      float s[KH];
 #pragma unroll
-      for (int cb = 0; cb < kKB / 16; ++cb) {
+      for (int cb = 0; cb < KH / 16; ++cb) {
         uint32_t v[16];
-        ld16(tS + lane_off + cb * 16, v);
+        ld16(tS + lane_off + half * KH + cb * 16, v);
 #pragma unroll
         for (int e = 0; e < 16; ++e) {
-          const int kpos = j * kKB + cb * 16 + e;
+          const int kpos = j * kKB + half * KH + cb * 16 + e;
           const float sc = AT::round(AT::round(__uint_as_float(v[e])) * scale);
           s[cb * 16 + e] = (kpos <= qpos && qi < a.M) ? sc : -INFINITY;
         }
       }
       float bm = -INFINITY;
 #pragma unroll
-      for (int i = 0; i < kKB; ++i) bm = fmaxf(bm, s[i]);
+      for (int i = 0; i < KH; ++i) bm = fmaxf(bm, s[i]);
+      // the row's block max: exchange with the other half (buffers by block
+      // parity: a warp cannot be two blocks ahead of its partner)
+      float* xj = xch + (j & 1) * 256;
+      xj[half * 128 + r] = bm;
+      pair_sync();
+      ++exchanged;
+      bm = fmaxf(bm, xj[(half ^ 1) * 128 + r]);
       const float m_new = fmaxf(m_run, bm);
       // exponentials through the hardware exp2 (__expf): its relative error
       // (about 1e-6 here) is far below the bf16 rounding P receives
       const float alpha = (m_run == -INFINITY) ? 0.f : __expf(m_run - m_new);
       float psum = 0.f;
 #pragma unroll
-      for (int i = 0; i < kKB; ++i) {
+      for (int i = 0; i < KH; ++i) {
         const float p = (m_new == -INFINITY) ? 0.f : __expf(s[i] - m_new);
         s[i] = p;
         psum += p;
@@ -318,43 +335,52 @@ __global__ void __launch_bounds__(kThreads, 1)
         // rescales its 32 rows, or none does when no row's max moved (alpha 1)
         if (__any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll
-          for (int cb = 0; cb < kHeadDim / 16; ++cb) {
+          for (int cb = 0; cb < kHeadDim / 32; ++cb) {  // this half's 64 dims
             uint32_t v[16];
-            ld16(tO + lane_off + cb * 16, v);
+            const uint32_t col = tO + lane_off + half * (kHeadDim / 2) + cb * 16;
+            ld16(col, v);
 #pragma unroll
             for (int e = 0; e < 16; ++e) v[e] = __float_as_uint(__uint_as_float(v[e]) * alpha);
-            st16(tO + lane_off + cb * 16, v);
+            st16(col, v);
           }
         }
       }
       // P row r as bf16 into the K-major swizzled tile: 16-byte chunk c holds keys 8c..8c+7
       uint8_t* prow = smem + OFF_P + (r >> 3) * 1024 + (r & 7) * 128;
 #pragma unroll
-      for (int c = 0; c < kKB / 8; ++c) {
+      for (int jj = 0; jj < KH / 8; ++jj) {  // this half's 8 chunks of 8 keys
         uint4 o;
         __nv_bfloat16* hv = reinterpret_cast<__nv_bfloat16*>(&o);
 #pragma unroll
-        for (int e = 0; e < 8; ++e) hv[e] = __float2bfloat16_rn(s[c * 8 + e]);
-        const int half = c >> 3, jj = c & 7;
+        for (int e = 0; e < 8; ++e) hv[e] = __float2bfloat16_rn(s[jj * 8 + e]);
         *reinterpret_cast<uint4*>(prow + half * HALF + ((jj ^ (r & 7)) << 4)) = o;
       }
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       fence_before();
       mbar_arrive(pready);
     }
+    // a warp that left the loop on a failed wait still meets its partner at
+    // every exchange (the status word already holds the error)
+    for (; exchanged < nkb; ++exchanged) pair_sync();
+    // row sum = both halves' shares (same running max sequence)
+    float* xl = xch + (nkb & 1) * 256;
+    xl[half * 128 + r] = l_run;
+    pair_sync();
+    const float l_tot = l_run + xl[(half ^ 1) * 128 + r];
     if (ok) {
       const bool okw =
           __all_sync(0xffffffffu, mbar_wait(obar, static_cast<uint32_t>(nkb - 1) & 1u, a.status,
                                             kStatusAttnTc));
       if (okw) {
         fence_after();
-        const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+        const float inv = l_tot > 0.f ? 1.f / l_tot : 0.f;
         __nv_bfloat16* orow = reinterpret_cast<__nv_bfloat16*>(a.out) +
-                              static_cast<size_t>(qi) * a.out_ld + h * kHeadDim;
+                              static_cast<size_t>(qi) * a.out_ld + h * kHeadDim +
+                              half * (kHeadDim / 2);
 #pragma unroll
-        for (int cb = 0; cb < kHeadDim / 16; ++cb) {
+        for (int cb = 0; cb < kHeadDim / 32; ++cb) {
           uint32_t v[16];
-          ld16(tO + lane_off + cb * 16, v);
+          ld16(tO + lane_off + half * (kHeadDim / 2) + cb * 16, v);
           if (qi < a.M) {
             uint4 o[2];
             __nv_bfloat16* hv = reinterpret_cast<__nv_bfloat16*>(o);
