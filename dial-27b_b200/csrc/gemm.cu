@@ -48,7 +48,9 @@ struct Cfg {
   static constexpr int BK = BK_;  // K per ring stage
   static constexpr int NATOM = BK / 64;
   static constexpr int CHUNK = BK == 128 ? 1152 : 1024;  // bytes per 16-row weight chunk
-  static constexpr int STAGES = (BM == 256 || BK == 128) ? 3 : 5;   // load ring
+  // load ring: 64-token tiles (calls of few rows) trade activation space for
+  // weight stages in flight
+  static constexpr int STAGES = (BM == 256 || BK == 128) ? 3 : (BN <= 64 ? 9 : 5);
   static constexpr int ASTAGES = (BM == 256 || BK == 128) ? 2 : 4;  // dequantized-weight ring
   static constexpr int A_HALF = 128 * BK * 2;  // one 128-row MMA operand
   static constexpr int A_BYTES = BM * BK * 2;
@@ -615,9 +617,10 @@ __global__ void splitk_finalize_kernel(const GemmArgs a, int ks) {
 }
 
 template <typename Act, int FMT, int BK>
-cudaError_t launch_split(const CUtensorMap& map, const GemmArgs& a, int epi, int ks,
+cudaError_t launch_split(const CUtensorMap& map, const GemmArgs& a, int epi, int ks, int bn,
                          cudaStream_t s) {
-  cudaError_t e = launch_gemm<Act, FMT, kEpiPartial, 128, 128, BK>(map, a, s, ks);
+  cudaError_t e = bn == 64 ? launch_gemm<Act, FMT, kEpiPartial, 128, 64, BK>(map, a, s, ks)
+                           : launch_gemm<Act, FMT, kEpiPartial, 128, 128, BK>(map, a, s, ks);
   if (e != cudaSuccess) return e;
   const long long n = static_cast<long long>(a.M) * (epi == kEpiSwiglu ? a.w.N / 2 : a.w.N);
   const int blocks = static_cast<int>((n + 255) / 256);
@@ -649,9 +652,9 @@ bool use_big_tiles(const GemmArgs& a) {
 
 // K splits for a 128 x 128-tile launch: as many as keep the grid within the
 // SMs (at most 8, at least 4 k-steps each, partials within the workspace).
-int k_splits(const GemmArgs& a) {
+int k_splits(const GemmArgs& a, int bn) {
   if (!a.part) return 1;
-  const long long base = static_cast<long long>((a.M + 127) / 128) * (a.w.T / 8);
+  const long long base = static_cast<long long>((a.M + bn - 1) / bn) * (a.w.T / 8);
   int ks = static_cast<int>(std::min<long long>(8, sm_count() / std::max(1ll, base)));
   ks = std::min(ks, a.w.C / 4);
   while (ks > 1 && static_cast<size_t>(ks) * a.M * a.w.N * 4 > a.part_bytes) --ks;
@@ -659,7 +662,7 @@ int k_splits(const GemmArgs& a) {
 }
 
 template <typename Act, int FMT>
-cudaError_t launch_fmt(const CUtensorMap& map, const GemmArgs& a, int epi, bool big,
+cudaError_t launch_fmt(const CUtensorMap& map, const GemmArgs& a, int epi, bool big, int bn,
                        cudaStream_t s) {
   if constexpr (FMT == kFmtNvfp4G16) {
     switch (epi) {
@@ -672,13 +675,16 @@ cudaError_t launch_fmt(const CUtensorMap& map, const GemmArgs& a, int epi, bool 
     switch (epi) {
       case kEpiStore:
         return big ? launch_gemm<Act, FMT, kEpiStore, 256, 256>(map, a, s)
-                   : launch_gemm<Act, FMT, kEpiStore, 128, 128>(map, a, s);
+               : bn == 64 ? launch_gemm<Act, FMT, kEpiStore, 128, 64>(map, a, s)
+                          : launch_gemm<Act, FMT, kEpiStore, 128, 128>(map, a, s);
       case kEpiResidual:
         return big ? launch_gemm<Act, FMT, kEpiResidual, 256, 256>(map, a, s)
-                   : launch_gemm<Act, FMT, kEpiResidual, 128, 128>(map, a, s);
+               : bn == 64 ? launch_gemm<Act, FMT, kEpiResidual, 128, 64>(map, a, s)
+                          : launch_gemm<Act, FMT, kEpiResidual, 128, 128>(map, a, s);
       case kEpiSwiglu:
         return big ? launch_gemm<Act, FMT, kEpiSwiglu, 256, 256>(map, a, s)
-                   : launch_gemm<Act, FMT, kEpiSwiglu, 128, 128>(map, a, s);
+               : bn == 64 ? launch_gemm<Act, FMT, kEpiSwiglu, 128, 64>(map, a, s)
+                          : launch_gemm<Act, FMT, kEpiSwiglu, 128, 128>(map, a, s);
       default: return cudaErrorInvalidValue;
     }
   }
@@ -686,7 +692,7 @@ cudaError_t launch_fmt(const CUtensorMap& map, const GemmArgs& a, int epi, bool 
 
 template <typename Act>
 cudaError_t launch_act(const CUtensorMap& map, const GemmArgs& a, int epi, bool big, int ks,
-                       cudaStream_t s) {
+                       int bn, cudaStream_t s) {
   const int prep_blocks = (a.M + kPrepRows - 1) / kPrepRows;
   if (a.M < 256) {  // few rows: a CTA per row keeps more of each row's loads in flight
     if (a.norm_w)
@@ -702,18 +708,18 @@ cudaError_t launch_act(const CUtensorMap& map, const GemmArgs& a, int epi, bool 
   if (e != cudaSuccess) return e;
   if (ks > 1) {
     switch (a.w.fmt) {
-      case kFmtW8A16Row: return launch_split<Act, kFmtW8A16Row, 64>(map, a, epi, ks, s);
-      case kFmtFp8Row: return launch_split<Act, kFmtFp8Row, 64>(map, a, epi, ks, s);
-      case kFmtFp8Block128: return launch_split<Act, kFmtFp8Block128, 64>(map, a, epi, ks, s);
-      case kFmtNvfp4G16: return launch_split<Act, kFmtNvfp4G16, 128>(map, a, epi, ks, s);
+      case kFmtW8A16Row: return launch_split<Act, kFmtW8A16Row, 64>(map, a, epi, ks, bn, s);
+      case kFmtFp8Row: return launch_split<Act, kFmtFp8Row, 64>(map, a, epi, ks, bn, s);
+      case kFmtFp8Block128: return launch_split<Act, kFmtFp8Block128, 64>(map, a, epi, ks, bn, s);
+      case kFmtNvfp4G16: return launch_split<Act, kFmtNvfp4G16, 128>(map, a, epi, ks, bn, s);
       default: return cudaErrorInvalidValue;
     }
   }
   switch (a.w.fmt) {
-    case kFmtW8A16Row: return launch_fmt<Act, kFmtW8A16Row>(map, a, epi, big, s);
-    case kFmtFp8Row: return launch_fmt<Act, kFmtFp8Row>(map, a, epi, big, s);
-    case kFmtFp8Block128: return launch_fmt<Act, kFmtFp8Block128>(map, a, epi, big, s);
-    case kFmtNvfp4G16: return launch_fmt<Act, kFmtNvfp4G16>(map, a, epi, false, s);
+    case kFmtW8A16Row: return launch_fmt<Act, kFmtW8A16Row>(map, a, epi, big, bn, s);
+    case kFmtFp8Row: return launch_fmt<Act, kFmtFp8Row>(map, a, epi, big, bn, s);
+    case kFmtFp8Block128: return launch_fmt<Act, kFmtFp8Block128>(map, a, epi, big, bn, s);
+    case kFmtNvfp4G16: return launch_fmt<Act, kFmtNvfp4G16>(map, a, epi, false, 128, s);
     default: return cudaErrorInvalidValue;
   }
 }
@@ -746,15 +752,17 @@ cudaError_t gemm_w8a16_launch(const GemmArgs& a, int act, int epi, cudaStream_t 
   const cuuint64_t dims[2] = {static_cast<cuuint64_t>(a.w.K_pad), static_cast<cuuint64_t>(a.M)};
   const cuuint64_t strides[1] = {static_cast<cuuint64_t>(a.w.K_pad) * 2};
   const bool big = a.w.fmt != kFmtNvfp4G16 && use_big_tiles(a);
-  const cuuint32_t box[2] = {64, big ? 256u : 128u};
+  // 64-token tiles for calls of at most 64 rows (int8 / e4m3 weights)
+  const int bn = big ? 256 : (a.w.fmt != kFmtNvfp4G16 && a.M <= 64 ? 64 : 128);
+  const cuuint32_t box[2] = {64, static_cast<cuuint32_t>(bn)};
   const cuuint32_t estr[2] = {1, 1};
   if (enc(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, a.xh, dims, strides, box, estr,
           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
     return cudaErrorInvalidValue;
-  const int ks = big ? 1 : k_splits(a);
-  return act == 0 ? launch_act<__nv_bfloat16>(map, a, epi, big, ks, s)
-                  : launch_act<__half>(map, a, epi, big, ks, s);
+  const int ks = big ? 1 : k_splits(a, bn);
+  return act == 0 ? launch_act<__nv_bfloat16>(map, a, epi, big, ks, bn, s)
+                  : launch_act<__half>(map, a, epi, big, ks, bn, s);
 }
 
 }  // namespace dialb200
