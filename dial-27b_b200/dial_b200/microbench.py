@@ -93,14 +93,36 @@ def run_case(name: str, M: int, iters: int, min_footprint: int, device: int = 0)
             "l2": f"rotation over {copies} weight copies ({copies * wbytes / 2**20:.0f} MiB)"}
 
 
+def run_prefill(n_prompt: int) -> dict:
+    """Two prefills of n_prompt seeded tokens on the synthetic Qwen3-8B W8A16
+    engine (the first loads kernels lazily); reports the second's TTFT and
+    how many kernels one prefill launches (the tail of a profiler's launch
+    list)."""
+    from .engine import Config, Engine
+
+    cfg = Config(max_seq_len=n_prompt + 64, max_sessions=1, max_tokens=n_prompt)
+    eng = Engine(cfg, device=0)
+    eng.load_synthetic(seed=0)
+    prompt = np.random.default_rng(1).integers(0, cfg.vocab_size, n_prompt).astype(np.int32)
+    eng.generate(prompt, 1)
+    _, ttft, _ = eng.generate(prompt, 1)
+    return {"prefill_tokens": n_prompt, "ttft_ms": ttft * 1e3,
+            "launches_per_prefill": eng.prefill_kernel_count(n_prompt)}
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--shapes", default=",".join(SHAPES))
     ap.add_argument("--M", default="1,4,16,128,2048")
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--min-footprint-mb", type=int, default=512)
+    ap.add_argument("--prefill", type=int, default=0,
+                    help="instead: time a warmed prefill of this many tokens on the synthetic model")
     args = ap.parse_args(argv)
     torch.cuda.set_device(0)
+    if args.prefill > 0:
+        print(json.dumps(run_prefill(args.prefill)), flush=True)
+        return
     for name in args.shapes.split(","):
         for M in (int(m) for m in args.M.split(",")):
             r = run_case(name, M, args.iters, args.min_footprint_mb << 20)
