@@ -25,8 +25,15 @@ namespace {
 
 constexpr int kD = kHeadDim;
 
+// CTAs per SM the plain kernel is register-limited to: 6 for groups of 4
+// query heads (80 registers, a few spills) keeps 48 KB of page loads in
+// flight per SM instead of 32 KB at the unconstrained 4 CTAs.
+template <int NREP>
+constexpr int decode_min_ctas() { return NREP == 4 ? 6 : 1; }
+
 template <typename Act, int NREP>
-__global__ void __launch_bounds__(NREP * 32) attn_decode_kernel(const AttnDecodeArgs a) {
+__global__ void __launch_bounds__(NREP * 32, decode_min_ctas<NREP>())
+    attn_decode_kernel(const AttnDecodeArgs a) {
   pdl_launch_dependents();
   __shared__ AttnItemSmem sm;
   attn_item<Act, NREP, true>(a, blockIdx.z, blockIdx.x, blockIdx.y, threadIdx.x >> 5,
