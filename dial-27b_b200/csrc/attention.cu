@@ -13,7 +13,10 @@
 // Scores follow the reference's rounding: act(act(q.k) * act(1/sqrt(d))),
 // then an f32 online softmax.  With more than one split, partials go to a
 // scratch buffer and the last CTA of each (row, kv head) combines them
-// (arrival counter, self-resetting to zero).
+// (arrival counter, self-resetting to zero).  Steps of more than 4 rows with
+// groups of 4 query heads take the token-split form instead: each warp reads
+// a quarter of every page and scores it for all 4 heads, so every K/V row is
+// loaded once per CTA rather than once per warp.
 #include <cmath>
 
 #include "attention.h"
@@ -38,6 +41,22 @@ __global__ void __launch_bounds__(NREP * 32, decode_min_ctas<NREP>())
   __shared__ AttnItemSmem sm;
   attn_item<Act, NREP, true>(a, blockIdx.z, blockIdx.x, blockIdx.y, threadIdx.x >> 5,
                              threadIdx.x & 31, sm, 1);
+}
+
+// Token-split form: the group's warps share each page's tokens (TSG pages of
+// loads in flight per warp) and merge their per-head partials in shared memory.
+// One page per warp (96 registers, 5 CTAs per SM) measured ahead of 2 and 4
+// (128 / 167 registers: 4 / 3 CTAs per SM).
+constexpr int kTokSplitPages = 1;
+
+template <typename Act, int NREP, int TSG>
+__global__ void __launch_bounds__(NREP * 32) attn_decode_ts_kernel(const AttnDecodeArgs a) {
+  pdl_launch_dependents();
+  __shared__ AttnItemSmem sm;
+  __shared__ AttnTokSplitSmem<NREP> ts;
+  attn_item<Act, NREP, true, 0, 0, TSG>(a, blockIdx.z, blockIdx.x, blockIdx.y, threadIdx.x >> 5,
+                                        threadIdx.x & 31, sm, 1, nullptr, nullptr, nullptr,
+                                        nullptr, &ts);
 }
 
 // Cluster form: the CL splits of a (row, kv head) that share a cluster merge
@@ -169,18 +188,25 @@ cudaError_t launch_decode_t(const AttnDecodeArgs& a, cudaStream_t s, bool pdl) {
     if (a.splits % 16 == 0 && launch_cluster<Act, NREP, 16, false>(a, s, pdl, err)) return err;
     if (a.splits % 8 == 0 && launch_cluster<Act, NREP, 8, false>(a, s, pdl, err)) return err;
   }
+  // token split for steps of many rows (groups of 4 query heads); it takes
+  // precedence over the page ring
+  const bool ts = NREP == 4 && a.tok_split && a.M > 4;
+  const bool ring = a.page_ring && !ts;
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(a.sh.kv_heads, a.splits, a.M);
-  cfg.blockDim = dim3((NREP + (a.page_ring ? 1 : 0)) * 32);
-  cfg.dynamicSmemBytes = a.page_ring ? kRingBytes : 0;
+  cfg.blockDim = dim3((NREP + (ring ? 1 : 0)) * 32);
+  cfg.dynamicSmemBytes = ring ? kRingBytes : 0;
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return a.page_ring ? cudaLaunchKernelEx(&cfg, attn_decode_ring_kernel<Act, NREP, 0>, a)
-                     : cudaLaunchKernelEx(&cfg, attn_decode_kernel<Act, NREP>, a);
+  if constexpr (NREP == 4) {
+    if (ts) return cudaLaunchKernelEx(&cfg, attn_decode_ts_kernel<Act, NREP, kTokSplitPages>, a);
+  }
+  return ring ? cudaLaunchKernelEx(&cfg, attn_decode_ring_kernel<Act, NREP, 0>, a)
+              : cudaLaunchKernelEx(&cfg, attn_decode_kernel<Act, NREP>, a);
 }
 
 template <typename Act>

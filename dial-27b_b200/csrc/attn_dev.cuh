@@ -6,7 +6,10 @@
 // normalizes/rotates its K, appends K/V to the pages and scores it from
 // shared memory, then an f32 online softmax over the span.  With several
 // splits the partials land in scratch and the last item to arrive on the
-// (row, kv head) counter combines them and writes the output.
+// (row, kv head) counter combines them and writes the output.  In the
+// token-split form (TSG > 0) the NREP warps instead share each page's tokens,
+// each scoring its share for every query head of the group, and merge their
+// per-head partials in shared memory before that combine.
 //
 // Reference: text.rs:1466-1467,1513-1514 (q/k norm), 1143-1153 (RoPE),
 // llama3/cache.rs:169-237 (KV append), text.rs:1258-1281 (grouped decode).
@@ -118,6 +121,16 @@ template <int NREP>
 struct __align__(16) AttnClusterSmem {
   float o[NREP][kHeadDim];
   float ml[NREP][2];
+};
+
+// Token-split form (register pages, many rows): the group's query heads
+// after norm + RoPE, and each warp's partial (o, m, l) for every head of the
+// group, merged per head after the span.
+template <int NREP>
+struct __align__(16) AttnTokSplitSmem {
+  float q[NREP][kHeadDim];
+  float o[NREP][NREP][kHeadDim];
+  float ml[NREP][NREP][2];
 };
 
 __device__ __forceinline__ uint32_t cluster_map(const void* p, int rank) {
@@ -301,11 +314,13 @@ __device__ void attn_global_combine(const AttnDecodeArgs& a, int m, int kvh, int
 // (K page then V page, 4 KB each; full[] / empty[] mbarriers) that the
 // CTA's producer warp fills (attn_ring_producer); the query warps read each
 // page from shared memory and release its slot.
-template <typename Act, int NREP, bool PDL = false, int CL = 0, int RING = 0>
+template <typename Act, int NREP, bool PDL = false, int CL = 0, int RING = 0, int TSG = 0>
 __device__ void attn_item(const AttnDecodeArgs& a, int m, int kvh, int split, int r, int lane,
                           AttnItemSmem& sm, int bar_id, AttnClusterSmem<NREP>* csm = nullptr,
                           const uint8_t* ring = nullptr, uint64_t* rfull = nullptr,
-                          uint64_t* rempty = nullptr) {
+                          uint64_t* rempty = nullptr, AttnTokSplitSmem<NREP>* tss = nullptr) {
+  static_assert(TSG == 0 || (CL == 0 && RING == 0 && kPageTokens % NREP == 0 && 32 % (TSG > 0 ? TSG : 1) == 0),
+                "token split: register pages, no cluster, NREP | 16, TSG | 32");
   using AT = ActTraits<Act>;
   const int QH = a.sh.q_heads, KVH = a.sh.kv_heads;
   const int h = kvh * NREP + r;
@@ -336,6 +351,8 @@ __device__ void attn_item(const AttnDecodeArgs& a, int m, int kvh, int split, in
   const int tok0 = split * span;
   const int tok1 = active ? min(ctx, tok0 + span) : tok0;
   const bool owner = tok0 <= pos && pos < tok1;
+  const int pg_first = tok0 / kPageTokens;
+  const int npg = (tok1 - tok0 + kPageTokens - 1) / kPageTokens;
 
   const Act* qkv = reinterpret_cast<const Act*>(a.qkv) + static_cast<size_t>(m) * a.qkv_ld;
   const Act* cos_row = reinterpret_cast<const Act*>(a.cos) + static_cast<size_t>(pos) * (kHeadDim / 2);
@@ -349,8 +366,7 @@ __device__ void attn_item(const AttnDecodeArgs& a, int m, int kvh, int split, in
   const int blk_first = (RING == 0 && active) ? bt[tok0 / kPageTokens] : 0;
   // the other block ids of the span's first 32 pages (register form)
   const int bt_lane0 =
-      (RING == 0 && active && lane < (tok1 - tok0 + kPageTokens - 1) / kPageTokens)
-          ? bt[tok0 / kPageTokens + lane]
+      (RING == 0 && active && lane < npg) ? bt[pg_first + lane]
           : 0;
   const int blk_pos = do_kv ? bt[pos / kPageTokens] : 0;
   float q[4], kn[4] = {0.f, 0.f, 0.f, 0.f}, vn[4] = {0.f, 0.f, 0.f, 0.f};
@@ -368,7 +384,29 @@ __device__ void attn_item(const AttnDecodeArgs& a, int m, int kvh, int split, in
   load4(sin_row + (lane & 15) * 4, sn);
   // first page's K/V (depends only on the block id)
   uint2 kr[kPageTokens], vr[kPageTokens];
-  if (RING == 0 && active) {
+  // token-split form: TSG pages at a time, TPW tokens of each for this warp
+  constexpr int TPW = TSG > 0 ? kPageTokens / NREP : 1;
+  constexpr int TG = TSG > 0 ? TSG : 1;
+  uint2 kg[TG][TPW], vg[TG][TPW];
+  auto load_group = [&](int pg0, int bt_l) {
+#pragma unroll
+    for (int p = 0; p < TG; ++p) {
+      const int blk = __shfl_sync(0xffffffffu, bt_l, (pg0 + p) & 31);
+      if (pg0 + p < npg) {
+        const size_t base =
+            ((static_cast<size_t>(blk) * KVH + kvh) * kPageTokens + r * TPW) * kHeadDim + lane * 4;
+#pragma unroll
+        for (int t = 0; t < TPW; ++t) {
+          kg[p][t] = *reinterpret_cast<const uint2*>(kpool + base + t * kHeadDim);
+          vg[p][t] = *reinterpret_cast<const uint2*>(vpool + base + t * kHeadDim);
+        }
+      }
+    }
+  };
+  if constexpr (TSG > 0) {
+    if (active) load_group(0, bt_lane0);
+  }
+  if (RING == 0 && TSG == 0 && active) {
     const size_t base =
         (static_cast<size_t>(blk_first) * KVH + kvh) * kPageTokens * kHeadDim + lane * 4;
 #pragma unroll
@@ -389,6 +427,8 @@ __device__ void attn_item(const AttnDecodeArgs& a, int m, int kvh, int split, in
   }
 
   norm_rope_pre<Act>(q, qw, a.sh.eps, cs, sn, lane);
+  if constexpr (TSG > 0)
+    *reinterpret_cast<float4*>(&tss->q[r][lane * 4]) = make_float4(q[0], q[1], q[2], q[3]);
   if (do_kv) {
     norm_rope_pre<Act>(kn, kw, a.sh.eps, cs, sn, lane);
 #pragma unroll
@@ -416,96 +456,224 @@ __device__ void attn_item(const AttnDecodeArgs& a, int m, int kvh, int split, in
                      ((lane >> 1) & 1);
 
   // block ids of the span's pages, 32 at a time: lane l holds page (32i + l)
-  const int pg_first = tok0 / kPageTokens;
-  const int npg = (tok1 - tok0 + kPageTokens - 1) / kPageTokens;
   int bt_lane = bt_lane0;
-  for (int b0 = tok0, pg = 0; b0 < tok1; b0 += kPageTokens, ++pg) {
-    if (RING == 0 && (pg & 31) == 0 && pg > 0)
-      bt_lane = pg + lane < npg ? bt[pg_first + pg + lane] : 0;
-    if constexpr (RING > 0) {
-      // the page's K/V rows (lane: dims 4*lane.. of every token) from the ring
-      const int slot = pg % RING;
-      mbar_wait(&rfull[slot], static_cast<uint32_t>(pg / RING) & 1u, a.status, kStatusAttnRing);
-      const uint8_t* kp = ring + slot * (2 * kPageBytes);
-      const uint8_t* vp = kp + kPageBytes;
+  if constexpr (TSG == 0) {
+    for (int b0 = tok0, pg = 0; b0 < tok1; b0 += kPageTokens, ++pg) {
+      if (RING == 0 && (pg & 31) == 0 && pg > 0)
+        bt_lane = pg + lane < npg ? bt[pg_first + pg + lane] : 0;
+      if constexpr (RING > 0) {
+        // the page's K/V rows (lane: dims 4*lane.. of every token) from the ring
+        const int slot = pg % RING;
+        mbar_wait(&rfull[slot], static_cast<uint32_t>(pg / RING) & 1u, a.status, kStatusAttnRing);
+        const uint8_t* kp = ring + slot * (2 * kPageBytes);
+        const uint8_t* vp = kp + kPageBytes;
+#pragma unroll
+        for (int j = 0; j < kPageTokens; ++j) {
+          kr[j] = *reinterpret_cast<const uint2*>(kp + j * kHeadDim * 2 + lane * 8);
+          vr[j] = *reinterpret_cast<const uint2*>(vp + j * kHeadDim * 2 + lane * 8);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&rempty[slot]);
+      } else if (b0 != tok0) {
+        const int blk = __shfl_sync(0xffffffffu, bt_lane, pg & 31);
+        const size_t base = (static_cast<size_t>(blk) * KVH + kvh) * kPageTokens * kHeadDim + lane * 4;
+#pragma unroll
+        for (int j = 0; j < kPageTokens; ++j) {
+          kr[j] = *reinterpret_cast<const uint2*>(kpool + base + j * kHeadDim);
+          vr[j] = *reinterpret_cast<const uint2*>(vpool + base + j * kHeadDim);
+        }
+      }
+      float v16[kPageTokens];
 #pragma unroll
       for (int j = 0; j < kPageTokens; ++j) {
-        kr[j] = *reinterpret_cast<const uint2*>(kp + j * kHeadDim * 2 + lane * 8);
-        vr[j] = *reinterpret_cast<const uint2*>(vp + j * kHeadDim * 2 + lane * 8);
+        const Act* kh = reinterpret_cast<const Act*>(&kr[j]);
+        float d = 0.f;
+        if (owner && b0 + j == pos) {
+#pragma unroll
+          for (int e = 0; e < 4; ++e) d = fmaf(q[e], sm.kn[lane * 4 + e], d);
+        } else {
+#pragma unroll
+          for (int e = 0; e < 4; ++e) d = fmaf(q[e], AT::to_f(kh[e]), d);
+        }
+        v16[j] = d;
       }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&rempty[slot]);
-    } else if (b0 != tok0) {
-      const int blk = __shfl_sync(0xffffffffu, bt_lane, pg & 31);
-      const size_t base = (static_cast<size_t>(blk) * KVH + kvh) * kPageTokens * kHeadDim + lane * 4;
+      // reduce-scatter: afterwards lane holds the full dot of token my_tok
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float send = (lane & 16) ? v16[i] : v16[i + 8];
+        const float keep = (lane & 16) ? v16[i + 8] : v16[i];
+        v16[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float send = (lane & 8) ? v16[i] : v16[i + 4];
+        const float keep = (lane & 8) ? v16[i + 4] : v16[i];
+        v16[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+      }
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        const float send = (lane & 4) ? v16[i] : v16[i + 2];
+        const float keep = (lane & 4) ? v16[i + 2] : v16[i];
+        v16[i] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+      }
+      {
+        const float send = (lane & 2) ? v16[0] : v16[1];
+        const float keep = (lane & 2) ? v16[1] : v16[0];
+        v16[0] = keep + __shfl_xor_sync(0xffffffffu, send, 2);
+      }
+      float s = v16[0] + __shfl_xor_sync(0xffffffffu, v16[0], 1);
+      const bool valid = b0 + my_tok < tok1;
+      s = valid ? AT::round(AT::round(s) * scale) : -INFINITY;
+      const float bm = warp_max(s);
+      const float mnew = fmaxf(mrun, bm);
+      const float p = valid ? expf(s - mnew) : 0.f;
+      const float alpha = expf(mrun - mnew);
+      const float lsum = warp_sum((lane & 1) ? 0.f : p);
+      lrun = lrun * alpha + lsum;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) acc[e] *= alpha;
 #pragma unroll
       for (int j = 0; j < kPageTokens; ++j) {
-        kr[j] = *reinterpret_cast<const uint2*>(kpool + base + j * kHeadDim);
-        vr[j] = *reinterpret_cast<const uint2*>(vpool + base + j * kHeadDim);
+        const float pj = __shfl_sync(0xffffffffu, p, lane_of_token(j));
+        const Act* vh = reinterpret_cast<const Act*>(&vr[j]);
+        if (owner && b0 + j == pos) {
+#pragma unroll
+          for (int e = 0; e < 4; ++e) acc[e] = fmaf(pj, sm.vn[lane * 4 + e], acc[e]);
+        } else {
+#pragma unroll
+          for (int e = 0; e < 4; ++e) acc[e] = fmaf(pj, AT::to_f(vh[e]), acc[e]);
+        }
+      }
+      mrun = mnew;
+    }
+  } else {
+    // Token-split scan: warp r takes tokens r*TPW .. r*TPW+TPW-1 of every
+    // page for all NREP query heads of the group.  The reduce-scatter leaves
+    // lane pair (2i, 2i+1) with the score of (head i / TPW, token i % TPW);
+    // each warp keeps an online softmax per head, merged below.
+    float qa[NREP][4], oa[NREP][4];
+#pragma unroll
+    for (int hh = 0; hh < NREP; ++hh) {
+      const float4 v = *reinterpret_cast<const float4*>(&tss->q[hh][lane * 4]);
+      qa[hh][0] = v.x;
+      qa[hh][1] = v.y;
+      qa[hh][2] = v.z;
+      qa[hh][3] = v.w;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) oa[hh][e] = 0.f;
+    }
+    const int my_h = my_tok / TPW, my_t = my_tok % TPW;
+    float mh = -INFINITY, lh = 0.f;
+    for (int pg0 = 0; pg0 < npg; pg0 += TSG) {
+      if (pg0 > 0) {
+        if ((pg0 & 31) == 0) bt_lane = pg0 + lane < npg ? bt[pg_first + pg0 + lane] : 0;
+        load_group(pg0, bt_lane);
+      }
+#pragma unroll
+      for (int p = 0; p < TG; ++p) {
+        if (pg0 + p >= npg) break;
+        const int t0 = tok0 + (pg0 + p) * kPageTokens + r * TPW;  // this warp's first token
+        float v16[kPageTokens];
+#pragma unroll
+        for (int t = 0; t < TPW; ++t) {
+          const bool fresh = owner && t0 + t == pos;
+          const Act* kh = reinterpret_cast<const Act*>(&kg[p][t]);
+          float kf[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) kf[e] = fresh ? sm.kn[lane * 4 + e] : AT::to_f(kh[e]);
+#pragma unroll
+          for (int hh = 0; hh < NREP; ++hh) {
+            float d = 0.f;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) d = fmaf(qa[hh][e], kf[e], d);
+            v16[hh * TPW + t] = d;
+          }
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float send = (lane & 16) ? v16[i] : v16[i + 8];
+          const float keep = (lane & 16) ? v16[i + 8] : v16[i];
+          v16[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float send = (lane & 8) ? v16[i] : v16[i + 4];
+          const float keep = (lane & 8) ? v16[i + 4] : v16[i];
+          v16[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+        }
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+          const float send = (lane & 4) ? v16[i] : v16[i + 2];
+          const float keep = (lane & 4) ? v16[i + 2] : v16[i];
+          v16[i] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+        }
+        {
+          const float send = (lane & 2) ? v16[0] : v16[1];
+          const float keep = (lane & 2) ? v16[1] : v16[0];
+          v16[0] = keep + __shfl_xor_sync(0xffffffffu, send, 2);
+        }
+        float s = v16[0] + __shfl_xor_sync(0xffffffffu, v16[0], 1);
+        const bool valid = t0 + my_t < tok1;
+        s = valid ? AT::round(AT::round(s) * scale) : -INFINITY;
+        // the head's TPW tokens sit on lane bits 1 .. log2(TPW)
+        float bm = s;
+#pragma unroll
+        for (int k = 2; k < 2 * TPW; k <<= 1) bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, k));
+        const float mnew = fmaxf(mh, bm);
+        const float pr = valid ? expf(s - mnew) : 0.f;
+        const float alpha = mnew == -INFINITY ? 1.f : expf(mh - mnew);
+        float ls = pr;
+#pragma unroll
+        for (int k = 2; k < 2 * TPW; k <<= 1) ls += __shfl_xor_sync(0xffffffffu, ls, k);
+        lh = lh * alpha + ls;
+        mh = mnew;
+        float vf[TPW][4];
+#pragma unroll
+        for (int t = 0; t < TPW; ++t) {
+          const bool fresh = owner && t0 + t == pos;
+          const Act* vh = reinterpret_cast<const Act*>(&vg[p][t]);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) vf[t][e] = fresh ? sm.vn[lane * 4 + e] : AT::to_f(vh[e]);
+        }
+#pragma unroll
+        for (int hh = 0; hh < NREP; ++hh) {
+          const float ah = __shfl_sync(0xffffffffu, alpha, lane_of_token(hh * TPW));
+#pragma unroll
+          for (int e = 0; e < 4; ++e) oa[hh][e] *= ah;
+#pragma unroll
+          for (int t = 0; t < TPW; ++t) {
+            const float pj = __shfl_sync(0xffffffffu, pr, lane_of_token(hh * TPW + t));
+#pragma unroll
+            for (int e = 0; e < 4; ++e) oa[hh][e] = fmaf(pj, vf[t][e], oa[hh][e]);
+          }
+        }
       }
     }
-    float v16[kPageTokens];
+    // merge the warps' partials: warp r ends with query head r's (m, l, o)
 #pragma unroll
-    for (int j = 0; j < kPageTokens; ++j) {
-      const Act* kh = reinterpret_cast<const Act*>(&kr[j]);
-      float d = 0.f;
-      if (owner && b0 + j == pos) {
-#pragma unroll
-        for (int e = 0; e < 4; ++e) d = fmaf(q[e], sm.kn[lane * 4 + e], d);
-      } else {
-#pragma unroll
-        for (int e = 0; e < 4; ++e) d = fmaf(q[e], AT::to_f(kh[e]), d);
-      }
-      v16[j] = d;
+    for (int hh = 0; hh < NREP; ++hh)
+      *reinterpret_cast<float4*>(&tss->o[r][hh][lane * 4]) =
+          make_float4(oa[hh][0], oa[hh][1], oa[hh][2], oa[hh][3]);
+    if ((lane & 1) == 0 && my_t == 0) {
+      tss->ml[r][my_h][0] = mh;
+      tss->ml[r][my_h][1] = lh;
     }
-    // reduce-scatter: afterwards lane holds the full dot of token my_tok
+    group_sync();
+    float mx = -INFINITY;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const float send = (lane & 16) ? v16[i] : v16[i + 8];
-      const float keep = (lane & 16) ? v16[i + 8] : v16[i];
-      v16[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+    for (int w = 0; w < NREP; ++w) mx = fmaxf(mx, tss->ml[w][r][0]);
+#pragma unroll
+    for (int w = 0; w < NREP; ++w) {
+      const float mw = tss->ml[w][r][0];
+      const float wt = mw == -INFINITY ? 0.f : expf(mw - mx);
+      lrun = fmaf(wt, tss->ml[w][r][1], lrun);
+      const float4 ov = *reinterpret_cast<const float4*>(&tss->o[w][r][lane * 4]);
+      acc[0] = fmaf(wt, ov.x, acc[0]);
+      acc[1] = fmaf(wt, ov.y, acc[1]);
+      acc[2] = fmaf(wt, ov.z, acc[2]);
+      acc[3] = fmaf(wt, ov.w, acc[3]);
     }
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float send = (lane & 8) ? v16[i] : v16[i + 4];
-      const float keep = (lane & 8) ? v16[i + 4] : v16[i];
-      v16[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
-    }
-#pragma unroll
-    for (int i = 0; i < 2; ++i) {
-      const float send = (lane & 4) ? v16[i] : v16[i + 2];
-      const float keep = (lane & 4) ? v16[i + 2] : v16[i];
-      v16[i] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
-    }
-    {
-      const float send = (lane & 2) ? v16[0] : v16[1];
-      const float keep = (lane & 2) ? v16[1] : v16[0];
-      v16[0] = keep + __shfl_xor_sync(0xffffffffu, send, 2);
-    }
-    float s = v16[0] + __shfl_xor_sync(0xffffffffu, v16[0], 1);
-    const bool valid = b0 + my_tok < tok1;
-    s = valid ? AT::round(AT::round(s) * scale) : -INFINITY;
-    const float bm = warp_max(s);
-    const float mnew = fmaxf(mrun, bm);
-    const float p = valid ? expf(s - mnew) : 0.f;
-    const float alpha = expf(mrun - mnew);
-    const float lsum = warp_sum((lane & 1) ? 0.f : p);
-    lrun = lrun * alpha + lsum;
-#pragma unroll
-    for (int e = 0; e < 4; ++e) acc[e] *= alpha;
-#pragma unroll
-    for (int j = 0; j < kPageTokens; ++j) {
-      const float pj = __shfl_sync(0xffffffffu, p, lane_of_token(j));
-      const Act* vh = reinterpret_cast<const Act*>(&vr[j]);
-      if (owner && b0 + j == pos) {
-#pragma unroll
-        for (int e = 0; e < 4; ++e) acc[e] = fmaf(pj, sm.vn[lane * 4 + e], acc[e]);
-      } else {
-#pragma unroll
-        for (int e = 0; e < 4; ++e) acc[e] = fmaf(pj, AT::to_f(vh[e]), acc[e]);
-      }
-    }
-    mrun = mnew;
+    mrun = mx;
   }
 
   Act* out =

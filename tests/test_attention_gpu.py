@@ -34,6 +34,21 @@ def test_attention_decode_f16_long_context(cuda):
     assert_attn_close(got, ref, "f16")
 
 
+def test_attention_decode_many_rows_f16_long_context(cuda):
+    """More than 4 rows with groups of 4 query heads take the token-split
+    form (each warp scores a quarter of every page for the whole group):
+    long and one-token contexts, 16 splits, and a second call that
+    reproduces the first bit for bit."""
+    import dial_b200
+
+    case = PagedCase(32, 8, [1000, 513, 64, 0, 250, 1023, 31, 600], seed=6, dtype="f16")
+    (a, b), _, _ = run(case, cuda, 16, calls=2)
+    assert dial_b200.device_status() == 0
+    ref, _, _ = case.oracle()
+    assert_attn_close(a, ref, "f16")
+    np.testing.assert_array_equal(a, b)
+
+
 def test_attention_decode_repeat_calls_agree(cuda):
     """Scratch counters reset themselves: a second call (which re-appends the
     same K/V) reproduces the first bit for bit."""
