@@ -70,6 +70,18 @@ __global__ void __launch_bounds__(NREP * 32) attn_decode_cluster_kernel(const At
                                  threadIdx.x & 31, sm, 1, &cs);
 }
 
+// Cluster form with the token-split scan.
+template <typename Act, int NREP, int CL, int TSG>
+__global__ void __launch_bounds__(NREP * 32) attn_decode_cluster_ts_kernel(const AttnDecodeArgs a) {
+  pdl_launch_dependents();
+  __shared__ AttnItemSmem sm;
+  __shared__ AttnClusterSmem<NREP> cs;
+  __shared__ AttnTokSplitSmem<NREP> ts;
+  attn_item<Act, NREP, true, CL, 0, TSG>(a, blockIdx.z, blockIdx.x, blockIdx.y, threadIdx.x >> 5,
+                                         threadIdx.x & 31, sm, 1, &cs, nullptr, nullptr, nullptr,
+                                         &ts);
+}
+
 // Ring form (optionally clustered, CL > 0): NREP query warps + one producer
 // warp that streams each split's K/V pages through a shared-memory ring.
 constexpr int kRingPages = 4;
@@ -139,9 +151,16 @@ __global__ void iota_pos_kernel(int32_t* pos, int32_t* sid, int M, int p0) {
 
 // Launch of the cluster form with CL splits per cluster; false when this
 // device cannot hold such a cluster (the caller then takes the plain form).
-template <typename Act, int NREP, int CL, bool RING>
+template <typename Act, int NREP, int CL, bool RING, bool TS>
+constexpr auto cluster_kernel() {
+  if constexpr (RING) return attn_decode_ring_kernel<Act, NREP, CL>;
+  else if constexpr (TS) return attn_decode_cluster_ts_kernel<Act, NREP, CL, kTokSplitPages>;
+  else return attn_decode_cluster_kernel<Act, NREP, CL>;
+}
+
+template <typename Act, int NREP, int CL, bool RING, bool TS = false>
 bool launch_cluster(const AttnDecodeArgs& a, cudaStream_t s, bool pdl, cudaError_t& err) {
-  auto kern = RING ? attn_decode_ring_kernel<Act, NREP, CL> : attn_decode_cluster_kernel<Act, NREP, CL>;
+  auto kern = cluster_kernel<Act, NREP, CL, RING, TS>();
   static int usable = -1;  // per instantiation: checked once per process
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(a.sh.kv_heads, a.splits, a.M);
@@ -185,6 +204,14 @@ cudaError_t launch_decode_t(const AttnDecodeArgs& a, cudaStream_t s, bool pdl) {
     if (a.splits % 16 == 0 && launch_cluster<Act, NREP, 16, true>(a, s, pdl, err)) return err;
     if (a.splits % 8 == 0 && launch_cluster<Act, NREP, 8, true>(a, s, pdl, err)) return err;
   } else {
+    if constexpr (NREP == 4) {
+      if (a.tok_split >= 2) {
+        if (a.splits % 16 == 0 && launch_cluster<Act, NREP, 16, false, true>(a, s, pdl, err))
+          return err;
+        if (a.splits % 8 == 0 && launch_cluster<Act, NREP, 8, false, true>(a, s, pdl, err))
+          return err;
+      }
+    }
     if (a.splits % 16 == 0 && launch_cluster<Act, NREP, 16, false>(a, s, pdl, err)) return err;
     if (a.splits % 8 == 0 && launch_cluster<Act, NREP, 8, false>(a, s, pdl, err)) return err;
   }

@@ -53,10 +53,11 @@ struct AttnDecodeArgs {
   // 1: a producer warp streams each split's K/V pages through a shared-memory
   // ring (bulk copies); 0: every query warp loads its pages into registers.
   int page_ring;
-  // 1 (register form, steps of more than 4 rows, 4 query heads per kv head):
-  // the group's warps split each page's tokens between them, each scoring
-  // its tokens for every query head of the group, and merge their partials
-  // in shared memory; 0: every warp reads every token for its own head.
+  // Groups of 4 query heads, register form: the group's warps split each
+  // page's tokens between them, each scoring its tokens for every query head
+  // of the group, and merge their partials in shared memory.  1: for steps
+  // of more than 4 rows; 2: also for the cluster-merge form of 4 rows or
+  // fewer; 0: every warp reads every token for its own head.
   int tok_split;
 };
 

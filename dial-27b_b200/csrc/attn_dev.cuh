@@ -319,8 +319,8 @@ __device__ void attn_item(const AttnDecodeArgs& a, int m, int kvh, int split, in
                           AttnItemSmem& sm, int bar_id, AttnClusterSmem<NREP>* csm = nullptr,
                           const uint8_t* ring = nullptr, uint64_t* rfull = nullptr,
                           uint64_t* rempty = nullptr, AttnTokSplitSmem<NREP>* tss = nullptr) {
-  static_assert(TSG == 0 || (CL == 0 && RING == 0 && kPageTokens % NREP == 0 && 32 % (TSG > 0 ? TSG : 1) == 0),
-                "token split: register pages, no cluster, NREP | 16, TSG | 32");
+  static_assert(TSG == 0 || (RING == 0 && kPageTokens % NREP == 0 && 32 % (TSG > 0 ? TSG : 1) == 0),
+                "token split: register pages, NREP | 16, TSG | 32");
   using AT = ActTraits<Act>;
   const int QH = a.sh.q_heads, KVH = a.sh.kv_heads;
   const int h = kvh * NREP + r;

@@ -301,7 +301,7 @@ GemvTuning g_tuning() {
   if (const char* v = std::getenv("DIAL_B200_ATTN_MIN_SPLIT")) t.attn_min_split = std::atoi(v);
   if (const char* v = std::getenv("DIAL_B200_ATTN_TC")) t.attn_tc = std::atoi(v) != 0;
   if (const char* v = std::getenv("DIAL_B200_ATTN_RING")) t.attn_ring = std::atoi(v) != 0;
-  if (const char* v = std::getenv("DIAL_B200_ATTN_TOKSPLIT")) t.attn_tok_split = std::atoi(v) != 0;
+  if (const char* v = std::getenv("DIAL_B200_ATTN_TOKSPLIT")) t.attn_tok_split = std::atoi(v);
   return t;
 }
 
@@ -693,7 +693,7 @@ AttnDecodeArgs decode_attn_args(dial_b200_engine* e, LayerW& L, int M) {
   // at 2048-token context, -11 % on the 27B shapes; with many rows the
   // register form packs more CTAs per SM)
   a.page_ring = g_tuning().attn_ring && M <= 4 ? 1 : 0;
-  a.tok_split = g_tuning().attn_tok_split ? 1 : 0;
+  a.tok_split = g_tuning().attn_tok_split;
   return a;
 }
 

@@ -42,7 +42,7 @@ struct GemvTuning {
   int attn_min_split = 0;    // decode attention: context tokens per split at least (0 = 16)
   bool attn_tc = true;       // prefill attention on the tensor cores when supported
   bool attn_ring = false;    // decode attention pages through a shared-memory ring (opt-in)
-  bool attn_tok_split = true;  // decode attention (many rows): warps split each page's tokens
+  int attn_tok_split = 1;  // decode attention: warps split each page's tokens (AttnDecodeArgs)
 };
 
 // act: 0 = bf16, 1 = f16.  Launches ceil(M/8) kernels on `stream`.
