@@ -442,7 +442,7 @@ def _relaunch_with_torchrun(args) -> None:
 
 
 def run_prefill2048(args) -> dict:
-    """BASELINE config 3 on one GPU: prefill of 2048 seeded token ids (TTFT,
+    """Long-prompt workload on one GPU: prefill of 2048 seeded token ids (TTFT,
     first token on the host), then bs1 greedy decode of 256 tokens."""
     import torch
 
@@ -492,7 +492,7 @@ def run_prefill2048(args) -> dict:
 
 
 def run_ragged32(args) -> dict:
-    """BASELINE config 4 on one GPU: 32 sessions with KV lengths uniform in
+    """Ragged multi-session workload on one GPU: 32 sessions with KV lengths uniform in
     [128, 8192] (seed 2) in 16-token pages, one decode token per session per
     iteration (device loop)."""
     import numpy as np
@@ -544,7 +544,7 @@ def run_ragged32(args) -> dict:
 
 
 def run_quant27b(args, fmt_name: str) -> dict:
-    """BASELINE config 5 on one GPU: the 27B-class dense decoder (64 layers,
+    """27B-class workload on one GPU: the dense decoder (64 layers,
     hidden 5120, 40 q / 8 kv heads, FFN 21504) with FP8 block-128 or NVFP4
     linears, prefill of 4096 seeded tokens (TTFT) then bs1 greedy decode."""
     import torch
@@ -626,9 +626,10 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--workload", default="decode",
                     choices=["decode", "prefill2048", "ragged32", "fp8_27b", "nvfp4_27b"],
-                    help="decode (BASELINE config 1, the headline), prefill2048 (config 3 on one "
-                         "GPU), ragged32 (config 4 on one GPU), fp8_27b / nvfp4_27b (config 5 on "
-                         "one GPU)")
+                    help="decode (bs1 Qwen3-8B W8A16 decode, the headline metric), prefill2048 "
+                         "(2048-token prefill then decode), ragged32 (32 ragged sessions), "
+                         "fp8_27b / nvfp4_27b (27B-class decoder with FP8 block-128 or NVFP4 "
+                         "linears); all on one GPU")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -126,7 +126,7 @@ def test_layer_prefill_on_tensor_cores(cuda, gemv_only):
 
 @pytest.mark.parametrize("K,N,M", [(5120, 1024, 64), (1024, 384, 200), (4096, 6144, 96)])
 def test_gemm_fp8_block128_vs_oracle(cuda, K, N, M):
-    """FP8 e4m3 with 128x128 block scales on the tensor
+    """FP8 e4m3 with 128x128 block scales (the 27B-class format) on the tensor
     cores: the block scale is folded into the f16 operand (relative error
     <= 2^-11 per weight), so the bound is max |d| <= 2^-7 max|y| + 1e-3 and
     98% of outputs within 1 bf16 ulp (measured 98.3% at K=5120)."""

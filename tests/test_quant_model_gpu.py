@@ -1,4 +1,4 @@
-"""27B-class formats end to end (BASELINE config 5 at test size): engines
+"""27B-class formats end to end (at test size): engines
 whose linears are FP8 e4m3 with 128x128 block scales or NVFP4 (e2m1 + e4m3
 group scale + f32 global), synthesised and quantised on the device, against
 the oracle model whose linears are the same weights quantised by the CPU
