@@ -66,6 +66,13 @@ size_t attn_decode_scratch_bytes(const AttnShape& sh, int M, int splits);
 
 cudaError_t attn_decode_launch(const AttnDecodeArgs& a, int act, cudaStream_t s, bool pdl);
 
+// Status word of dial_b200_attention_decode_noalloc on device `dev` (0 when
+// that entry point never ran there): read into *out and, with `clear`, set to
+// zero; clearing a non-zero status also re-zeroes that entry point's split
+// counters, which a call that gave up early may have left non-zero.  Allocates
+// nothing.
+cudaError_t noalloc_status(int dev, bool clear, int* out);
+
 // Prefill of one session: M tokens at positions p0 .. p0+M-1.
 struct AttnPrefillArgs {
   AttnShape sh;

@@ -18,6 +18,14 @@
 // belongs before any stream capture.  Calls that overlap in time on one
 // device (two streams, two host threads) share the one scratch and race;
 // serialize them.
+//
+// Device-side status (a position outside the KV capacity, a bounded wait that
+// expired) goes to the status word inside the scratch; dial_b200_device_status
+// reports it (noalloc_status below) and, when asked to clear it, also
+// re-zeroes the split counters, since a call that gave up early can leave
+// them non-zero.  The call uses the same kernel forms as
+// dial_b200_attention_decode (page ring for steps of up to 4 rows, token split
+// for more rows in groups of 4 query heads).
 #include <cuda_runtime.h>
 
 #include <cstdarg>
@@ -79,6 +87,27 @@ cudaError_t scratch_for_device(int dev, NoAllocScratch** out) {
 }
 
 }  // namespace
+
+cudaError_t noalloc_status(int dev, bool clear, int* out) {
+  *out = 0;
+  if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+  NoAllocScratch* s = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(g_setup_mu);
+    s = g_addr[dev];
+  }
+  if (!s) return cudaSuccess;
+  int v = 0;
+  cudaError_t e = cudaMemcpy(&v, &s->status, sizeof(int), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return e;
+  *out = v;
+  if (clear && v != 0) {
+    e = cudaMemset(s->counters, 0, sizeof(s->counters) + sizeof(s->status));
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  }
+  return e;
+}
+
 }  // namespace dialb200
 
 using namespace dialb200;
@@ -154,6 +183,8 @@ extern "C" int dial_b200_attention_decode_noalloc(
   a.part_ml = s->part_ml;
   a.counters = s->counters;
   a.status = &s->status;
+  a.page_ring = 1;
+  a.tok_split = 1;
   e = attn_decode_launch(a, sh->act, static_cast<cudaStream_t>(stream), false);
   if (e != cudaSuccess)
     return fail(err, n, DIAL_ERR_CUDA, "attention launch failed: %s", cudaGetErrorString(e));

@@ -21,7 +21,6 @@
 #include "gemv.h"
 #include "layout.h"
 #include "misc.h"
-#include "step.h"
 
 using namespace dialb200;
 
@@ -73,13 +72,14 @@ int guarded(char* err, size_t n, F&& f) {
   }
 }
 
-// Device status word, one per device, allocated on first use.
-int* device_status_word() {
+// Device status word, one per device, allocated on first use (`create`); the
+// reader passes create = false and sees nullptr on a device that has none.
+int* device_status_word(bool create = true) {
   static int* words[64] = {nullptr};
   int dev = 0;
   DIAL_CUDA(cudaGetDevice(&dev));
   if (dev < 0 || dev >= 64) throw Error{DIAL_ERR_INVALID, "device index out of range"};
-  if (!words[dev]) {
+  if (!words[dev] && create) {
     DIAL_CUDA(cudaMalloc(&words[dev], sizeof(int)));
     DIAL_CUDA(cudaMemset(words[dev], 0, sizeof(int)));
   }
@@ -296,7 +296,6 @@ GemvTuning g_tuning() {
   if (const char* v = std::getenv("DIAL_B200_GEMV_SLOTS")) t.slots = std::atoi(v);
   if (const char* v = std::getenv("DIAL_B200_GEMV_GRID")) t.grid = std::atoi(v);
   if (const char* v = std::getenv("DIAL_B200_PDL")) t.pdl = std::atoi(v) != 0;
-  if (const char* v = std::getenv("DIAL_B200_STEP_KERNEL")) t.step_kernel = std::atoi(v) != 0;
   if (const char* v = std::getenv("DIAL_B200_GEMM_MIN_ROWS")) t.gemm_min_rows = std::atoi(v);
   if (const char* v = std::getenv("DIAL_B200_ATTN_MIN_SPLIT")) t.attn_min_split = std::atoi(v);
   if (const char* v = std::getenv("DIAL_B200_ATTN_TC")) t.attn_tc = std::atoi(v) != 0;
@@ -389,15 +388,6 @@ struct Graph {
   }
 };
 
-// Op program of the persistent decode-step kernel for one row count.
-struct StepProgram {
-  int M = 0, n_ops = 0, grid = 0, nrep = 0;
-  StepPlan plan{};
-  DevBuf ops, bar, tile_cnt, tile_part;
-  DevBuf trace;          // DIAL_B200_STEP_TRACE=<file>: per-op timestamps of the last launch
-  std::string trace_path;
-};
-
 }  // namespace
 
 struct dial_b200_engine {
@@ -420,7 +410,6 @@ struct dial_b200_engine {
   int32_t* h_out = nullptr;  // pinned: [max_rows] tokens + status
   int* status = nullptr;
   std::map<int64_t, std::unique_ptr<Graph>> step_graphs, loop_graphs;
-  std::unique_ptr<StepProgram> step_prog;  // built on first use, dropped with the graphs
   // pipeline-stage decode graphs keyed by (rows, tokens in, hidden, tokens out)
   std::map<std::tuple<int64_t, const void*, const void*, const void*>, std::unique_ptr<Graph>>
       stage_graphs;
@@ -820,146 +809,11 @@ void require_full_model(dial_b200_engine* e) {
   DIAL_CHECK(e->lm_head.ready(), "lm_head weights not loaded");
 }
 
-// The persistent step kernel covers a full model whose layer linears are
-// W8A16 or FP8-row and whose lm_head is dense, W8A16 or FP8-row (1 KB chunks).
-bool step_kernel_usable(dial_b200_engine* e, int M) {
-  if (!g_tuning().step_kernel || M < 1 || M > kStepMaxM) return false;
-  if (!(e->cfg.has_embed && e->cfg.has_head && e->cfg.first_layer == 0 &&
-        e->cfg.num_layers == e->cfg.num_hidden_layers))
-    return false;
-  const int rep = e->QH / e->KVH;
-  if (!(rep == 1 || rep == 2 || rep == 4 || rep == 5 || rep == 8)) return false;
-  auto ok_fmt = [](const Linear& L, bool head) {
-    const int f = L.d.fmt;
-    return L.ready() && (f == kFmtW8A16Row || f == kFmtFp8Row || (head && f == kFmtDense));
-  };
-  int kmax = 0;
-  for (auto& L : e->layers) {
-    if (!ok_fmt(L.qkv, false) || !ok_fmt(L.o, false) || !ok_fmt(L.gate_up, false) ||
-        !ok_fmt(L.down, false))
-      return false;
-    kmax = std::max({kmax, L.qkv.d.K_pad, L.o.d.K_pad, L.gate_up.d.K_pad, L.down.d.K_pad});
-  }
-  if (!ok_fmt(e->lm_head, true)) return false;
-  kmax = std::max(kmax, e->lm_head.d.K_pad);
-  return step_plan(kmax, M).slots >= 4;
-}
-
-StepProgram* get_step_program(dial_b200_engine* e, int M) {
-  if (e->step_prog && e->step_prog->M == M) return e->step_prog.get();
-  auto p = std::make_unique<StepProgram>();
-  p->M = M;
-  std::vector<StepOp> ops;
-  int kmax = 0, tmax = 1;
-  auto gemv = [&](const Linear& L, const void* x, int x_ld, const void* norm, void* out,
-                  int out_ld, int epi) {
-    StepOp o{};
-    o.kind = kOpGemv;
-    o.epi = epi;
-    o.w = L.d;
-    o.x = x;
-    o.x_ld = x_ld;
-    o.norm_w = norm;
-    o.out = out;
-    o.out_ld = out_ld;
-    o.S = (L.d.C + 15) / 16;
-    kmax = std::max(kmax, L.d.K_pad);
-    tmax = std::max(tmax, L.d.T);
-    ops.push_back(o);
-  };
-  {
-    StepOp o{};
-    o.kind = kOpEmbed;
-    ops.push_back(o);
-  }
-  for (auto& L : e->layers) {
-    gemv(L.qkv, e->hidden.p, e->H, L.input_norm.p, e->qkv.p, e->QKV, kEpiStore);
-    StepOp at{};
-    at.kind = kOpAttn;
-    at.attn = decode_attn_args(e, L, M);
-    ops.push_back(at);
-    gemv(L.o, e->attn.p, e->QH * e->D, nullptr, e->hidden.p, e->H, kEpiResidual);
-    gemv(L.gate_up, e->hidden.p, e->H, L.post_norm.p, e->inter.p, e->I, kEpiSwiglu);
-    gemv(L.down, e->inter.p, e->I, nullptr, e->hidden.p, e->H, kEpiResidual);
-  }
-  gemv(e->lm_head, e->hidden.p, e->H, e->final_norm.p, nullptr, e->V, kEpiArgmax);
-  int sms = 0;
-  DIAL_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, e->device));
-  p->grid = sms;
-  p->nrep = e->QH / e->KVH;
-  p->plan = step_plan(kmax, M);
-  DIAL_CHECK(p->plan.slots >= 4, "step kernel plan does not fit shared memory");
-  p->n_ops = static_cast<int>(ops.size());
-  p->ops.alloc(ops.size() * sizeof(StepOp));
-  DIAL_CUDA(cudaMemcpy(p->ops.p, ops.data(), p->ops.bytes, cudaMemcpyHostToDevice));
-  p->bar.alloc(64);
-  DIAL_CUDA(cudaMemset(p->bar.p, 0, 64));
-  p->tile_cnt.alloc(static_cast<size_t>(tmax) * 4);
-  DIAL_CUDA(cudaMemset(p->tile_cnt.p, 0, p->tile_cnt.bytes));
-  p->tile_part.alloc(static_cast<size_t>(p->grid) * 2 * 128 * 4);
-  if (const char* tp = std::getenv("DIAL_B200_STEP_TRACE")) {
-    p->trace_path = tp;
-    p->trace.alloc(static_cast<size_t>(p->n_ops) * kTraceFields * 8);
-    DIAL_CUDA(cudaMemset(p->trace.p, 0, p->trace.bytes));
-  }
-  e->step_prog = std::move(p);
-  return e->step_prog.get();
-}
-
-void launch_step_program(dial_b200_engine* e, StepProgram* p, bool loop, cudaStream_t s) {
-  StepArgs a{};
-  a.ops = static_cast<const StepOp*>(p->ops.p);
-  a.n_ops = p->n_ops;
-  a.M = p->M;
-  a.eps = e->cfg.rms_norm_eps;
-  a.embed = e->embed.p;
-  a.vocab = e->V;
-  a.H = e->H;
-  a.tok_in = e->tok_in.as<int32_t>();
-  a.hidden = e->hidden.p;
-  a.bar = static_cast<unsigned int*>(p->bar.p);
-  a.tile_cnt = p->tile_cnt.as<int>();
-  a.tile_part = p->tile_part.as<float>();
-  a.amax_key = e->amax_key.as<unsigned long long>();
-  a.amax_count = e->amax_count.as<int>();
-  a.tok_out = e->tok_out.as<int32_t>();
-  a.tok_loop = loop ? e->tok_in.as<int32_t>() : nullptr;
-  a.pos_loop = loop ? e->pos.as<int32_t>() : nullptr;
-  a.status = e->status;
-  a.trace = p->trace.p ? p->trace.as<unsigned long long>() : nullptr;
-  if (a.trace) DIAL_CUDA(cudaMemsetAsync(p->trace.p, 0, p->trace.bytes, s));
-  DIAL_CUDA(cudaMemsetAsync(p->bar.p, 0, 4, s));
-  DIAL_CUDA(step_launch(a, p->plan, e->cfg.act, p->nrep, p->grid, s));
-}
-
-// Per-op timing of the last step-kernel launch, one CSV line per op: the
-// latest CTA start, latest end of staging, latest and earliest CTA end, in ns
-// from the first op's latest start.
-void dump_step_trace(StepProgram* p) {
-  std::vector<unsigned long long> t(static_cast<size_t>(p->n_ops) * kTraceFields);
-  std::vector<StepOp> ops(p->n_ops);
-  DIAL_CUDA(cudaMemcpy(t.data(), p->trace.p, t.size() * 8, cudaMemcpyDeviceToHost));
-  DIAL_CUDA(cudaMemcpy(ops.data(), p->ops.p, ops.size() * sizeof(StepOp), cudaMemcpyDeviceToHost));
-  FILE* f = std::fopen(p->trace_path.c_str(), "w");
-  if (!f) return;
-  const unsigned long long t0 = t[0];
-  std::fprintf(f, "op,kind,epi,N,K,start_max,staged_max,end_max,end_min\n");
-  for (int k = 0; k < p->n_ops; ++k) {
-    const unsigned long long* r = &t[static_cast<size_t>(k) * kTraceFields];
-    auto rel = [&](unsigned long long v) { return v ? static_cast<long long>(v - t0) : -1ll; };
-    std::fprintf(f, "%d,%d,%d,%d,%d,%lld,%lld,%lld,%lld\n", k, ops[k].kind, ops[k].epi, ops[k].w.N,
-                 ops[k].w.K, rel(r[0]), rel(r[1]), rel(r[2]),
-                 r[3] ? static_cast<long long>(kTraceBig - r[3] - t0) : -1ll);
-  }
-  std::fclose(f);
-}
-
 void drop_graphs(dial_b200_engine* e) {
   cudaStreamSynchronize(e->stream);
   e->step_graphs.clear();
   e->loop_graphs.clear();
   e->stage_graphs.clear();
-  e->step_prog.reset();
 }
 
 Graph* get_graph(dial_b200_engine* e, int M, bool loop) {
@@ -968,8 +822,6 @@ Graph* get_graph(dial_b200_engine* e, int M, bool loop) {
   if (it != map.end()) return it->second.get();
   cudaStream_t s = e->stream;
   auto g = std::make_unique<Graph>();
-  // the program's buffers are allocated before the capture starts
-  StepProgram* prog = step_kernel_usable(e, M) ? get_step_program(e, M) : nullptr;
   DIAL_CUDA(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
   try {
     if (!loop) {
@@ -977,14 +829,10 @@ Graph* get_graph(dial_b200_engine* e, int M, bool loop) {
       DIAL_CUDA(cudaMemcpyAsync(e->sid.p, e->h_in + M, M * 4, cudaMemcpyHostToDevice, s));
       DIAL_CUDA(cudaMemcpyAsync(e->pos.p, e->h_in + 2 * M, M * 4, cudaMemcpyHostToDevice, s));
     }
-    if (prog) {
-      launch_step_program(e, prog, loop, s);
-    } else {
-      step_body(e, M, s);
-      if (loop)
-        DIAL_CUDA(advance_launch(e->tok_out.as<int32_t>(), e->tok_in.as<int32_t>(),
-                                 e->pos.as<int32_t>(), M, s, g_tuning().pdl));
-    }
+    step_body(e, M, s);
+    if (loop)
+      DIAL_CUDA(advance_launch(e->tok_out.as<int32_t>(), e->tok_in.as<int32_t>(),
+                               e->pos.as<int32_t>(), M, s, g_tuning().pdl));
     if (!loop) {
       DIAL_CUDA(cudaMemcpyAsync(e->h_out, e->tok_out.p, M * 4, cudaMemcpyDeviceToHost, s));
       DIAL_CUDA(cudaMemcpyAsync(e->h_out + M, e->status, 4, cudaMemcpyDeviceToHost, s));
@@ -1037,11 +885,17 @@ uint32_t dial_b200_abi_version(void) { return DIAL_B200_ABI_VERSION; }
 
 int dial_b200_device_status(int* status_out, int clear, char* err, size_t n) {
   return guarded(err, n, [&] {
-    int* w = device_status_word();
+    int dev = 0;
+    DIAL_CUDA(cudaGetDevice(&dev));
+    int* w = device_status_word(false);
     int v = 0;
-    DIAL_CUDA(cudaMemcpy(&v, w, 4, cudaMemcpyDeviceToHost));
-    if (status_out) *status_out = v;
-    if (clear) DIAL_CUDA(cudaMemset(w, 0, 4));
+    if (w) {
+      DIAL_CUDA(cudaMemcpy(&v, w, 4, cudaMemcpyDeviceToHost));
+      if (clear) DIAL_CUDA(cudaMemset(w, 0, 4));
+    }
+    int v_noalloc = 0;
+    DIAL_CUDA(noalloc_status(dev, clear != 0, &v_noalloc));
+    if (status_out) *status_out = v != 0 ? v : v_noalloc;
   });
 }
 
@@ -1204,7 +1058,6 @@ void dial_b200_engine_destroy(dial_b200_engine* eng) {
   cudaStreamSynchronize(eng->stream);
   eng->step_graphs.clear();
   eng->loop_graphs.clear();
-  eng->step_prog.reset();
   eng->stage_graphs.clear();
   if (eng->h_in) cudaFreeHost(eng->h_in);
   if (eng->h_out) cudaFreeHost(eng->h_out);
@@ -1448,7 +1301,6 @@ int dial_b200_decode_loop_state(dial_b200_engine* eng, int64_t rows, int32_t* to
     if (pos) DIAL_CUDA(cudaMemcpy(pos, eng->pos.p, rows * 4, cudaMemcpyDeviceToHost));
     int st = 0;
     DIAL_CUDA(cudaMemcpy(&st, eng->status, 4, cudaMemcpyDeviceToHost));
-    if (eng->step_prog && eng->step_prog->trace.p) dump_step_trace(eng->step_prog.get());
     check_status(eng, st);
   });
 }

@@ -37,7 +37,6 @@ struct GemvTuning {
   int slots = 0;   // ring stages (0 = as many as fit)
   int grid = 0;    // CTAs (0 = one per SM)
   bool pdl = true; // programmatic dependent launch
-  bool step_kernel = false;  // whole decode step as one persistent kernel when supported
   int gemm_min_rows = 16;    // rows from which linears take the tcgen05 GEMM (0 = never)
   int attn_min_split = 0;    // decode attention: context tokens per split at least (0 = 16)
   bool attn_tc = true;       // prefill attention on the tensor cores when supported

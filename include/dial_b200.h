@@ -53,9 +53,12 @@ extern "C" {
 /* Library version; replaces nothing (the reference links statically). */
 uint32_t dial_b200_abi_version(void);
 
-/* Read (and optionally clear) the device status word of the current device.
+/* Read (and optionally clear) the device status of the current device.
  * A non-zero value names the first bounded wait that expired or the first
- * out-of-range index a kernel saw since the last clear. */
+ * out-of-range index a kernel saw since the last clear: the word shared by
+ * the engines and the scratch-taking ops, else the word of
+ * dial_b200_attention_decode_noalloc (clearing also resets that entry
+ * point's split counters).  Synchronizes; allocates nothing. */
 int dial_b200_device_status(int* status_out, int clear, char* err, size_t err_size);
 
 /* ------------------------------------------------------------------------ */
@@ -152,8 +155,11 @@ int dial_b200_attention_decode(const dial_b200_attn_shape* sh, const void* qkv, 
  * kv_heads > DIAL_B200_NOALLOC_MAX_COUNTERS.  The first call on a device sets
  * the scratch up (address lookup, zero fill, a synchronize): make it before
  * any stream capture.  Calls that overlap in time on one device share the
- * scratch and race: serialize them.  Device-side status of this entry point
- * goes to its own static word, which dial_b200_device_status does not read. */
+ * scratch and race: serialize them.  It runs the same kernel forms as
+ * dial_b200_attention_decode.  Device-side status of this entry point (for
+ * instance a position outside max_pos: that row's KV append is skipped) is
+ * reported by dial_b200_device_status; after a non-zero status, clear it
+ * there before the next call, which also re-zeroes the split counters. */
 int dial_b200_attention_decode_noalloc(const dial_b200_attn_shape* sh, const void* qkv,
                                        int64_t qkv_ld, const void* q_norm_w, const void* k_norm_w,
                                        const void* cos, const void* sin, void* k_pages,
@@ -301,8 +307,7 @@ int dial_b200_session_fill_random(dial_b200_engine* eng, int32_t session, int64_
                                   size_t err_size);
 
 /* Number of kernels one device-loop decode step launches for `rows` rows,
- * counted as the kernel nodes of the captured step graph (1 when the
- * persistent step kernel runs the step); -1 on error. */
+ * counted as the kernel nodes of the captured step graph; -1 on error. */
 int64_t dial_b200_step_kernel_count(dial_b200_engine* eng, int64_t rows);
 
 /* Number of kernels dial_b200_generate launches for a prompt of `n_prompt`

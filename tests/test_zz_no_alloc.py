@@ -61,3 +61,60 @@ def test_noalloc_at_the_limit_and_beyond(cuda):
     sh = A.make_shape(32, 8, case.max_blocks, case.max_pos)
     with pytest.raises(dial_b200.DialError, match="static scratch limit of 2048"):
         A.attention_decode_noalloc(sh, splits=17, **dev)
+
+
+STATUS_BAD_ARGS = 0x104  # kStatusBadArgs (csrc/common.cuh)
+
+
+def test_noalloc_host_rejection_leaves_device_status_clear(cuda):
+    """An argument the host side rejects never reaches the GPU: the call
+    raises, writes nothing and leaves the device status at zero."""
+    import dial_b200
+    from dial_b200 import attention as A
+
+    dial_b200.device_status(clear=True)
+    case = PagedCase(32, 8, [100, 5], seed=5)
+    dev = case.device(cuda)
+    sh = A.make_shape(32, 8, case.max_blocks, case.max_pos)
+    with pytest.raises(dial_b200.DialError, match="splits 0 outside"):
+        A.attention_decode_noalloc(sh, splits=0, **dev)
+    bad_shape = A.make_shape(32, 6, case.max_blocks, case.max_pos)
+    with pytest.raises(dial_b200.DialError, match="multiple of kv_heads"):
+        A.attention_decode_noalloc(bad_shape, splits=4, **dev)
+    torch.cuda.synchronize()
+    assert dial_b200.device_status() == 0
+    assert not bool(torch.any(dev["out"] != 0))
+
+
+def test_noalloc_position_beyond_capacity_reports_status(cuda):
+    """A row at a position outside max_pos: the kernel records the bad-argument
+    status and skips that row's KV append (the other row appends normally);
+    dial_b200_device_status reports the status of this entry point, clearing
+    it resets the static split counters, and the next calls match the scratch
+    entry point again."""
+    import dial_b200
+    from dial_b200 import attention as A
+
+    dial_b200.device_status(clear=True)
+    case = PagedCase(32, 8, [200, 40], seed=6, max_pos=512)
+    dev = case.device(cuda)
+    sh = A.make_shape(32, 8, case.max_blocks, case.max_pos)
+    k0, v0 = dev["k_pages"].clone(), dev["v_pages"].clone()
+    bad = dev["positions"].clone()
+    bad[1] = case.max_pos
+    A.attention_decode_noalloc(sh, splits=8, **{**dev, "positions": bad})
+    torch.cuda.synchronize()
+    assert dial_b200.device_status() == STATUS_BAD_ARGS
+    # only row 0's slot (position 200 of session 0) changed in the pages
+    b0, t0 = int(case.block_table[0, 200 // 16]), 200 % 16
+    for new, old in ((dev["k_pages"], k0), (dev["v_pages"], v0)):
+        changed = (new != old).any(dim=3).any(dim=1)  # [blocks, 16 tokens]
+        assert bool(changed[b0, t0])
+        changed[b0, t0] = False
+        assert not bool(changed.any())
+    assert dial_b200.device_status(clear=True) == STATUS_BAD_ARGS
+    assert dial_b200.device_status() == 0
+    want, got, _, _ = _both(case, cuda, 8)
+    for g in got:
+        np.testing.assert_allclose(g, want, rtol=2 ** -7, atol=1e-3)
+    assert dial_b200.device_status() == 0
