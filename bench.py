@@ -2,18 +2,21 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-One step = one decode token through embed -> 36 W8A16 decoder layers
-(RMSNorm + fused QKV GEMV + q/k-norm + RoPE + paged split-KV attention +
-o_proj + fused gate/up SwiGLU + down) -> ln_f -> bf16 lm_head -> argmax.
-Weights are seeded random-init N(0, 0.02) bf16 quantized to int8 at load
-(8.2 GB streamed per token, far larger than L2); the context starts from a
-128-token prompt (seed 1) prefilled before timing.
+One step = the greedy decode of BASELINE config 1: 128 tokens (positions
+128..255) after the 128-token seed-1 prompt, each token through embed -> 36
+W8A16 decoder layers (RMSNorm + fused QKV GEMV + q/k-norm + RoPE + paged
+split-KV attention + o_proj + fused gate/up SwiGLU + down) -> ln_f -> bf16
+lm_head -> argmax.  Weights are seeded random-init N(0, 0.02) bf16 quantized
+to int8 at load (8.2 GB streamed per token, far larger than L2); the prompt is
+prefilled before timing and every step restarts from its first token.
 
 ``value`` is tok/s of the device-resident decode loop (CUDA-graph replays,
-CUDA events on the engine stream).  ``e2e`` is the same metric through the
-public C ABI call dial_b200_decode_step with host token buffers (H2D of the
-token/session/position, D2H of the next token + status inside the timed
-region).  ``roofline`` reports the dominant kernel (the fused gate/up W8A16
+CUDA events on the engine stream around each step's 128 tokens).  ``e2e`` is
+the same metric through the public C ABI call dial_b200_decode_step with host
+token buffers (H2D of the token/session/position, D2H of the next token +
+status inside the timed region), 128 calls per step.  ``tokens`` carries the
+sha256 of the first 32 greedy tokens and how many of them equal the oracle's
+(tests/golden/config1_qwen3_8b_w8a16.npz).  ``roofline`` reports the dominant kernel (the fused gate/up W8A16
 GEMV) timed live with CUDA events on the engine stream.  With --gpus N > 1
 (torchrun) the 36 layers are split into N pipeline stages that hand the
 hidden state to the next GPU with NCCL send/recv.
@@ -35,12 +38,17 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT / "dial-27b_b200"))
 
 PROMPT_LEN = 128
+GEN_TOKENS = 128      # config 1: greedy decode of 128 tokens per step
+CHECK_TOKENS = 32     # north_star: the first 32 greedy tokens are checked
 WORKLOAD = "qwen3-8b-w8a16-bs1-decode"
+METRIC = "decode tok/s (bs1, Qwen3-8B W8A16)"
+GOLDEN = ROOT / "tests" / "golden" / "config1_qwen3_8b_w8a16.npz"
 # DRAM bytes (read + write) of one launch of the W8A16 GEMV on the fused gate/up weight
-# (N=24576, K=4096, M=1), from an `ncu --set full` capture of the same kernel and weight shape
-# with the store epilogue.
-GATE_UP_TRAFFIC_BYTES = 100_804_864 + 3_187_968
-GATE_UP_TRAFFIC_SOURCE = "ncu dram__bytes_read+write, gemv_kernel<bf16,W8A16,store> N=24576 K=4096 M=1"
+# (N=24576, K=4096, M=1) with the decode step's fused RMSNorm + SwiGLU epilogue, from an ncu
+# capture of that kernel variant (profiles/gemv_w8a16_gate_up_m1_swiglu_norm.md).
+GATE_UP_TRAFFIC_BYTES = 100_844_544 + 588_032
+GATE_UP_TRAFFIC_SOURCE = ("ncu dram__bytes_read+write, gemv_kernel<bf16,W8A16,SwiGLU,norm> "
+                          "N=24576 K=4096 M=1 (decode-step variant, replayed over 4 layers)")
 
 
 def load_peaks() -> dict:
@@ -114,73 +122,122 @@ class ClockSampler:
 
 
 # ----------------------------------------------------------------- CPU leg
-def cpu_decode_sample(budget_s: float = 20.0) -> dict:
-    """Time the CPU oracle on a bounded sample of the same decode step: whole
-    decoder layers of Qwen3-8B shape (W8A16, one token at context 128) plus
-    one lm_head, scaled to a full 36-layer token."""
-    sys.path.insert(0, str(ROOT / "oracle"))
+def headline_config(parallelism: str, world: int = 1) -> dict:
+    """The `config` of the headline line; both arms print the same dict."""
+    cfg = {"workload": WORKLOAD, "prompt_len": PROMPT_LEN, "gen_tokens_per_step": GEN_TOKENS,
+           "batch": 1, "layers": 36, "hidden": 4096, "linear": "W8A16 row int8 + f32 scale",
+           "lm_head": "bf16 dense", "parallelism": parallelism,
+           "l2": "inputs larger than L2 (8.2 GB weights streamed per token)"}
+    if world > 1:
+        from dial_b200.pipeline import plan_stages
+
+        cfg["stages"] = [p.num_layers for p in plan_stages(36, world)]
+    return cfg
+
+
+def tokens_report(tokens) -> dict:
+    """sha256 of the first CHECK_TOKENS greedy tokens (int32 little endian) and
+    the length of their common prefix with the oracle's greedy tokens."""
+    import hashlib
+
     import numpy as np
 
-    import dial_oracle as O
+    t = np.asarray(tokens[:CHECK_TOKENS], dtype="<i4")
+    rep = {"sha256": hashlib.sha256(t.tobytes()).hexdigest(), "n": int(t.size)}
+    if GOLDEN.exists():
+        g = np.load(GOLDEN)["tokens_f32p"][:CHECK_TOKENS]
+        same = np.nonzero(t != g[:t.size])[0]
+        rep["oracle_prefix"] = int(same[0]) if same.size else int(t.size)
+    return rep
 
-    cfg = O.ModelConfig(layers=1)
-    table = O.normal_table(0.02)
-    H, I, D = cfg.hidden, cfg.inter, cfg.head_dim
-    rng = np.random.default_rng(0)
 
-    def qw(n, k, stream):
-        return O.quantize_w8a16_rows(O.synth_normal(0, stream, n * k, table).reshape(n, k))
+class CpuDecoder:
+    """The C++/OpenMP oracle (oracle/dial_oracle_c.cpp, f32 accumulation as in
+    the reference kernels) on the host cores: the first `layers` layers of the
+    headline model plus its full embedding and lm_head, the prompt prefilled,
+    then greedy decode.  One token's time is scaled to the 36-layer model as
+    36 / layers x (layer stack) + head."""
 
-    qkv = qw(cfg.heads * D + 2 * cfg.kv_heads * D, H, 0x100)
-    o = qw(H, H, 0x103)
-    gu = qw(2 * I, H, 0x104)
-    dn = qw(H, I, 0x106)
-    one = lambda n: np.ones(n, np.float32)  # noqa: E731
-    lw = O.LayerWeights(*qkv, *o, *gu, *dn, one(H), one(H), one(D), one(D))
-    cos, sin = O.rope_tables(D, 512, cfg.rope_theta)
-    cache = O.Cache(1, 512)
-    ctx = PROMPT_LEN
-    kv = O.bf16_round(rng.standard_normal((1, cfg.kv_heads, ctx, D)).astype(np.float32))
-    cache.process_kv(0, 0, kv, kv.copy())
-    x = O.bf16_round(rng.standard_normal((1, H)).astype(np.float32))
-    lm = O.synth_normal(0, 0xE0002, 8192 * H, table).reshape(8192, H)
-    t_layer, n_layer = 0.0, 0
-    t0 = time.perf_counter()
-    while time.perf_counter() - t0 < budget_s or n_layer < 2:
+    def __init__(self, layers: int = 4):
+        sys.path.insert(0, str(ROOT / "oracle"))
+        import dial_oracle as O
+        import dial_oracle_fast as F
+
+        self.F, self.layers = F, layers
+        self.cfg = O.ModelConfig(max_seq_len=PROMPT_LEN + 2048)
+        self.m = F.FastModel(self.cfg, seed=0, num_layers=layers)
+        self._prefill()
+
+    def _prefill(self):
+        self.cache = self.m.new_cache()
+        x = self.m.embed(_prompt_tokens(self.cfg.vocab))
+        self.m.forward(x, self.cache, 0, accum=32, round_probs=False)
+        self.tok = int(self.m.logits(x[-1], accum=32)[0].argmax())
+        self.pos = PROMPT_LEN
+
+    def token_seconds(self) -> tuple[float, float]:
+        """Decode one token; returns (layer-stack seconds, head seconds)."""
+        if self.pos >= self.cfg.max_seq_len:
+            self._prefill()
+        x = self.m.embed([self.tok])
         a = time.perf_counter()
-        O.layer_forward(x, lw, cfg, ctx + n_layer, 0, cache, cos, sin)
-        t_layer += time.perf_counter() - a
-        n_layer += 1
-        if n_layer >= 64:
-            break
-    a = time.perf_counter()
-    O.dense_linear(x, lm)
-    t_head = (time.perf_counter() - a) * (cfg.vocab / 8192)
-    per_token = 36 * t_layer / n_layer + t_head
-    cores = len(os.sched_getaffinity(0))
-    return {"value": 1.0 / per_token, "unit": "tok/s", "cores": cores, "kind": "port",
-            "sample": f"{n_layer} single-token W8A16 decoder layers of Qwen3-8B shape at context "
-                      f"{PROMPT_LEN} + an 8192-row slice of the bf16 lm_head, numpy oracle "
-                      f"(dial_oracle.py), scaled to 36 layers + full vocab"}
+        self.m.forward(x, self.cache, self.pos, accum=32, round_probs=False)
+        b = time.perf_counter()
+        self.tok = int(self.m.logits(x, accum=32)[0].argmax())
+        c = time.perf_counter()
+        self.pos += 1
+        return b - a, c - b
+
+    def sample(self, n_tokens: int) -> float:
+        """tok/s of the 36-layer model estimated from n_tokens decode tokens."""
+        ls, hs = zip(*(self.token_seconds() for _ in range(n_tokens)))
+        return 1.0 / (36 / self.layers * statistics.median(ls) + statistics.median(hs))
+
+    def describe(self, n_tokens: int) -> dict:
+        import platform
+
+        cpu = platform.processor() or ""
+        try:
+            for ln in open("/proc/cpuinfo"):
+                if ln.startswith("model name"):
+                    cpu = ln.split(":", 1)[1].strip()
+                    break
+        except OSError:
+            pass
+        return {"unit": "tok/s", "cores": self.F.threads(), "kind": "port", "cpu_model": cpu,
+                "sample": f"{n_tokens} greedy decode tokens at context {PROMPT_LEN}+ of the "
+                          f"first {self.layers} W8A16 layers + full bf16 lm_head of the same "
+                          f"synthetic model, C++/OpenMP CPU restatement of the reference "
+                          f"(oracle/dial_oracle_c.cpp, f32 accumulation; not the reference "
+                          f"binary), scaled to 36 layers"}
+
+
+def cpu_decode_sample(n_tokens: int = 24) -> dict:
+    d = CpuDecoder()
+    d.sample(2)
+    return {"value": d.sample(n_tokens), **d.describe(n_tokens)}
 
 
 def run_reference(args) -> None:
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    budget = max(2.0, 60.0 / max(1, args.steps + args.warmup))
+    d = CpuDecoder()
+    per_step = 6
     vals = []
     for i in range(args.warmup + args.steps):
-        r = cpu_decode_sample(budget_s=budget)
+        v = d.sample(per_step)
         if i >= args.warmup:
-            vals.append(r["value"])
+            vals.append(v)
     v = statistics.median(vals)
-    line = {"impl": "reference", "metric": "decode tok/s (bs1, Qwen3-8B W8A16)", "value": v,
+    world = int(os.environ.get("WORLD_SIZE", str(args.gpus)))
+    par = "single GPU" if world <= 1 else f"pp{world}"
+    line = {"impl": "reference", "metric": METRIC, "value": v,
             "unit": "tok/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": 1000.0 / v, "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": WORKLOAD, "prompt_len": PROMPT_LEN, "batch": 1},
-            "cpu_baseline": {**r, "value": v},
+            "ms_per_step": GEN_TOKENS * 1000.0 / v, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": headline_config(par, world),
+            "cpu_baseline": {"value": v, **d.describe(per_step * args.steps)},
             "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -191,48 +248,60 @@ def run_single(args) -> dict:
     import torch
 
     import dial_b200
-    from dial_b200.synth import STREAM_TOKENS  # noqa: F401
 
     dev = 0
     torch.cuda.set_device(dev)
     cfg = dial_b200.Config(max_seq_len=4096, max_sessions=1, max_tokens=PROMPT_LEN)
     eng = dial_b200.Engine(cfg, device=dev)
     eng.load_synthetic(seed=0)
-    sys.path.insert(0, str(ROOT / "oracle"))
     prompt = _prompt_tokens(cfg.vocab_size)
-    eng.generate(prompt, 1)  # first call: lazy kernel loading, tensor-map set-up
+    eng.generate(prompt, 2)  # first call: lazy kernel loading, tensor maps, graphs
     first, ttft, _ = eng.generate(prompt, 1)
+    check, _, _ = eng.generate(prompt, CHECK_TOKENS)
     stream = eng.stream
-    pos = PROMPT_LEN
-    tok = int(first[0])
+    tok0 = int(first[0])
 
-    # ---- e2e through the public C ABI (host buffers, synchronous per step)
+    # ---- e2e through the public C ABI (host buffers, synchronous per token)
+    def e2e_step():
+        tok = tok0
+        for i in range(GEN_TOKENS):
+            tok = int(eng.decode_step([tok], [0], [PROMPT_LEN + i])[0])
+        return tok
+
     for _ in range(args.warmup):
-        tok = int(eng.decode_step([tok], [0], [pos])[0])
-        pos += 1
+        e2e_step()
     torch.cuda.synchronize()
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        tok = int(eng.decode_step([tok], [0], [pos])[0])
-        pos += 1
+        last_e2e = e2e_step()
     e2e_s = time.perf_counter() - t0
 
-    # ---- device-resident loop (graph replays, tokens fed back on device)
-    eng.loop_prepare([tok], [0], [pos])
-    eng.loop_run(1, args.warmup)
+    # ---- device-resident loop: each step decodes positions 128..255 from the
+    # prompt's first token (graph replays, tokens fed back on the device)
+    def loop_step(ev_a=None, ev_b=None):
+        eng.loop_prepare([tok0], [0], [PROMPT_LEN])
+        if ev_a is not None:
+            ev_a.record(stream)
+        eng.loop_run(1, GEN_TOKENS)
+        if ev_b is not None:
+            ev_b.record(stream)
+
+    for _ in range(args.warmup):
+        loop_step()
     torch.cuda.synchronize()
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(args.steps)]
     with ClockSampler(dev) as clk:
         time.sleep(0.3)
-        ev0.record(stream)
-        eng.loop_run(1, args.steps)
-        ev1.record(stream)
-        ev1.synchronize()
-    step_ms = ev0.elapsed_time(ev1) / args.steps
+        for a, b in evs:
+            loop_step(a, b)
+        torch.cuda.synchronize()
+    step_ms = sum(a.elapsed_time(b) for a, b in evs) / args.steps
     toks, positions = eng.loop_state(1)
 
     # ---- dominant kernel live: fused gate/up GEMV, same launch config, rotating
     # over the 36 layers' weights (3.6 GB) so every launch streams from HBM
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     iters = 72
     eng.linear_replay(-1, 2, 1, 3)
     torch.cuda.synchronize()
@@ -242,32 +311,39 @@ def run_single(args) -> dict:
     ev1.synchronize()
     k_us = ev0.elapsed_time(ev1) * 1000.0 / iters
     k_bytes = eng.linear_bytes(0, 2, 1)
-    step_bytes = sum(eng.linear_bytes(0, w, 1) for w in range(4)) * cfg.num_hidden_layers + \
-        eng.linear_bytes(0, 4, 1) + 36 * 2 * 8 * 128 * 2 * (pos + args.steps)
+    mean_ctx = PROMPT_LEN + GEN_TOKENS / 2
+    token_bytes = sum(eng.linear_bytes(0, w, 1) for w in range(4)) * cfg.num_hidden_layers + \
+        eng.linear_bytes(0, 4, 1) + 36 * 2 * 8 * 128 * 2 * mean_ctx
     peaks = load_peaks()
     achieved = k_bytes / (k_us * 1e-6) / 1e9
     status = dial_b200.device_status()
+    tok_ms = step_ms / GEN_TOKENS
     return {
-        "value": 1000.0 / step_ms, "ms_per_step": step_ms, "e2e_tok_s": args.steps / e2e_s,
+        "value": 1000.0 / tok_ms, "ms_per_step": step_ms,
+        "e2e_tok_s": args.steps * GEN_TOKENS / e2e_s,
         "ttft_s": ttft, "clocks": clk.summary(), "status": status,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": achieved / peaks["hbm_gbs"], "traffic": GATE_UP_TRAFFIC_BYTES,
                      "traffic_source": GATE_UP_TRAFFIC_SOURCE,
                      "kernel": "gemv_kernel<bf16,W8A16,SwiGLU,norm> (fused gate/up, N=24576 K=4096 M=1)",
                      "launch_us": k_us, "bytes_per_launch": k_bytes, "peak_source": peaks["source"],
-                     "step_bytes": step_bytes,
-                     "step_frac": step_bytes / (step_ms * 1e-3) / 1e9 / peaks["hbm_gbs"]},
-        "gpu_launches": eng.step_kernel_count(1) * args.steps,
-        "final_token": int(toks[0]), "final_pos": int(positions[0]),
+                     "token_bytes": token_bytes,
+                     "token_frac": token_bytes / (tok_ms * 1e-3) / 1e9 / peaks["hbm_gbs"]},
+        "gpu_launches": eng.step_kernel_count(1) * GEN_TOKENS * args.steps,
+        "tokens": tokens_report(check),
+        "loop_consistent": bool(int(positions[0]) == PROMPT_LEN + GEN_TOKENS and
+                                int(toks[0]) == last_e2e),
     }
 
 
 def run_pipeline(args) -> None:
     """N > 1: one process per GPU (torchrun), the 36 layers split evenly into N
-    pipeline stages, the hidden state handed stage to stage with NCCL
-    send/recv and the token returned to stage 0 (dial_b200.pipeline)."""
+    pipeline stages, the hidden state handed stage to stage and the token
+    returned to stage 0 (dial_b200.pipeline).  Same step as N = 1: 128 greedy
+    tokens from the prompt's first token, positions 128..255."""
     import datetime
 
+    import numpy as np
     import torch
     import torch.distributed as dist
 
@@ -288,78 +364,97 @@ def run_pipeline(args) -> None:
         eng.load_synthetic(seed=0)
         runner = StageRunner(eng, plan, cfg.hidden_size)
         stream = torch.cuda.Stream(dev)
-        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
 
         def max_over_ranks(v: float) -> float:
             t = torch.tensor([v], dtype=torch.float64, device=dev)
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             return float(t.item())
 
-        with torch.cuda.stream(stream):
-            prompt = torch.as_tensor(_prompt_tokens(cfg.vocab_size), device=dev) \
-                if plan.is_first else None
-            # bring up the NCCL p2p communicators of the stage ring before timing
-            probe = torch.zeros(PROMPT_LEN, cfg.hidden_size, dtype=torch.bfloat16, device=dev)
-            tok_probe = torch.zeros(1, dtype=torch.int32, device=dev)
-            if not plan.is_first:
-                dist.recv(probe, rank - 1)
-            if not plan.is_last:
-                dist.send(probe, rank + 1)
-            else:
-                dist.send(tok_probe, 0)
-            if plan.is_first:
-                dist.recv(tok_probe, world - 1)
+        def sync_all():
             torch.cuda.synchronize()
             dist.barrier()
-            t0 = time.perf_counter()
-            tok = runner.step(prompt, PROMPT_LEN, 0)
             torch.cuda.synchronize()
-            ttft = max_over_ranks(time.perf_counter() - t0)
-            runner.decode_prepare(PROMPT_LEN)
+
+        prompt_np = _prompt_tokens(cfg.vocab_size)
+        with torch.cuda.stream(stream):
+            prompt = torch.as_tensor(prompt_np, device=dev) if plan.is_first else None
+            # warm-up: communicators, kernel loading, the stage graph
+            runner.generate(prompt_np, 4)
+            sync_all()
+            ttfts = []
+            for _ in range(3):
+                sync_all()
+                t0 = time.perf_counter()
+                runner.step(prompt, PROMPT_LEN, 0)
+                torch.cuda.synchronize()
+                ttfts.append(max_over_ranks(time.perf_counter() - t0))
+            ttft = statistics.median(ttfts)
+            check = runner.generate(prompt_np, CHECK_TOKENS)
+            first = torch.zeros(1, dtype=torch.int32, device=dev)
+            if plan.is_first:
+                first.fill_(int(check[0]))
 
             # ---- device-resident decode: tokens stay on the GPUs
+            def loop_step(ev_a=None, ev_b=None):
+                stream.synchronize()  # the previous step's graphs read the positions
+                runner.decode_prepare(PROMPT_LEN)
+                tok = first.clone() if plan.is_first else None
+                if ev_a is not None:
+                    ev_a.record(stream)
+                for _ in range(GEN_TOKENS):
+                    tok = runner.decode_step(tok)
+                if ev_b is not None:
+                    ev_b.record(stream)
+                return tok
+
             for _ in range(args.warmup):
-                tok = runner.decode_step(tok)
-            torch.cuda.synchronize()
-            dist.barrier()
-            torch.cuda.synchronize()
+                loop_step()
+            sync_all()
+            evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                   for _ in range(args.steps)]
             with ClockSampler(local) as clk:
                 time.sleep(0.2)
-                ev0.record(stream)
-                for _ in range(args.steps):
-                    tok = runner.decode_step(tok)
-                ev1.record(stream)
-                ev1.synchronize()
-            torch.cuda.synchronize()
-            dist.barrier()
-            step_ms = max_over_ranks(ev0.elapsed_time(ev1) / args.steps)
+                for a, b in evs:
+                    last_loop = loop_step(a, b)
+                torch.cuda.synchronize()
+            sync_all()
+            step_ms = max_over_ranks(sum(a.elapsed_time(b) for a, b in evs) / args.steps)
+            last_loop = int(last_loop.item()) if plan.is_first else -1
 
-            # ---- end to end: the token goes host -> stage 0 and back to host every step
+            # ---- end to end: each token goes host -> stage 0 and back to the host
             pin_in = torch.zeros(1, dtype=torch.int32).pin_memory()
             pin_out = torch.zeros(1, dtype=torch.int32).pin_memory()
             tok_dev = torch.zeros(1, dtype=torch.int32, device=dev)
-            if plan.is_first:
-                pin_out.copy_(tok)
+
+            def e2e_step():
                 stream.synchronize()
-            for i in range(args.warmup + args.steps):
-                if i == args.warmup:
-                    torch.cuda.synchronize()
-                    dist.barrier()
-                    t0 = time.perf_counter()
+                runner.decode_prepare(PROMPT_LEN)
                 if plan.is_first:
-                    pin_in.copy_(pin_out)
-                    tok_dev.copy_(pin_in, non_blocking=True)
-                    out = runner.decode_step(tok_dev)
-                    pin_out.copy_(out, non_blocking=True)
-                    stream.synchronize()
-                else:
-                    runner.decode_step(None)
+                    pin_out.fill_(int(check[0]))
+                for _ in range(GEN_TOKENS):
+                    if plan.is_first:
+                        pin_in.copy_(pin_out)
+                        tok_dev.copy_(pin_in, non_blocking=True)
+                        out = runner.decode_step(tok_dev)
+                        pin_out.copy_(out, non_blocking=True)
+                        stream.synchronize()
+                    else:
+                        runner.decode_step(None)
+                return int(pin_out.item())
+
+            for _ in range(args.warmup):
+                e2e_step()
+            sync_all()
+            t0 = time.perf_counter()
+            for _ in range(args.steps):
+                last_e2e = e2e_step()
             torch.cuda.synchronize()
             e2e_s = max_over_ranks(time.perf_counter() - t0)
 
             # ---- stage handoff alone: [1, H] bf16 ping-pong between ranks 0 and 1
+            ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             x = torch.zeros(1, cfg.hidden_size, dtype=torch.bfloat16, device=dev)
-            dist.barrier()
+            sync_all()
             reps = 50
             if rank in (0, 1):
                 for i in range(reps + 5):
@@ -391,24 +486,21 @@ def run_pipeline(args) -> None:
             k_us = ev0.elapsed_time(ev1) * 1000.0 / iters
             k_bytes = eng.linear_bytes(layers[0], 2, 1)
         per_stage = plan.num_layers * 5 + int(plan.is_first) + 2 * int(plan.is_last) + 1
-        launches = torch.tensor([per_stage * args.steps], dtype=torch.int64, device=dev)
+        launches = torch.tensor([per_stage * GEN_TOKENS * args.steps], dtype=torch.int64,
+                                device=dev)
         dist.all_reduce(launches)
         status = dial_b200.device_status()
         peaks = load_peaks()
         achieved = k_bytes / (k_us * 1e-6) / 1e9
         if rank == 0:
             line = {
-                "metric": "decode tok/s (bs1, Qwen3-8B W8A16)", "value": 1000.0 / step_ms,
+                "metric": METRIC, "value": GEN_TOKENS * 1000.0 / step_ms,
                 "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
                 "ms_per_step": step_ms, "higher_is_better": True, "scaling": "strong",
                 "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-                "config": {"workload": WORKLOAD, "prompt_len": PROMPT_LEN, "batch": 1,
-                           "layers": 36, "hidden": 4096, "linear": "W8A16 row int8 + f32 scale",
-                           "lm_head": "bf16 dense", "parallelism": f"pp{world}",
-                           "stages": [p.num_layers for p in plan_stages(36, world)],
-                           "l2": "inputs larger than L2 (8.2 GB weights streamed per step)"},
-                "e2e": {"value": args.steps / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": 4,
-                        "d2h_bytes_per_step": 4},
+                "config": headline_config(f"pp{world}", world),
+                "e2e": {"value": GEN_TOKENS * args.steps / e2e_s, "unit": "tok/s",
+                        "h2d_bytes_per_step": 4 * GEN_TOKENS, "d2h_bytes_per_step": 4 * GEN_TOKENS},
                 "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"],
                              "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"],
                              "traffic": GATE_UP_TRAFFIC_BYTES,
@@ -420,10 +512,11 @@ def run_pipeline(args) -> None:
                 "cpu_baseline": None, "clocks": clk.summary(),
                 "gpu_launches": int(launches.item()), "ttft_s": ttft,
                 "handoff_us": hop_us, "device_status": status,
+                "tokens": tokens_report(check),
+                "loop_consistent": bool(last_loop == last_e2e),
             }
             print(json.dumps(line), flush=True)
-        torch.cuda.synchronize()
-        dist.barrier()
+        sync_all()
     finally:
         dist.destroy_process_group()
 
@@ -620,8 +713,8 @@ def _prompt_tokens(vocab: int, n: int = PROMPT_LEN):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=64)
-    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--workload", default="decode",
@@ -655,18 +748,15 @@ def main():
     r = run_single(args)
     cpu = None if args.no_cpu_baseline else cpu_decode_sample()
     line = {
-        "metric": "decode tok/s (bs1, Qwen3-8B W8A16)", "value": r["value"], "unit": "tok/s",
+        "metric": METRIC, "value": r["value"], "unit": "tok/s",
         "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": r["ms_per_step"],
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
-        "data": "synthetic",
-        "config": {"workload": WORKLOAD, "prompt_len": PROMPT_LEN, "batch": 1,
-                   "layers": 36, "hidden": 4096, "linear": "W8A16 row int8 + f32 scale",
-                   "lm_head": "bf16 dense", "parallelism": "single GPU",
-                   "l2": "inputs larger than L2 (8.2 GB weights streamed per step)"},
-        "e2e": {"value": r["e2e_tok_s"], "unit": "tok/s", "h2d_bytes_per_step": 12,
-                "d2h_bytes_per_step": 8},
+        "data": "synthetic", "config": headline_config("single GPU"),
+        "e2e": {"value": r["e2e_tok_s"], "unit": "tok/s", "h2d_bytes_per_step": 12 * GEN_TOKENS,
+                "d2h_bytes_per_step": 8 * GEN_TOKENS},
         "roofline": r["roofline"], "cpu_baseline": cpu, "clocks": r["clocks"],
         "gpu_launches": r["gpu_launches"], "ttft_s": r["ttft_s"], "device_status": r["status"],
+        "tokens": r["tokens"], "loop_consistent": r["loop_consistent"],
     }
     print(json.dumps(line), flush=True)
 

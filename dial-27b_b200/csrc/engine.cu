@@ -1272,6 +1272,8 @@ int dial_b200_decode_loop_prepare(dial_b200_engine* eng, int64_t rows, const int
       DIAL_CHECK(sids[i] >= 0 && sids[i] < eng->cfg.max_sessions, "session out of range");
       DIAL_CHECK(pos[i] >= 0 && pos[i] < eng->cfg.max_seq_len, "position out of range");
     }
+    // loop replays still in flight on the engine stream read these buffers
+    DIAL_CUDA(cudaStreamSynchronize(eng->stream));
     DIAL_CUDA(cudaMemcpy(eng->tok_in.p, toks, M * 4, cudaMemcpyHostToDevice));
     DIAL_CUDA(cudaMemcpy(eng->sid.p, sids, M * 4, cudaMemcpyHostToDevice));
     DIAL_CUDA(cudaMemcpy(eng->pos.p, pos, M * 4, cudaMemcpyHostToDevice));

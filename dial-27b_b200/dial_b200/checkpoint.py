@@ -109,10 +109,33 @@ class LinearSpec:
 
 
 def _u8(t: torch.Tensor) -> np.ndarray:
+    """Packed bytes (NVFP4 ``weight_packed``): one-byte tensors are viewed as
+    u8; a wider integer tensor holding byte values is narrowed."""
     t = t.detach().cpu().contiguous()
     if t.dtype != torch.uint8:
         t = t.view(torch.uint8) if t.element_size() == 1 else t.to(torch.uint8)
     return t.numpy()
+
+
+def _e4m3_codes(t: torch.Tensor, name: str) -> np.ndarray:
+    """e4m3 codes of an FP8 weight or NVFP4 group-scale tensor.  One-byte
+    tensors (float8_e4m3fn or u8) are the codes themselves, bit for bit
+    (quant.rs:528-544); a wider float tensor holds e4m3 values, as in the
+    reference's loader tests (quant.rs:547-601, where f32 tensors carry them),
+    and is converted to the code of each value, which must be exact."""
+    t = t.detach().cpu().contiguous()
+    if t.element_size() == 1:
+        return t.view(torch.uint8).numpy()
+    if not t.dtype.is_floating_point:
+        raise _err(f"{name}: expected e4m3 codes or values, got {t.dtype}")
+    v = t.to(torch.float32)
+    codes = v.to(torch.float8_e4m3fn)
+    back = codes.to(torch.float32)
+    if not torch.equal(back, v):
+        bad = int(torch.nonzero(back != v)[0, 0]) if v.ndim == 1 else int(
+            torch.nonzero((back != v).reshape(-1))[0, 0])
+        raise _err(f"{name}: value {float(v.reshape(-1)[bad])} is not an e4m3 value")
+    return codes.view(torch.uint8).numpy()
 
 
 def _f32(t: torch.Tensor) -> np.ndarray:
@@ -140,13 +163,13 @@ def read_linear(ck: Checkpoint, prefix: str, in_dim: int, out_dim: int,
         if in_dim % 16:
             raise _err(f"{prefix}: NVFP4 needs in_dim % 16 == 0, got {in_dim}")
         codes = _u8(ck.get(packed)).reshape(-1)
-        sc = _u8(ck.get(p + "weight_scale")).reshape(-1)
+        sc = _e4m3_codes(ck.get(p + "weight_scale"), p + "weight_scale").reshape(-1)
         if codes.size != out_dim * in_dim // 2 or sc.size != out_dim * in_dim // 16:
             raise _err(f"{prefix}: NVFP4 tensors do not match [{out_dim}, {in_dim}]")
         return LinearSpec(_abi.FMT_NVFP4_G16, codes.reshape(out_dim, in_dim // 2),
                           sc.reshape(out_dim, in_dim // 16), glob, out_dim, in_dim)
     if ck.has(p + "weight_scale"):
-        codes = _u8(ck.get(p + "weight")).reshape(-1)
+        codes = _e4m3_codes(ck.get(p + "weight"), p + "weight").reshape(-1)
         if codes.size != out_dim * in_dim:
             raise _err(f"{prefix}: FP8 weight does not match [{out_dim}, {in_dim}]")
         sc = _f32(ck.get(p + "weight_scale"))

@@ -2,6 +2,7 @@
 
     PYTHONPATH=dial-27b_b200 python -m dial_b200.microbench [--shapes q,gate_up] [--M 1,4,16]
         [--iters 20] [--min-footprint-mb 512]
+    PYTHONPATH=dial-27b_b200 python -m dial_b200.microbench --replay gate_up --layers 4 --M 1
 
 Each case builds enough copies of the quantized weight that one rotation
 through them streams more than the L2 cache (126 MB) from HBM, captures the
@@ -110,6 +111,38 @@ def run_prefill(n_prompt: int) -> dict:
             "launches_per_prefill": eng.prefill_kernel_count(n_prompt)}
 
 
+LINEARS = {"qkv": 0, "o": 1, "gate_up": 2, "down": 3}
+
+
+def run_replay(name: str, layers: int, rows: int, iters: int) -> dict:
+    """One decode-step linear of the synthetic Qwen3-8B W8A16 engine (the
+    epilogue the decode step uses: fused RMSNorm + SwiGLU for gate_up, RMSNorm
+    for qkv, residual add for o and down) replayed `iters` times, rotating over
+    `layers` layers so that no launch finds its weights in L2
+    (dial_b200_engine_linear_replay).  A small device footprint for profiler
+    captures of the exact kernel variant the decode step runs."""
+    from .engine import Config, Engine
+
+    cfg = Config(num_hidden_layers=layers, max_seq_len=64, max_sessions=1,
+                 max_tokens=max(rows, 16))
+    eng = Engine(cfg, device=0, has_embed=False, has_head=False)
+    eng.load_synthetic(seed=0)
+    which = LINEARS[name]
+    eng.linear_replay(-1, which, rows, 200)  # clocks up before timing
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(eng.stream)
+    eng.linear_replay(-1, which, rows, iters)
+    e1.record(eng.stream)
+    e1.synchronize()
+    us = e0.elapsed_time(e1) * 1000.0 / iters
+    nbytes = eng.linear_bytes(0, which, rows)
+    peak, src = measured_hbm_gbs()
+    gbs = nbytes / (us * 1e-6) / 1e9
+    return {"linear": name, "rows": rows, "layers": layers, "us": us, "bytes": nbytes,
+            "GB_s": gbs, "frac_hbm": gbs / peak, "peak_gbs": peak, "peak_source": src}
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--shapes", default=",".join(SHAPES))
@@ -118,8 +151,16 @@ def main(argv=None):
     ap.add_argument("--min-footprint-mb", type=int, default=512)
     ap.add_argument("--prefill", type=int, default=0,
                     help="instead: time a warmed prefill of this many tokens on the synthetic model")
+    ap.add_argument("--replay", default="",
+                    help="instead: replay one decode-step linear (qkv, o, gate_up, down) of a "
+                         "--layers-layer synthetic engine, --M rows (first value)")
+    ap.add_argument("--layers", type=int, default=4)
     args = ap.parse_args(argv)
     torch.cuda.set_device(0)
+    if args.replay:
+        rows = int(args.M.split(",")[0])
+        print(json.dumps(run_replay(args.replay, args.layers, rows, args.iters)), flush=True)
+        return
     if args.prefill > 0:
         print(json.dumps(run_prefill(args.prefill)), flush=True)
         return

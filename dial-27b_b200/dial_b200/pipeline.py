@@ -117,9 +117,10 @@ class StageRunner:
         self.pos = index_pos
         if self.graphs:
             self.eng.stage_prepare([self.session], [index_pos])
-            self._x = torch.empty(1, self.H, dtype=self.dtype, device=self.device)
-            self._tok_in = torch.zeros(1, dtype=torch.int32, device=self.device)
-            self._tok_out = torch.zeros(1, dtype=torch.int32, device=self.device)
+            if not hasattr(self, "_x"):  # fixed buffers: the stage graph is captured once
+                self._x = torch.empty(1, self.H, dtype=self.dtype, device=self.device)
+                self._tok_in = torch.zeros(1, dtype=torch.int32, device=self.device)
+                self._tok_out = torch.zeros(1, dtype=torch.int32, device=self.device)
 
     def decode_step(self, token: torch.Tensor | None) -> torch.Tensor | None:
         """One bs1 decode token through this stage; stage 0 passes the current

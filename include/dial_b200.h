@@ -269,8 +269,9 @@ int dial_b200_generate(dial_b200_engine* eng, int32_t session, const int32_t* pr
 
 /* Device-resident decode loop for measurement: `n_steps` replays of the
  * step graph with the sampled tokens fed back on the device; rows of state
- * are seeded by dial_b200_decode_loop_prepare.  Asynchronous on the engine
- * stream. */
+ * are seeded by dial_b200_decode_loop_prepare (synchronous: it waits for
+ * loop replays still running on the engine stream).  dial_b200_decode_loop_run
+ * is asynchronous on the engine stream. */
 int dial_b200_decode_loop_prepare(dial_b200_engine* eng, int64_t rows, const int32_t* tokens_host,
                                   const int32_t* sids_host, const int32_t* positions_host,
                                   char* err, size_t err_size);

@@ -261,3 +261,63 @@ def test_sharded_directory_and_config(tmp_path):
         (H, KVH, 1e6, 256)
     eng = _load(tmp_path)
     assert len([k for k in eng.linears if k[1] != 4]) == 4 * LAYERS
+
+
+def test_reference_loader_known_answers(tmp_path):
+    """The reference's own loader tests (qwen3_8/quant.rs:528-662), each as a
+    tiny safetensors file read by dial_b200.checkpoint.read_linear and
+    dequantised by the oracle: raw e4m3 bit patterns survive (528-544);
+    ModelOpt NVFP4 with weight_scale_2 (547-576); FP8 with a per-output f32
+    scale, also at the f16 runtime dtype (579-630); compressed-tensors NVFP4
+    whose weight_global_scale is a divisor (633-662).  As in those tests, the
+    e4m3 fields of 547-662 are stored as f32 values."""
+    from dial_b200 import FMT_FP8_ROW, FMT_NVFP4_G16
+    from dial_b200.checkpoint import Checkpoint, read_linear
+
+    def no_dense(_):
+        raise AssertionError("a quantised layer must not reach the dense path")
+
+    # 528-544: raw e4m3 codes, one scale
+    raw = torch.tensor([0x00, 0x38, 0xB8, 0x7E], dtype=torch.uint8).view(torch.float8_e4m3fn)
+    _write(tmp_path, {"a.weight": raw.reshape(2, 2), "a.weight_scale": torch.tensor([1.0])},
+           name="a.safetensors")
+    spec = read_linear(Checkpoint(tmp_path / "a.safetensors"), "a", 2, 2, no_dense)
+    assert spec.fmt == FMT_FP8_ROW
+    assert spec.codes.reshape(-1).tolist() == [0x00, 0x38, 0xB8, 0x7E]
+
+    # 547-576: ModelOpt NVFP4
+    _write(tmp_path, {"b.weight": torch.full((1, 8), 0x92, dtype=torch.uint8),
+                      "b.weight_scale": torch.tensor([[2.0]]),
+                      "b.weight_scale_2": torch.tensor([4.0])}, name="b.safetensors")
+    spec = read_linear(Checkpoint(tmp_path / "b.safetensors"), "b", 16, 1, no_dense)
+    assert spec.fmt == FMT_NVFP4_G16 and spec.global_scale == 4.0
+    w = O.nvfp4_dense_weight(spec.codes, spec.scales, spec.global_scale, 16, 1)
+    assert w.reshape(-1).tolist() == [8.0, -4.0] * 8
+
+    # 579-630: FP8 values [[1,2],[3,4]] with per-output scale [2, 0.5]
+    _write(tmp_path, {"c.weight": torch.tensor([[1.0, 2.0], [3.0, 4.0]]),
+                      "c.weight_scale": torch.tensor([2.0, 0.5])}, name="c.safetensors")
+    spec = read_linear(Checkpoint(tmp_path / "c.safetensors"), "c", 2, 2, no_dense)
+    assert spec.fmt == FMT_FP8_ROW
+    w = O.fp8_row_dense_weight(spec.codes, spec.scales, 2, 2)
+    assert w.reshape(-1).tolist() == [2.0, 4.0, 1.5, 2.0]
+    assert O.f16_round(w).reshape(-1).tolist() == [2.0, 4.0, 1.5, 2.0]
+
+    # 633-662: compressed-tensors NVFP4, global scale 4.0 is a divisor
+    _write(tmp_path, {"d.weight_packed": torch.full((1, 8), 0x92, dtype=torch.uint8),
+                      "d.weight_scale": torch.tensor([[2.0]]),
+                      "d.weight_global_scale": torch.tensor([4.0])}, name="d.safetensors")
+    spec = read_linear(Checkpoint(tmp_path / "d.safetensors"), "d", 16, 1, no_dense)
+    assert spec.global_scale == 0.25
+    w = O.nvfp4_dense_weight(spec.codes, spec.scales, spec.global_scale, 16, 1)
+    assert w.reshape(-1).tolist() == [0.5, -0.25] * 8
+
+
+def test_e4m3_fields_must_hold_e4m3_values(tmp_path):
+    from dial_b200 import DialError
+    from dial_b200.checkpoint import Checkpoint, read_linear
+
+    _write(tmp_path, {"e.weight": torch.tensor([[1.0, 2.0], [3.0, 4.1]]),
+                      "e.weight_scale": torch.tensor([1.0])}, name="e.safetensors")
+    with pytest.raises(DialError, match="not an e4m3 value"):
+        read_linear(Checkpoint(tmp_path / "e.safetensors"), "e", 2, 2, lambda w: None)

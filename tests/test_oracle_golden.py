@@ -34,10 +34,11 @@ def test_nvfp4_rejects_invalid_shapes():
         O.decode_nvfp4_values(np.zeros(7, np.uint8), [1.0], 1.0, 16, 1)
 
 
-def test_fp8_bit_patterns_preserved():
-    # quant.rs:528-544: raw e4m3 codes survive loading unchanged; their decode
+def test_e4m3_decode_of_the_raw_codes():
+    # the codes of quant.rs:528-544 and their decode (cuda_quant.rs:27-41); the
+    # loading half of that test runs through the checkpoint reader in
+    # tests/test_checkpoint_cpu.py::test_reference_loader_known_answers
     codes = np.array([0x00, 0x38, 0xB8, 0x7E], dtype=np.uint8)
-    assert codes.tolist() == [0x00, 0x38, 0xB8, 0x7E]
     assert O.e4m3_to_f32(codes).tolist() == [0.0, 1.0, -1.0, 448.0]
 
 
@@ -48,15 +49,13 @@ def test_modelopt_nvfp4_linear():
 
 
 def test_fp8_per_output_scale():
-    # quant.rs:579-601: weight [[1,2],[3,4]] (f32 values), scale [2, 0.5]
-    w = np.array([[1.0, 2.0], [3.0, 4.0]], dtype=np.float32)
-    s = np.array([2.0, 0.5], dtype=np.float32)
-    assert (w * s[:, None]).reshape(-1).tolist() == [2.0, 4.0, 1.5, 2.0]
-
-
-def test_fp8_scales_f16_runtime():
-    # quant.rs:604-630: same values survive the f16 runtime dtype exactly
-    w = np.array([[1.0, 2.0], [3.0, 4.0]], dtype=np.float32) * np.array([[2.0], [0.5]], np.float32)
+    # quant.rs:579-601 (weight codes of [[1,2],[3,4]], scale [2, 0.5]) through
+    # the oracle's FP8 row dequant (quant.rs:408-429); the checkpoint reader
+    # half is tests/test_checkpoint_cpu.py::test_reference_loader_known_answers
+    codes = O.f32_to_e4m3(np.array([[1.0, 2.0], [3.0, 4.0]], np.float32))
+    w = O.fp8_row_dense_weight(codes, [2.0, 0.5], 2, 2)
+    assert w.reshape(-1).tolist() == [2.0, 4.0, 1.5, 2.0]
+    # quant.rs:604-630: the same values survive the f16 runtime dtype exactly
     assert O.f16_round(w).reshape(-1).tolist() == [2.0, 4.0, 1.5, 2.0]
 
 
