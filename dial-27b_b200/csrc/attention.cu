@@ -38,9 +38,14 @@ template <typename Act, int NREP>
 __global__ void __launch_bounds__(NREP * 32, decode_min_ctas<NREP>())
     attn_decode_kernel(const AttnDecodeArgs a) {
   pdl_launch_dependents();
+  const unsigned long long t_entry = a.trace ? global_ns() : 0ull;
   __shared__ AttnItemSmem sm;
   attn_item<Act, NREP, true>(a, blockIdx.z, blockIdx.x, blockIdx.y, threadIdx.x >> 5,
                              threadIdx.x & 31, sm, 1);
+  if (a.trace && threadIdx.x == 0) {
+    const unsigned long long t[4] = {t_entry, 0ull, 0ull, global_ns()};
+    trace_record(a.trace, a.trace_tag, t);
+  }
 }
 
 // Token-split form: the group's warps share each page's tokens (TSG pages of
@@ -52,11 +57,16 @@ constexpr int kTokSplitPages = 1;
 template <typename Act, int NREP, int TSG>
 __global__ void __launch_bounds__(NREP * 32) attn_decode_ts_kernel(const AttnDecodeArgs a) {
   pdl_launch_dependents();
+  const unsigned long long t_entry = a.trace ? global_ns() : 0ull;
   __shared__ AttnItemSmem sm;
   __shared__ AttnTokSplitSmem<NREP> ts;
   attn_item<Act, NREP, true, 0, 0, TSG>(a, blockIdx.z, blockIdx.x, blockIdx.y, threadIdx.x >> 5,
                                         threadIdx.x & 31, sm, 1, nullptr, nullptr, nullptr,
                                         nullptr, &ts);
+  if (a.trace && threadIdx.x == 0) {
+    const unsigned long long t[4] = {t_entry, 0ull, 0ull, global_ns()};
+    trace_record(a.trace, a.trace_tag, t);
+  }
 }
 
 // Cluster form: the CL splits of a (row, kv head) that share a cluster merge
@@ -64,22 +74,32 @@ __global__ void __launch_bounds__(NREP * 32) attn_decode_ts_kernel(const AttnDec
 template <typename Act, int NREP, int CL>
 __global__ void __launch_bounds__(NREP * 32) attn_decode_cluster_kernel(const AttnDecodeArgs a) {
   pdl_launch_dependents();
+  const unsigned long long t_entry = a.trace ? global_ns() : 0ull;
   __shared__ AttnItemSmem sm;
   __shared__ AttnClusterSmem<NREP> cs;
   attn_item<Act, NREP, true, CL>(a, blockIdx.z, blockIdx.x, blockIdx.y, threadIdx.x >> 5,
                                  threadIdx.x & 31, sm, 1, &cs);
+  if (a.trace && threadIdx.x == 0) {
+    const unsigned long long t[4] = {t_entry, 0ull, 0ull, global_ns()};
+    trace_record(a.trace, a.trace_tag, t);
+  }
 }
 
 // Cluster form with the token-split scan.
 template <typename Act, int NREP, int CL, int TSG>
 __global__ void __launch_bounds__(NREP * 32) attn_decode_cluster_ts_kernel(const AttnDecodeArgs a) {
   pdl_launch_dependents();
+  const unsigned long long t_entry = a.trace ? global_ns() : 0ull;
   __shared__ AttnItemSmem sm;
   __shared__ AttnClusterSmem<NREP> cs;
   __shared__ AttnTokSplitSmem<NREP> ts;
   attn_item<Act, NREP, true, CL, 0, TSG>(a, blockIdx.z, blockIdx.x, blockIdx.y, threadIdx.x >> 5,
                                          threadIdx.x & 31, sm, 1, &cs, nullptr, nullptr, nullptr,
                                          &ts);
+  if (a.trace && threadIdx.x == 0) {
+    const unsigned long long t[4] = {t_entry, 0ull, 0ull, global_ns()};
+    trace_record(a.trace, a.trace_tag, t);
+  }
 }
 
 // Ring form (optionally clustered, CL > 0): NREP query warps + one producer
@@ -90,6 +110,7 @@ constexpr int kRingBytes = kRingPages * 2 * kPageBytes;
 template <typename Act, int NREP, int CL>
 __global__ void __launch_bounds__((NREP + 1) * 32) attn_decode_ring_kernel(const AttnDecodeArgs a) {
   pdl_launch_dependents();
+  const unsigned long long t_entry = a.trace ? global_ns() : 0ull;
   __shared__ AttnItemSmem sm;
   __shared__ AttnClusterSmem<NREP> cs;  // partials of the cluster merge (CL > 0)
   __shared__ uint64_t bars[2 * kRingPages];
@@ -110,6 +131,10 @@ __global__ void __launch_bounds__((NREP + 1) * 32) attn_decode_ring_kernel(const
   }
   attn_item<Act, NREP, true, CL, kRingPages>(a, blockIdx.z, blockIdx.x, blockIdx.y, warp, lane, sm,
                                              1, &cs, ring, bars, bars + kRingPages);
+  if (a.trace && threadIdx.x == 0) {
+    const unsigned long long t[4] = {t_entry, 0ull, 0ull, global_ns()};
+    trace_record(a.trace, a.trace_tag, t);
+  }
 }
 
 // Prefill KV append: token t of the session at position p0+t.  One warp per

@@ -59,6 +59,8 @@ struct AttnDecodeArgs {
   // of more than 4 rows; 2: also for the cluster-merge form of 4 rows or
   // fewer; 0: every warp reads every token for its own head.
   int tok_split;
+  unsigned long long* trace; // opt-in timeline records (common.cuh), null = off
+  int trace_tag;
 };
 
 // Scratch bytes needed for (M, splits).

@@ -11,6 +11,8 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include "trace.h"
+
 #if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ < 1000)
 #error "dial_b200 kernels target sm_100a only"
 #endif
@@ -26,6 +28,7 @@ enum DevStatus : int {
   kStatusBadArgs = 0x104,
   kStatusAttnCounter = 0x201,
   kStatusAttnRing = 0x202,          // decode-attention page ring wait timed out
+  kStatusLinkTimeout = 0x301,       // a stage link receive waited past the bound
 };
 
 // Wall-clock bound (ns) on any spin-wait; well above any legitimate wait.
@@ -35,6 +38,24 @@ __device__ __forceinline__ unsigned long long global_ns() {
   unsigned long long t;
   asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
   return t;
+}
+
+// Opt-in timeline of the decode step (DIAL_B200_TRACE=<csv> on the engine):
+// thread 0 of every CTA appends one record (trace.h), [tag << 32 | CTA] and
+// four %globaltimer stamps (0 = not taken), after the header words
+// trace[0] = records written, trace[1] = capacity.
+__device__ __forceinline__ void trace_record(unsigned long long* trace, int tag,
+                                             const unsigned long long (&t)[4]) {
+  if (!trace) return;
+  const unsigned long long i = atomicAdd(trace, 1ull);
+  if (i >= trace[1]) return;
+  unsigned long long* r = trace + kTraceHeader + i * kTraceWords;
+  const unsigned cta = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
+  r[0] = (static_cast<unsigned long long>(static_cast<unsigned>(tag)) << 32) | cta;
+  r[1] = t[0];
+  r[2] = t[1];
+  r[3] = t[2];
+  r[4] = t[3];
 }
 
 __device__ __forceinline__ void set_status(int* status, int code) {

@@ -4,6 +4,7 @@
 // the extern "C" entry points declared in include/dial_b200.h.
 #include <cuda_fp16.h>
 
+#include <algorithm>
 #include <chrono>
 #include <cmath>
 #include <cstdarg>
@@ -20,6 +21,7 @@
 #include "gemm.h"
 #include "gemv.h"
 #include "layout.h"
+#include "trace.h"
 #include "misc.h"
 
 using namespace dialb200;
@@ -344,7 +346,8 @@ void run_gemm(const Linear& L, const void* x, int x_ld, const void* norm_w, floa
 
 void run_linear(const Linear& L, const void* x, int x_ld, const void* norm_w, float eps, void* out,
                 int out_ld, int M, int epi, cudaStream_t s, int* status,
-                const GemmScratch* scratch = nullptr) {
+                const GemmScratch* scratch = nullptr, unsigned long long* trace = nullptr,
+                int trace_tag = 0) {
   if (use_gemm(L, M, scratch != nullptr && scratch->stage != nullptr)) {
     run_gemm(L, x, x_ld, norm_w, eps, out, out_ld, M, epi, s, status, *scratch);
     return;
@@ -359,6 +362,8 @@ void run_linear(const Linear& L, const void* x, int x_ld, const void* norm_w, fl
   a.out_ld = out_ld;
   a.M = M;
   a.status = status;
+  a.trace = trace;
+  a.trace_tag = trace_tag;
   DIAL_CUDA(gemv_launch(a, L.act, epi, norm_w != nullptr, s, g_tuning()));
 }
 
@@ -406,6 +411,8 @@ struct dial_b200_engine {
   DevBuf amax_key, amax_count;  // head argmax keys / arrival counters, zero between steps
   DevBuf gemm_scratch;          // prefill GEMM activation staging (max_tokens rows)
   DevBuf gemm_part;             // split-K partial sums of small-row GEMM calls
+  DevBuf trace;                 // DIAL_B200_TRACE=<csv>: per-CTA timeline of decode steps
+  std::string trace_path;
   int32_t* h_in = nullptr;   // pinned: [3][max_rows] tokens, sids, positions
   int32_t* h_out = nullptr;  // pinned: [max_rows] tokens + status
   int* status = nullptr;
@@ -562,6 +569,14 @@ void engine_init(dial_b200_engine* e, const dial_b200_model_config& c, int devic
     e->counters.alloc(static_cast<size_t>(e->max_rows_decode) * e->KVH * 4);
     DIAL_CUDA(cudaMemset(e->counters.p, 0, e->counters.bytes));
   }
+  if (const char* tp = std::getenv("DIAL_B200_TRACE")) {
+    constexpr unsigned long long kRecords = 1ull << 18;
+    e->trace_path = tp;
+    e->trace.alloc((kTraceHeader + kRecords * kTraceWords) * 8);
+    const unsigned long long hdr[2] = {0ull, kRecords};
+    DIAL_CUDA(cudaMemset(e->trace.p, 0, e->trace.bytes));
+    DIAL_CUDA(cudaMemcpy(e->trace.p, hdr, sizeof(hdr), cudaMemcpyHostToDevice));
+  }
   DIAL_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&e->h_in), 3 * T * 4, cudaHostAllocDefault));
   DIAL_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&e->h_out), (T + 1) * 4, cudaHostAllocDefault));
   DIAL_CUDA(cudaStreamSynchronize(e->stream));
@@ -653,7 +668,7 @@ void set_rows_decode(dial_b200_engine* e, int M, const int32_t* sids, const int3
   DIAL_CUDA(cudaStreamSynchronize(s));
 }
 
-AttnDecodeArgs decode_attn_args(dial_b200_engine* e, LayerW& L, int M) {
+AttnDecodeArgs decode_attn_args(dial_b200_engine* e, LayerW& L, int M, int row0 = 0) {
   AttnDecodeArgs a{};
   a.sh = e->shape();
   a.qkv = e->qkv.p;
@@ -664,8 +679,8 @@ AttnDecodeArgs decode_attn_args(dial_b200_engine* e, LayerW& L, int M) {
   a.sin = e->sin.p;
   a.kv = KvLayer{L.kpool.p, L.vpool.p};
   a.block_table = e->block_table.as<int32_t>();
-  a.sid = e->sid.as<int32_t>();
-  a.pos = e->pos.as<int32_t>();
+  a.sid = e->sid.as<int32_t>() + row0;
+  a.pos = e->pos.as<int32_t>() + row0;
   a.out = e->attn.p;
   a.out_ld = e->QH * e->D;
   a.M = M;
@@ -683,23 +698,30 @@ AttnDecodeArgs decode_attn_args(dial_b200_engine* e, LayerW& L, int M) {
   // register form packs more CTAs per SM)
   a.page_ring = g_tuning().attn_ring && M <= 4 ? 1 : 0;
   a.tok_split = g_tuning().attn_tok_split;
+  a.trace = e->trace.as<unsigned long long>();
   return a;
 }
 
-void layer_decode(dial_b200_engine* e, LayerW& L, void* hidden, int M, cudaStream_t s) {
+// One decoder layer for M decode rows whose sessions / positions are the
+// engine's rows [row0, row0 + M).
+void layer_decode(dial_b200_engine* e, LayerW& L, void* hidden, int M, cudaStream_t s,
+                  int row0 = 0) {
   const float eps = e->cfg.rms_norm_eps;
   const GemmScratch gsv{e->gemm_scratch.p, e->gemm_part.as<float>(), e->gemm_part.bytes};
   const GemmScratch* gs = &gsv;
-  run_linear(L.qkv, hidden, e->H, L.input_norm.p, eps, e->qkv.p, e->QKV, M, kEpiStore, s, e->status,
-             gs);
-  const AttnDecodeArgs a = decode_attn_args(e, L, M);
+  unsigned long long* tr = e->trace.as<unsigned long long>();
+  const int tag = static_cast<int>(&L - e->layers.data() + e->cfg.first_layer) << 8;
+  run_linear(L.qkv, hidden, e->H, L.input_norm.p, eps, e->qkv.p, e->QKV, M, kEpiStore, s,
+             e->status, gs, tr, tag | 0);
+  AttnDecodeArgs a = decode_attn_args(e, L, M, row0);
+  a.trace_tag = tag | 1;
   DIAL_CUDA(attn_decode_launch(a, e->cfg.act, s, g_tuning().pdl));
   run_linear(L.o, e->attn.p, e->QH * e->D, nullptr, eps, hidden, e->H, M, kEpiResidual, s, e->status,
-             gs);
+             gs, tr, tag | 2);
   run_linear(L.gate_up, hidden, e->H, L.post_norm.p, eps, e->inter.p, e->I, M, kEpiSwiglu, s,
-             e->status, gs);
+             e->status, gs, tr, tag | 3);
   run_linear(L.down, e->inter.p, e->I, nullptr, eps, hidden, e->H, M, kEpiResidual, s, e->status,
-             gs);
+             gs, tr, tag | 4);
 }
 
 void layer_prefill(dial_b200_engine* e, LayerW& L, void* hidden, int M, int session, int p0,
@@ -790,7 +812,36 @@ void head_forward(dial_b200_engine* e, const void* hidden, int rows, void* logit
   a.amax_key = e->amax_key.as<unsigned long long>();
   a.amax_count = e->amax_count.as<int>();
   a.amax_tok = toks;
+  a.trace = e->trace.as<unsigned long long>();
+  a.trace_tag = (0xFFFF << 8) | 5;
   DIAL_CUDA(gemv_launch(a, e->lm_head.act, kEpiArgmax, true, s, g_tuning()));
+}
+
+// Write the trace records taken since the last dump as CSV (layer, op, cta,
+// entry, wait released, staged, end in ns; 0 = not taken) and start over.
+void dump_trace(dial_b200_engine* e) {
+  if (!e->trace.p) return;
+  unsigned long long hdr[2] = {0ull, 0ull};
+  DIAL_CUDA(cudaMemcpy(hdr, e->trace.p, sizeof(hdr), cudaMemcpyDeviceToHost));
+  const unsigned long long n = std::min(hdr[0], hdr[1]);
+  std::vector<unsigned long long> r(n * kTraceWords);
+  if (n)
+    DIAL_CUDA(cudaMemcpy(r.data(), e->trace.as<unsigned long long>() + kTraceHeader, r.size() * 8,
+                         cudaMemcpyDeviceToHost));
+  FILE* f = std::fopen(e->trace_path.c_str(), "w");
+  if (f) {
+    std::fprintf(f, "layer,op,cta,entry,released,staged,end\n");
+    for (unsigned long long i = 0; i < n; ++i) {
+      const unsigned long long* q = &r[i * kTraceWords];
+      const unsigned tag = static_cast<unsigned>(q[0] >> 32);
+      std::fprintf(f, "%d,%u,%u,%llu,%llu,%llu,%llu\n", static_cast<int>(tag >> 8) == 0xFFFF ? -1
+                   : static_cast<int>(tag >> 8), tag & 0xFF, static_cast<unsigned>(q[0] & 0xFFFFFFFFu),
+                   q[1], q[2], q[3], q[4]);
+    }
+    std::fclose(f);
+  }
+  const unsigned long long zero = 0ull;
+  DIAL_CUDA(cudaMemcpy(e->trace.p, &zero, 8, cudaMemcpyHostToDevice));
 }
 
 // Whole decode step on device buffers (tok_in, sid, pos -> tok_out).
@@ -816,6 +867,7 @@ void drop_graphs(dial_b200_engine* e) {
   e->stage_graphs.clear();
 }
 
+// Step graph of M rows (loop: tokens fed back on the device).
 Graph* get_graph(dial_b200_engine* e, int M, bool loop) {
   auto& map = loop ? e->loop_graphs : e->step_graphs;
   auto it = map.find(M);
@@ -1303,6 +1355,7 @@ int dial_b200_decode_loop_state(dial_b200_engine* eng, int64_t rows, int32_t* to
     if (pos) DIAL_CUDA(cudaMemcpy(pos, eng->pos.p, rows * 4, cudaMemcpyDeviceToHost));
     int st = 0;
     DIAL_CUDA(cudaMemcpy(&st, eng->status, 4, cudaMemcpyDeviceToHost));
+    dump_trace(eng);
     check_status(eng, st);
   });
 }
@@ -1326,19 +1379,23 @@ int dial_b200_stage_prepare(dial_b200_engine* eng, int64_t rows, const int32_t* 
   });
 }
 
-int dial_b200_stage_step(dial_b200_engine* eng, int64_t rows, const int32_t* tokens_dev,
-                         void* hidden, int32_t* tokens_out_dev, void* stream, char* err,
-                         size_t n) {
+int dial_b200_stage_step_rows(dial_b200_engine* eng, int64_t row_offset, int64_t rows,
+                              const int32_t* tokens_dev, void* hidden, int32_t* tokens_out_dev,
+                              void* stream, char* err, size_t n) {
   return guarded(err, n, [&] {
     DIAL_CHECK(eng && hidden, "null pointer argument");
     DIAL_CUDA(cudaSetDevice(eng->device));
     const int M = static_cast<int>(rows);
-    DIAL_CHECK(M >= 1 && M <= eng->max_rows_decode && M <= 256, "rows %d out of range", M);
+    const int r0 = static_cast<int>(row_offset);
+    DIAL_CHECK(M >= 1 && M <= 256, "rows %d out of range", M);
+    DIAL_CHECK(r0 >= 0 && r0 + M <= eng->max_rows_decode,
+               "rows [%d, %d) outside the %d decode rows", r0, r0 + M, eng->max_rows_decode);
     DIAL_CHECK(!eng->cfg.has_embed || tokens_dev, "the first stage needs device token ids");
     DIAL_CHECK(!eng->cfg.has_head || tokens_out_dev, "the last stage needs a token output");
     check_weights(eng, eng->cfg.first_layer, eng->cfg.num_layers);
     if (eng->cfg.has_head) DIAL_CHECK(eng->lm_head.ready(), "lm_head weights not loaded");
-    const auto key = std::make_tuple(rows, static_cast<const void*>(tokens_dev),
+    const auto key = std::make_tuple(rows | (static_cast<int64_t>(r0) << 32),
+                                     static_cast<const void*>(tokens_dev),
                                      static_cast<const void*>(hidden),
                                      static_cast<const void*>(tokens_out_dev));
     auto it = eng->stage_graphs.find(key);
@@ -1351,9 +1408,9 @@ int dial_b200_stage_step(dial_b200_engine* eng, int64_t rows, const int32_t* tok
           DIAL_CUDA(embed_launch(eng->embed.p, tokens_dev, M, eng->V, eng->H, hidden, eng->H,
                                  eng->status, s, g_tuning().pdl));
         for (int li = 0; li < eng->cfg.num_layers; ++li)
-          layer_decode(eng, eng->layers[li], hidden, M, s);
+          layer_decode(eng, eng->layers[li], hidden, M, s, r0);
         if (eng->cfg.has_head) head_forward(eng, hidden, M, nullptr, tokens_out_dev, s);
-        DIAL_CUDA(advance_launch(nullptr, nullptr, eng->pos.as<int32_t>(), M, s,
+        DIAL_CUDA(advance_launch(nullptr, nullptr, eng->pos.as<int32_t>() + r0, M, s,
                                  g_tuning().pdl));
       } catch (...) {
         cudaGraph_t tmp = nullptr;
@@ -1367,6 +1424,13 @@ int dial_b200_stage_step(dial_b200_engine* eng, int64_t rows, const int32_t* tok
     }
     DIAL_CUDA(cudaGraphLaunch(it->second->exec, static_cast<cudaStream_t>(stream)));
   });
+}
+
+int dial_b200_stage_step(dial_b200_engine* eng, int64_t rows, const int32_t* tokens_dev,
+                         void* hidden, int32_t* tokens_out_dev, void* stream, char* err,
+                         size_t n) {
+  return dial_b200_stage_step_rows(eng, 0, rows, tokens_dev, hidden, tokens_out_dev, stream, err,
+                                   n);
 }
 
 void* dial_b200_engine_stream(dial_b200_engine* eng) { return eng ? eng->stream : nullptr; }

@@ -143,6 +143,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1)
   uint64_t* sbar = empty + kMaxSlots;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  unsigned long long tstamp[4] = {a.trace ? global_ns() : 0ull, 0ull, 0ull, 0ull};
   const int T = a.w.T, C = a.w.C;
   const int t0 = static_cast<int>(static_cast<long long>(T) * blockIdx.x / gridDim.x);
   const int t1 = static_cast<int>(static_cast<long long>(T) * (blockIdx.x + 1) / gridDim.x);
@@ -221,6 +222,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1)
   if constexpr (EPI == kEpiArgmax) {
     if (threadIdx.x < kMaxM) skey[threadIdx.x] = 0ull;
   }
+
   if constexpr (NORM) {
     // the RMSNorm weight is constant: bring it into L1 before the wait so
     // that staging after it touches only the activations in L2
@@ -230,8 +232,10 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1)
       asm volatile("prefetch.global.L1 [%0];" ::"l"(nw + off));
   }
   pdl_wait();
+  if (a.trace) tstamp[1] = global_ns();
   stage_x<Act, XT, NORM, kScaleX, kNW>(a, xs, p.xs_stride, xexp, scratch);
   named_bar_sync(1, kNW * 32);
+  if (a.trace) tstamp[2] = global_ns();
   if constexpr (FMT == kFmtFp8Block128) mbar_wait(sbar, 0, a.status, kStatusFullWaitTimeout);
 
   const int g = lane >> 2;
@@ -380,6 +384,10 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1)
         }
       }
     }
+  }
+  if (a.trace && threadIdx.x == 0) {
+    tstamp[3] = global_ns();
+    trace_record(a.trace, a.trace_tag, tstamp);
   }
   if constexpr (EPI == kEpiArgmax) {
     // CTA best -> global keys; the last CTA to arrive decodes and resets them.

@@ -31,6 +31,8 @@ struct GemvArgs {
   unsigned long long* amax_key;
   int* amax_count;
   int32_t* amax_tok;
+  unsigned long long* trace;  // opt-in timeline records (common.cuh), null = off
+  int trace_tag;
 };
 
 struct GemvTuning {

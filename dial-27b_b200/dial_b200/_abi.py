@@ -44,6 +44,18 @@ class AttnShape(C.Structure):
     ]
 
 
+class GdnShape(C.Structure):
+    _fields_ = [
+        ("k_heads", C.c_int32),
+        ("v_heads", C.c_int32),
+        ("k_head_dim", C.c_int32),
+        ("v_head_dim", C.c_int32),
+        ("conv_kernel", C.c_int32),
+        ("eps", C.c_float),
+        ("act", C.c_int32),
+    ]
+
+
 class ModelConfig(C.Structure):
     _fields_ = [
         ("hidden_size", C.c_int32),
@@ -90,6 +102,10 @@ _SIGS = {
                                                      _vp, *_err]),
     "dial_b200_stage_prepare": (C.c_int, [_vp, _i64, _vp, _vp, *_err]),
     "dial_b200_stage_step": (C.c_int, [_vp, _i64, _vp, _vp, _vp, _vp, *_err]),
+    "dial_b200_stage_step_rows": (C.c_int, [_vp, _i64, _i64, _vp, _vp, _vp, _vp, *_err]),
+    "dial_b200_gdn_scratch_bytes": (_i64, [C.POINTER(GdnShape), _i64]),
+    "dial_b200_gdn_forward": (C.c_int, [C.POINTER(GdnShape), _vp, _vp, _vp, _vp, _vp, _vp, _vp,
+                                        _vp, _vp, _vp, _i64, _i64, _vp, _vp, _vp, *_err]),
     "dial_b200_engine_create": (C.c_int, [C.POINTER(ModelConfig), C.c_int, C.POINTER(_vp), *_err]),
     "dial_b200_engine_destroy": (None, [_vp]),
     "dial_b200_engine_load_synthetic": (C.c_int, [_vp, _u64, _vp, *_err]),

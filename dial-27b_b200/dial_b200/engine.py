@@ -273,6 +273,15 @@ class Engine:
         call("dial_b200_stage_step", self._h, rows, ptr(tokens), ptr(hidden), ptr(tokens_out),
              self._stream_ptr())
 
+    def stage_step_rows(self, row_offset: int, rows: int, tokens: torch.Tensor | None,
+                        hidden: torch.Tensor, tokens_out: torch.Tensor | None = None):
+        """stage_step for the prepared rows [row_offset, row_offset + rows) (one
+        micro-batch of the sessions given to stage_prepare)."""
+        self._check_hidden(hidden)
+        ptr = lambda t: C.c_void_p(t.data_ptr() if t is not None else 0)  # noqa: E731
+        call("dial_b200_stage_step_rows", self._h, row_offset, rows, ptr(tokens), ptr(hidden),
+             ptr(tokens_out), self._stream_ptr())
+
     def session_fill_random(self, session: int, length: int, seed: int, std: float = 1.0):
         call("dial_b200_session_fill_random", self._h, session, length, seed,
              _np_ptr(normal_table_bits(std)))

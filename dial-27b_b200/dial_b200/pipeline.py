@@ -169,3 +169,97 @@ class StageRunner:
         if self.plan.is_first:
             return torch.cat(out).cpu().numpy()
         return None
+
+
+class MicroBatchRunner:
+    """Ragged multi-session decode pipelined over the stages.
+
+    The decode rows (one per session) are cut into ``n_micro`` contiguous
+    micro-batches; on every rank an iteration runs the micro-batches in order,
+    each as one graph-captured stage step (``Engine.stage_step_rows``), with
+    the hidden state of micro-batch j handed to the next stage while this
+    stage already works on j + 1.  The last stage returns each micro-batch's
+    sampled tokens to stage 0, which embeds them in the next iteration.  With
+    ``n_micro`` >= the number of stages every stage is busy in the steady
+    state.  This is the in-box form of the reference Worker serving one
+    layer range for many Master connections at once (spm/worker.rs:316-325,
+    899-912), each connection's hop replaced by a send/recv between GPUs.
+
+    The engine needs ``stage_prepare``, ``stage_step_rows``, ``dtype`` and a
+    device; the same logic runs on CPU with ``gloo`` ranks in the tests.
+    """
+
+    def __init__(self, engine, plan: StagePlan, hidden_size: int, n_rows: int, n_micro: int,
+                 group=None):
+        if not 1 <= n_micro <= n_rows:
+            raise ValueError(f"n_micro must be in [1, {n_rows}], got {n_micro}")
+        self.eng, self.plan, self.H, self.group = engine, plan, hidden_size, group
+        self.device = getattr(engine, "torch_device", None) or torch.device("cuda", engine.device)
+        self.dtype = engine.dtype
+        bounds = [n_rows * j // n_micro for j in range(n_micro + 1)]
+        self.micro = [(bounds[j], bounds[j + 1] - bounds[j]) for j in range(n_micro)]
+        mk = lambda rows, **kw: torch.zeros(rows, **kw, device=self.device)  # noqa: E731
+        self._h = [mk(r, dtype=self.dtype).reshape(r, 1).expand(r, hidden_size).contiguous()
+                   for _, r in self.micro]
+        self._tok_in = [mk(r, dtype=torch.int32) for _, r in self.micro]
+        self._tok_out = [mk(r, dtype=torch.int32) for _, r in self.micro]
+        self._pending = False  # stage 0 owes receives of the last iteration's tokens
+        # sends are asynchronous (only receives block, so no two ranks can wait
+        # on each other's sends); a buffer is rewritten only after its send
+        self._sent = [None] * n_micro
+
+    def prepare(self, sids, positions, tokens=None):
+        """Sessions and positions of all rows (host arrays); stage 0 also takes
+        the rows' current token ids."""
+        self.finish()
+        self.eng.stage_prepare(sids, positions)
+        if self.plan.is_first:
+            t = torch.as_tensor(np.asarray(tokens, dtype=np.int32))
+            for (off, rows), buf in zip(self.micro, self._tok_in):
+                buf.copy_(t[off:off + rows])
+
+    def _recv(self, t, src):
+        dist.recv(t, src, group=self.group)
+
+    def _sent_wait(self, j):
+        if self._sent[j] is not None:
+            self._sent[j].wait()
+            self._sent[j] = None
+
+    def iteration(self):
+        """One decode token for every row, micro-batch by micro-batch."""
+        p = self.plan
+        for j, (off, rows) in enumerate(self.micro):
+            h = self._h[j]
+            self._sent_wait(j)  # h (or the last stage's tokens) is rewritten below
+            if p.is_first:
+                if self._pending:
+                    self._recv(self._tok_in[j], p.world - 1)
+            else:
+                self._recv(h, p.rank - 1)
+            self.eng.stage_step_rows(off, rows, self._tok_in[j] if p.is_first else None, h,
+                                     self._tok_out[j] if p.is_last else None)
+            if not p.is_last:
+                self._sent[j] = dist.isend(h, p.rank + 1, group=self.group)
+            elif p.world > 1:
+                self._sent[j] = dist.isend(self._tok_out[j], 0, group=self.group)
+            else:
+                self._tok_in[j].copy_(self._tok_out[j])
+        self._pending = p.is_first and p.world > 1
+
+    def finish(self):
+        """Complete every send and, on stage 0, receive the tokens of the last
+        iteration (before the next prepare or the end of the run)."""
+        if self._pending:
+            for j in range(len(self.micro)):
+                self._recv(self._tok_in[j], self.plan.world - 1)
+            self._pending = False
+        for j in range(len(self.micro)):
+            self._sent_wait(j)
+
+    def tokens(self) -> np.ndarray | None:
+        """Stage 0: the rows' current token ids (after finish())."""
+        if not self.plan.is_first:
+            return None
+        self.finish()
+        return torch.cat(self._tok_in).cpu().numpy()

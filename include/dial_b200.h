@@ -169,6 +169,45 @@ int dial_b200_attention_decode_noalloc(const dial_b200_attn_shape* sh, const voi
                                        char* err, size_t err_size);
 
 /* ------------------------------------------------------------------------ */
+/* Gated-DeltaNet token mixer (Qwen3.8 hybrid linear-attention layers)      */
+/* ------------------------------------------------------------------------ */
+
+/* Shape of a Gated-DeltaNet layer (qwen3_8/config.rs:49-53; head dims must
+ * be 128, conv kernel at most 8). */
+typedef struct {
+  int32_t k_heads;     /* linear_num_key_heads */
+  int32_t v_heads;     /* linear_num_value_heads (a multiple of k_heads) */
+  int32_t k_head_dim;  /* linear_key_head_dim */
+  int32_t v_head_dim;  /* linear_value_head_dim */
+  int32_t conv_kernel; /* linear_conv_kernel_dim */
+  float eps;           /* rms_norm_eps of the gated norm */
+  int32_t act;         /* DIAL_ACT_BF16 or DIAL_ACT_F16 */
+} dial_b200_gdn_shape;
+
+/* Bytes of the scratch dial_b200_gdn_forward needs for `seq_len` tokens. */
+int64_t dial_b200_gdn_scratch_bytes(const dial_b200_gdn_shape* sh, int64_t seq_len);
+
+/* GatedDeltaNet::forward (qwen3_8/text.rs:390-481) from the outputs of its
+ * input projections to the input of out_proj, for one session (device
+ * arrays; the projections and out_proj are dial_b200_qlinear_forward calls):
+ *   mixed [seq_len][2*k_heads*128 + v_heads*128] = in_proj_qkv(x) (q | k | v),
+ *   z [seq_len][v_heads*128] = in_proj_z(x), b and a [seq_len][v_heads];
+ *   conv_weight [channels][conv_kernel] (activation dtype); dt_bias, a_log
+ *   [v_heads] and norm_weight [128] as f32;
+ *   conv_state [channels][conv_kernel-1] (activation dtype) and
+ *   recurrent_state [v_heads][128][128] (f32): the per-session linear-attention
+ *   cache (llama3/cache.rs:267-290), read unless index_pos == 0 (a sequence
+ *   start, cache.rs semantics) and replaced by the state after the call;
+ *   core_out [seq_len][v_heads*128] receives the gated-normed output.
+ * Asynchronous on `stream`.  Tokens of one call are scanned in order. */
+int dial_b200_gdn_forward(const dial_b200_gdn_shape* sh, const void* mixed, const void* z,
+                          const void* b, const void* a, const void* conv_weight,
+                          const float* dt_bias, const float* a_log, const float* norm_weight,
+                          void* conv_state, float* recurrent_state, int64_t seq_len,
+                          int64_t index_pos, void* scratch, void* core_out, void* stream,
+                          char* err, size_t err_size);
+
+/* ------------------------------------------------------------------------ */
 /* Decoder layers: Forwarder + per-session KV cache + Worker                */
 /* ------------------------------------------------------------------------ */
 
@@ -292,6 +331,15 @@ int dial_b200_stage_prepare(dial_b200_engine* eng, int64_t rows, const int32_t* 
 int dial_b200_stage_step(dial_b200_engine* eng, int64_t rows, const int32_t* tokens_dev,
                          void* hidden, int32_t* tokens_out_dev, void* stream, char* err,
                          size_t err_size);
+/* dial_b200_stage_step for the prepared rows [row_offset, row_offset + rows):
+ * the micro-batch form of the stage loop, where the sessions prepared by
+ * dial_b200_stage_prepare are cut into micro-batches that are in flight on
+ * different stages at once (the per-connection concurrency of the
+ * reference's Worker, spm/worker.rs:316-325, 899-912).  One graph per
+ * (offset, rows, buffer addresses); positions of those rows advance by one. */
+int dial_b200_stage_step_rows(dial_b200_engine* eng, int64_t row_offset, int64_t rows,
+                              const int32_t* tokens_dev, void* hidden, int32_t* tokens_out_dev,
+                              void* stream, char* err, size_t err_size);
 
 /* Copy the loop's current tokens/positions back to host (synchronizes). */
 int dial_b200_decode_loop_state(dial_b200_engine* eng, int64_t rows, int32_t* tokens_host,

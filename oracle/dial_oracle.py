@@ -680,3 +680,140 @@ def synth_normal(seed: int, stream: int, n: int, table: np.ndarray, offset: int 
 def synth_tokens(seed: int, n: int, vocab: int) -> np.ndarray:
     idx = np.arange(n, dtype=np.uint64)
     return (synth_hash(seed, 0x70CE, idx) % np.uint64(vocab)).astype(np.int64)
+
+
+# ---------------------------------------------------------------------------
+# f4: Gated-DeltaNet token mixer of the Qwen3.8 hybrid (qwen3_8/text.rs:233-481)
+# ---------------------------------------------------------------------------
+#
+# Rounding points (candle-owned, unpinned by any reference test): the causal
+# depthwise conv sums its K products in f32 and rounds once to the activation
+# dtype; SiLU and sigmoid round each elementary step to the activation dtype
+# (SiLU as silu_mul above, sigmoid act(1 / act(1 + act(exp(-x))))); everything
+# from the l2 normalisation on (q, k, v, beta, g, the recurrence) is f32 as
+# the reference states (text.rs:393-459); the scan output is rounded to the
+# activation dtype before the gated RMSNorm (text.rs:460-466), which is f32
+# with one rounding at its end (text.rs:240-250).
+
+
+def silu_act(v, act: str = "bf16") -> np.ndarray:
+    """candle SiLU on activation-dtype values: act(v / act(1 + act(exp(-v))))."""
+    r = lambda t: act_round(t, act)  # noqa: E731
+    v = np.asarray(v, dtype=np.float32)
+    e = r(np.exp((-v).astype(np.float64)).astype(np.float32))
+    return r(v / r(np.float32(1.0) + e))
+
+
+def sigmoid_act(v, act: str = "bf16") -> np.ndarray:
+    """candle sigmoid on activation-dtype values: act(1 / act(1 + act(exp(-v))))."""
+    r = lambda t: act_round(t, act)  # noqa: E731
+    v = np.asarray(v, dtype=np.float32)
+    e = r(np.exp((-v).astype(np.float64)).astype(np.float32))
+    return r(np.float32(1.0) / r(np.float32(1.0) + e))
+
+
+def gdn_causal_conv(mixed, weight, prev, act: str = "bf16"):
+    """GatedDeltaNet::causal_conv (text.rs:301-337): depthwise causal conv1d of
+    kernel K over time, then SiLU.  mixed [S, C]; weight [C, K]; prev [C, K-1]
+    (the carried conv state) or None (zeros: a sequence start).  Returns
+    (silu(conv) [S, C], new state [C, K-1] = the last K-1 inputs)."""
+    mixed = np.asarray(mixed, dtype=np.float32)
+    S, C = mixed.shape
+    K = weight.shape[1]
+    hist = np.zeros((C, K - 1), np.float32) if prev is None else np.asarray(prev, np.float32)
+    inp = np.concatenate([hist, mixed.T], axis=1)  # [C, K-1+S]
+    out = np.empty((S, C), np.float32)
+    w = np.asarray(weight, dtype=np.float32)
+    for t in range(S):
+        out[t] = act_round(np.sum(inp[:, t:t + K].astype(np.float64) * w, axis=1)
+                           .astype(np.float32), act)
+    state = inp[:, -(K - 1):].copy() if K > 1 else np.zeros((C, 0), np.float32)
+    return silu_act(out, act), state
+
+
+def gdn_l2_normalize(x) -> np.ndarray:
+    """GatedDeltaNet::l2_normalize (text.rs:339-342): x / sqrt(sum x^2 + 1e-6), f32."""
+    x = np.asarray(x, dtype=np.float32)
+    ss = np.sum(x.astype(np.float64) ** 2, axis=-1, keepdims=True).astype(np.float32)
+    return (x / np.sqrt(ss + np.float32(1e-6))).astype(np.float32)
+
+
+def gdn_recurrent_scan(q, k, v, g, beta, state):
+    """GatedDeltaNet::recurrent_scan (text.rs:344-388), f32: per token
+    state *= exp(g); pred = k . state; delta = (v - pred) * beta;
+    state += k (x) delta; out = q . state.  q, k [H, S, dk]; v [H, S, dv];
+    g, beta [H, S]; state [H, dk, dv].  Returns (out [H, S, dv], state)."""
+    q, k, v = (np.asarray(t, np.float32) for t in (q, k, v))
+    st = np.array(state, dtype=np.float32, copy=True)
+    H, S, _ = q.shape
+    out = np.empty((H, S, v.shape[2]), np.float32)
+    for t in range(S):
+        st = (st * np.exp(g[:, t].astype(np.float32))[:, None, None]).astype(np.float32)
+        pred = np.einsum("hi,hij->hj", k[:, t].astype(np.float64), st.astype(np.float64))
+        delta = ((v[:, t] - pred.astype(np.float32)) * beta[:, t][:, None]).astype(np.float32)
+        st = (st + k[:, t][:, :, None] * delta[:, None, :]).astype(np.float32)
+        out[:, t] = np.einsum("hi,hij->hj", q[:, t].astype(np.float64),
+                              st.astype(np.float64)).astype(np.float32)
+    return out, st
+
+
+def gdn_gated_rms_norm(x, gate, weight, eps: float, act: str = "bf16") -> np.ndarray:
+    """GatedRmsNorm::forward (text.rs:240-250): f32 x / sqrt(mean x^2 + eps) *
+    w * silu(gate), rounded once to the activation dtype."""
+    x = np.asarray(x, dtype=np.float32)
+    ms = (np.sum(x.astype(np.float64) ** 2, axis=-1, keepdims=True) / x.shape[-1]).astype(np.float32)
+    y = x / np.sqrt(ms + np.float32(eps))
+    gate = np.asarray(gate, dtype=np.float32)
+    silu = gate / (np.float32(1.0) + np.exp(-gate.astype(np.float64)).astype(np.float32))
+    return act_round(y * np.asarray(weight, np.float32) * silu, act)
+
+
+def zero_centered_rms_norm(x, weight, eps: float, act: str = "bf16") -> np.ndarray:
+    """ZeroCenteredRmsNorm::forward (text.rs:26-38): f32 x / sqrt(mean x^2 + eps)
+    * (w + 1), rounded once to the activation dtype."""
+    x = np.asarray(x, dtype=np.float32)
+    ms = (np.sum(x.astype(np.float64) ** 2, axis=-1, keepdims=True) / x.shape[-1]).astype(np.float32)
+    y = x / np.sqrt(ms + np.float32(eps))
+    return act_round(y * (np.asarray(weight, np.float32) + np.float32(1.0)), act)
+
+
+@dataclass
+class GdnState:
+    """Per-session linear-attention state of one layer (cache.rs:267-290):
+    conv [C, K-1] (activation values) and recurrent [Hv, dk, dv] f32."""
+    conv: np.ndarray
+    recurrent: np.ndarray
+
+
+def gdn_mixer(mixed, z, b, a, conv_w, dt_bias, a_log, norm_w, hk: int, hv: int, dk: int,
+              dv: int, eps: float, state: GdnState | None, act: str = "bf16"):
+    """GatedDeltaNet::forward (text.rs:390-481) from the outputs of its input
+    projections to the input of out_proj: mixed [S, 2*hk*dk + hv*dv] (q | k |
+    v), z [S, hv*dv], b and a [S, hv]; conv_w [C, K]; dt_bias, a_log [hv];
+    norm_w [dv]; state None at a sequence start (index_pos 0).  Returns
+    (core [S, hv*dv] in the activation dtype, the new GdnState)."""
+    mixed = np.asarray(mixed, np.float32)
+    S = mixed.shape[0]
+    conv_out, conv_state = gdn_causal_conv(mixed, conv_w, None if state is None else state.conv,
+                                           act)
+    ks = hk * dk
+    q = conv_out[:, :ks].reshape(S, hk, dk).transpose(1, 0, 2)
+    k = conv_out[:, ks:2 * ks].reshape(S, hk, dk).transpose(1, 0, 2)
+    v = conv_out[:, 2 * ks:].reshape(S, hv, dv).transpose(1, 0, 2)
+    rep = hv // hk
+    q = np.repeat(q, rep, axis=0)  # repeat_kv: v head h reads key head h // rep
+    k = np.repeat(k, rep, axis=0)
+    q = (gdn_l2_normalize(q) / np.float32(math.sqrt(dk))).astype(np.float32)
+    k = gdn_l2_normalize(k)
+    beta = sigmoid_act(b, act).T.astype(np.float32)  # [hv, S]
+    af = np.asarray(a, np.float32)
+    sp = np.log(np.exp((af + np.asarray(dt_bias, np.float32)).astype(np.float64)) + 1.0) \
+        .astype(np.float32)
+    g = (-(sp * np.exp(np.asarray(a_log, np.float32).astype(np.float64)).astype(np.float32))) \
+        .T.astype(np.float32)  # [hv, S]
+    rec = np.zeros((hv, dk, dv), np.float32) if state is None else state.recurrent
+    core, rec = gdn_recurrent_scan(q, k, v, g, beta, rec)
+    core = act_round(core.transpose(1, 0, 2), act)  # [S, hv, dv]
+    zz = np.asarray(z, np.float32).reshape(S, hv, dv)
+    out = gdn_gated_rms_norm(core, zz, norm_w, eps, act).reshape(S, hv * dv)
+    return out, GdnState(conv_state, rec)

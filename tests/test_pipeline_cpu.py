@@ -125,3 +125,102 @@ def test_plan_rejects_mismatched_world():
     plans = plan_stages(36, 8)
     assert [p.num_layers for p in plans] == [5, 5, 5, 5, 4, 4, 4, 4]
     assert plans[0].is_first and plans[-1].is_last
+
+
+class OracleRowsStage:
+    """Stand-in engine for the micro-batch runner: stage_prepare /
+    stage_step_rows over per-session oracle caches for this stage's layers."""
+
+    dtype = torch.float32
+    torch_device = torch.device("cpu")
+
+    def __init__(self, model, plan, caches):
+        import dial_oracle as O
+
+        self.O, self.model, self.plan, self.caches = O, model, plan, caches
+
+    def stage_prepare(self, sids, positions):
+        self.sids = list(np.asarray(sids))
+        self.pos = list(np.asarray(positions))
+
+    def stage_step_rows(self, off, rows, tokens, hidden, tokens_out=None):
+        O, m, p = self.O, self.model, self.plan
+        for r in range(off, off + rows):
+            sid, pos = int(self.sids[r]), int(self.pos[r])
+            if p.is_first:
+                x = m.embed[[int(tokens[r - off])]]
+            else:
+                x = hidden[r - off:r - off + 1].numpy()
+            for l in range(p.first_layer, p.first_layer + p.num_layers):
+                x = O.layer_forward(x, m.layers[l], m.cfg, pos, l, self.caches[sid], m.cos, m.sin)
+            hidden[r - off] = torch.from_numpy(np.ascontiguousarray(x[0], dtype=np.float32))
+            if p.is_last:
+                tokens_out[r - off] = O.argmax_first(O.model_logits(m, x[0]))
+            self.pos[r] += 1
+
+
+def _sessions(cfg, model, n):
+    """Prompts of different lengths, their prefilled caches and first tokens
+    (the single-process oracle)."""
+    import dial_oracle as O
+
+    rng = np.random.default_rng(8)
+    prompts = [list(rng.integers(0, cfg.vocab, size=int(rng.integers(2, 9)))) for _ in range(n)]
+    caches, first = [], []
+    for pr in prompts:
+        c = O.Cache(cfg.layers, cfg.max_seq_len)
+        h = O.model_hidden(model, pr, 0, c)
+        caches.append(c)
+        first.append(O.argmax_first(O.model_logits(model, h[-1])))
+    return prompts, caches, first
+
+
+def _mb_worker(rank, world, port, n_sess, n_micro, n_iter, out_path):
+    sys.path[:0] = [str(ROOT / "dial-27b_b200"), str(ROOT / "oracle"), str(ROOT / "tests")]
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    import datetime
+
+    import dial_oracle as O
+    from dial_b200.pipeline import MicroBatchRunner, plan_stages
+
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60))
+    try:
+        cfg = _cfg()
+        model = O.synth_model(cfg, seed=3, std=0.05)
+        prompts, caches, first = _sessions(cfg, model, n_sess)
+        plan = plan_stages(cfg.layers, world)[rank]
+        runner = MicroBatchRunner(OracleRowsStage(model, plan, caches), plan, cfg.hidden, n_sess,
+                                  n_micro)
+        runner.prepare(np.arange(n_sess), [len(p) for p in prompts], first)
+        seen = []
+        for _ in range(n_iter):
+            runner.iteration()
+            toks = runner.tokens()
+            if rank == 0:
+                seen.append(toks.copy())
+        if rank == 0:
+            np.save(out_path, np.stack(seen))
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world,n_micro", [(1, 2), (2, 2), (3, 4), (2, 5)])
+def test_micro_batched_ragged_sessions_match_single_process(tmp_path, world, n_micro):
+    """5 sessions with prompts of different lengths, cut into micro-batches
+    that are in flight on different stages: the tokens of every iteration
+    equal each session's own greedy decode."""
+    import dial_oracle as O
+
+    n_sess, n_iter = 5, 3
+    out = tmp_path / "mb.npy"
+    mp.start_processes(_mb_worker, args=(world, _free_port(), n_sess, n_micro, n_iter, str(out)),
+                       nprocs=world, start_method="spawn", join=True)
+    got = np.load(out)
+    cfg = _cfg()
+    model = O.synth_model(cfg, seed=3, std=0.05)
+    prompts, _, _ = _sessions(cfg, model, n_sess)
+    for s, pr in enumerate(prompts):
+        want, _ = O.greedy_generate(model, pr, n_iter + 1)
+        np.testing.assert_array_equal(got[:, s], np.asarray(want[1:], dtype=np.int32))
