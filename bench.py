@@ -530,8 +530,205 @@ def _relaunch_with_torchrun(args) -> None:
     cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
            f"--nproc-per-node={args.gpus}", "--master-addr", "127.0.0.1", "--master-port",
            str(port), str(Path(__file__).resolve()), "--gpus", str(args.gpus), "--steps",
-           str(args.steps), "--warmup", str(args.warmup), "--impl", args.impl]
+           str(args.steps), "--warmup", str(args.warmup), "--impl", args.impl,
+           "--workload", args.workload]
     raise SystemExit(subprocess.call(cmd))
+
+
+def _pipeline_init():
+    """torchrun rank, world, local GPU and the NCCL process group (short timeout)."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    rank = int(os.environ["RANK"])
+    world = int(os.environ["WORLD_SIZE"])
+    local = int(os.environ.get("LOCAL_RANK", rank))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    return rank, world, local, dev
+
+
+def _max_over_ranks(v: float, dev) -> float:
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([v], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def _sync_all():
+    import torch
+    import torch.distributed as dist
+
+    torch.cuda.synchronize()
+    dist.barrier()
+    torch.cuda.synchronize()
+
+
+def run_pipeline_long(args) -> None:
+    """N > 1, BASELINE configs 3 and 5: the decoder split evenly into N
+    pipeline stages (dial_b200.pipeline.StageRunner), a long prompt prefilled
+    through the stages (TTFT, warmed, median of the timed steps) and bs1
+    greedy decode of 256 tokens after it (device-side stage graphs, CUDA
+    events, max over ranks).  prefill2048: Qwen3-8B W8A16, 2048-token prompt;
+    fp8_27b / nvfp4_27b: the 27B-class decoder (64 layers) with FP8 block-128
+    or NVFP4 linears, 4096-token prompt."""
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    import dial_b200
+    from dial_b200.pipeline import StageRunner, plan_stages
+
+    rank, world, local, dev = _pipeline_init()
+    try:
+        n_gen = 256
+        if args.workload == "prefill2048":
+            n_prompt = 2048
+            cfg = dial_b200.Config(max_seq_len=n_prompt + n_gen + 64, max_sessions=1,
+                                   max_tokens=n_prompt)
+            tag, metric_model = "qwen3-8b-w8a16-prefill2048-decode256", "Qwen3-8B W8A16"
+        else:
+            n_prompt = 4096
+            fmt = dial_b200.FMT_FP8_BLOCK128 if args.workload == "fp8_27b" \
+                else dial_b200.FMT_NVFP4_G16
+            cfg = dial_b200.Config.dense_27b(max_seq_len=n_prompt + n_gen + 64, max_sessions=1,
+                                             max_tokens=n_prompt, linear_fmt=fmt)
+            ftag = "fp8-block128" if args.workload == "fp8_27b" else "nvfp4"
+            tag, metric_model = f"dense27b-{ftag}-prefill4096-decode256", f"27B-class {ftag}"
+        plan = plan_stages(cfg.num_hidden_layers, world)[rank]
+        eng = dial_b200.Engine(cfg, first_layer=plan.first_layer, num_layers=plan.num_layers,
+                               device=local)
+        eng.load_synthetic(seed=0)
+        runner = StageRunner(eng, plan, cfg.hidden_size)
+        stream = torch.cuda.Stream(dev)
+        prompt_np = _prompt_tokens(cfg.vocab_size, n_prompt)
+        with torch.cuda.stream(stream):
+            prompt = torch.as_tensor(prompt_np, device=dev) if plan.is_first else None
+            runner.generate(prompt_np[:64], 2)  # communicators, kernels, stage graph
+            ttfts = []
+            for i in range(args.warmup + args.steps):
+                _sync_all()
+                t0 = time.perf_counter()
+                tok = runner.step(prompt, n_prompt, 0)
+                torch.cuda.synchronize()
+                if i >= args.warmup:
+                    ttfts.append(_max_over_ranks(time.perf_counter() - t0, dev))
+            ttft = statistics.median(ttfts)
+            runner.decode_prepare(n_prompt)
+            for _ in range(8):
+                tok = runner.decode_step(tok)
+            _sync_all()
+            ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            with ClockSampler(local) as clk:
+                ev0.record(stream)
+                for _ in range(n_gen - 8):
+                    tok = runner.decode_step(tok)
+                ev1.record(stream)
+                ev1.synchronize()
+            _sync_all()
+            dec_ms = _max_over_ranks(ev0.elapsed_time(ev1) / (n_gen - 8), dev)
+            last = int(tok.item()) if plan.is_first else -1
+        w_bytes = torch.tensor([sum(eng.linear_bytes(plan.first_layer, w, 1) for w in range(4)) *
+                                plan.num_layers + (eng.linear_bytes(0, 4, 1) if plan.is_last
+                                                   else 0)], dtype=torch.float64, device=dev)
+        dist.all_reduce(w_bytes)
+        status = dial_b200.device_status()
+        peaks = load_peaks()
+        gbs = float(w_bytes.item()) / (dec_ms * 1e-3) / 1e9
+        if rank == 0:
+            line = {"metric": f"decode tok/s (bs1, {metric_model}, after a {n_prompt}-token "
+                              f"prefill, pipelined)", "value": 1000.0 / dec_ms, "unit": "tok/s",
+                    "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                    "ms_per_step": dec_ms, "higher_is_better": True, "scaling": "strong",
+                    "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+                    "config": {"workload": tag, "prompt_len": n_prompt, "gen_tokens": n_gen,
+                               "parallelism": f"pp{world}",
+                               "stages": [p.num_layers for p in
+                                          plan_stages(cfg.num_hidden_layers, world)],
+                               "l2": "inputs larger than L2"},
+                    "ttft_ms": ttft * 1e3, "prefill_tok_s": n_prompt / ttft,
+                    "hbm": {"weight_bytes_per_token": float(w_bytes.item()),
+                            "aggregate_gbs": gbs, "frac_of_one_gpu": gbs / peaks["hbm_gbs"],
+                            "peak": peaks["hbm_gbs"]},
+                    "clocks": clk.summary(), "device_status": status, "last_token": last}
+            print(json.dumps(line), flush=True)
+        _sync_all()
+    finally:
+        dist.destroy_process_group()
+
+
+def run_pipeline_ragged(args) -> None:
+    """N > 1: 32 sessions with KV lengths uniform in
+    [128, 8192] (seed 2), the decoder split evenly into N stages, the
+    sessions cut into N micro-batches that are in flight on different stages
+    at once (dial_b200.pipeline.MicroBatchRunner); one decode token per
+    session per iteration, CUDA events on every rank, max over ranks."""
+    import hashlib
+
+    import numpy as np
+    import torch
+
+    import dial_b200
+    from dial_b200.pipeline import MicroBatchRunner, plan_stages
+
+    rank, world, local, dev = _pipeline_init()
+    try:
+        n_sess = 32
+        n_micro = world
+        lengths = np.random.default_rng(2).integers(128, 8193, size=n_sess).astype(np.int32)
+        cfg = dial_b200.Config(max_seq_len=8192 + args.steps + args.warmup + 16,
+                               max_sessions=n_sess, max_tokens=64)
+        plan = plan_stages(cfg.num_hidden_layers, world)[rank]
+        eng = dial_b200.Engine(cfg, first_layer=plan.first_layer, num_layers=plan.num_layers,
+                               device=local)
+        eng.load_synthetic(seed=0)
+        for sidx in range(n_sess):
+            eng.session_fill_random(sidx, int(lengths[sidx]), seed=2 + sidx)
+        runner = MicroBatchRunner(eng, plan, cfg.hidden_size, n_sess, n_micro)
+        stream = torch.cuda.Stream(dev)
+        with torch.cuda.stream(stream):
+            runner.prepare(np.arange(n_sess), lengths, _prompt_tokens(cfg.vocab_size, n_sess))
+            for _ in range(args.warmup):
+                runner.iteration()
+            runner.finish()
+            _sync_all()
+            ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            with ClockSampler(local) as clk:
+                ev0.record(stream)
+                for _ in range(args.steps):
+                    runner.iteration()
+                runner.finish()
+                ev1.record(stream)
+                ev1.synchronize()
+            _sync_all()
+            it_ms = _max_over_ranks(ev0.elapsed_time(ev1) / args.steps, dev)
+            toks = runner.tokens()
+        status = dial_b200.device_status()
+        if rank == 0:
+            line = {"metric": "decode tok/s (32 ragged sessions, KV 128-8192, Qwen3-8B W8A16, "
+                              "pipelined)", "value": n_sess * 1000.0 / it_ms, "unit": "tok/s",
+                    "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                    "ms_per_step": it_ms, "higher_is_better": True, "scaling": "strong",
+                    "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+                    "config": {"workload": "qwen3-8b-w8a16-ragged32", "sessions": n_sess,
+                               "kv_lengths": "U[128, 8192] seed 2",
+                               "kv_tokens": int(lengths.sum()), "page_tokens": 16,
+                               "parallelism": f"pp{world}", "micro_batches": n_micro,
+                               "stages": [p.num_layers for p in plan_stages(36, world)],
+                               "l2": "inputs larger than L2"},
+                    "clocks": clk.summary(), "device_status": status,
+                    "tokens_sha256": hashlib.sha256(toks.astype("<i4").tobytes()).hexdigest()}
+            print(json.dumps(line), flush=True)
+        _sync_all()
+    finally:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
 
 
 def run_prefill2048(args) -> dict:
@@ -722,12 +919,22 @@ def main():
                     help="decode (bs1 Qwen3-8B W8A16 decode, the headline metric), prefill2048 "
                          "(2048-token prefill then decode), ragged32 (32 ragged sessions), "
                          "fp8_27b / nvfp4_27b (27B-class decoder with FP8 block-128 or NVFP4 "
-                         "linears); all on one GPU")
+                         "linears); with --gpus N > 1 each runs as N pipeline stages "
+                         "(ragged32 with N micro-batches in flight)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
+        return
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if world == 1 and args.gpus > 1:
+        _relaunch_with_torchrun(args)
+    if world > 1 and args.workload != "decode":
+        if args.workload == "ragged32":
+            run_pipeline_ragged(args)
+        else:
+            run_pipeline_long(args)
         return
     if args.workload != "decode":
         if args.workload == "prefill2048":
@@ -739,12 +946,9 @@ def main():
                              else "FMT_NVFP4_G16")
         print(json.dumps(r), flush=True)
         return
-    world = int(os.environ.get("WORLD_SIZE", "1"))
     if world > 1:
         run_pipeline(args)
         return
-    if args.gpus > 1:
-        _relaunch_with_torchrun(args)
     r = run_single(args)
     cpu = None if args.no_cpu_baseline else cpu_decode_sample()
     line = {
