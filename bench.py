@@ -394,6 +394,21 @@ def run_pipeline(args) -> None:
             if plan.is_first:
                 first.fill_(int(check[0]))
 
+            # ---- the stage hop: NCCL send/recv, or the peer-memory link
+            # (DIAL_B200_PEER_LINK=1; NCCL again if it cannot open on every rank)
+            transport = "nccl"
+            if os.environ.get("DIAL_B200_PEER_LINK", "0") == "1":
+                transport = "peer"
+                try:
+                    runner.link()
+                except Exception as e:  # noqa: BLE001  (reported, the NCCL path still runs)
+                    transport = f"nccl ({type(e).__name__}: {e})"
+            peer = transport == "peer"
+            ok = torch.tensor([1 if peer else 0], dtype=torch.int32, device=dev)
+            dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+            if peer and int(ok.item()) == 0:
+                peer, transport = False, "nccl (the link did not open on every rank)"
+
             # ---- device-resident decode: tokens stay on the GPUs
             def loop_step(ev_a=None, ev_b=None):
                 stream.synchronize()  # the previous step's graphs read the positions
@@ -401,11 +416,15 @@ def run_pipeline(args) -> None:
                 tok = first.clone() if plan.is_first else None
                 if ev_a is not None:
                     ev_a.record(stream)
-                for _ in range(GEN_TOKENS):
-                    tok = runner.decode_step(tok)
+                if peer:
+                    last = runner.decode_linked(tok, GEN_TOKENS)
+                else:
+                    for _ in range(GEN_TOKENS):
+                        tok = runner.decode_step(tok)
+                    last = int(tok.item()) if plan.is_first else None
                 if ev_b is not None:
                     ev_b.record(stream)
-                return tok
+                return last
 
             for _ in range(args.warmup):
                 loop_step()
@@ -419,7 +438,7 @@ def run_pipeline(args) -> None:
                 torch.cuda.synchronize()
             sync_all()
             step_ms = max_over_ranks(sum(a.elapsed_time(b) for a, b in evs) / args.steps)
-            last_loop = int(last_loop.item()) if plan.is_first else -1
+            last_loop = last_loop if plan.is_first else -1
 
             # ---- end to end: each token goes host -> stage 0 and back to the host
             pin_in = torch.zeros(1, dtype=torch.int32).pin_memory()
@@ -429,18 +448,24 @@ def run_pipeline(args) -> None:
             def e2e_step():
                 stream.synchronize()
                 runner.decode_prepare(PROMPT_LEN)
-                if plan.is_first:
-                    pin_out.fill_(int(check[0]))
+                tok_host = int(check[0]) if plan.is_first else 0
                 for _ in range(GEN_TOKENS):
                     if plan.is_first:
-                        pin_in.copy_(pin_out)
+                        pin_in.fill_(tok_host)
                         tok_dev.copy_(pin_in, non_blocking=True)
-                        out = runner.decode_step(tok_dev)
-                        pin_out.copy_(out, non_blocking=True)
-                        stream.synchronize()
+                        if peer:
+                            eng.stage_link_step(1, tok_dev)
+                            tok_host = int(eng.stage_link_finish(1)[0])
+                        else:
+                            out = runner.decode_step(tok_dev)
+                            pin_out.copy_(out, non_blocking=True)
+                            stream.synchronize()
+                            tok_host = int(pin_out.item())
+                    elif peer:
+                        eng.stage_link_step(1, None)
                     else:
                         runner.decode_step(None)
-                return int(pin_out.item())
+                return tok_host
 
             for _ in range(args.warmup):
                 e2e_step()
@@ -451,28 +476,28 @@ def run_pipeline(args) -> None:
             torch.cuda.synchronize()
             e2e_s = max_over_ranks(time.perf_counter() - t0)
 
-            # ---- stage handoff alone: [1, H] bf16 ping-pong between ranks 0 and 1
+            # ---- each stage's own compute per token (its stage graph, no hop), summed
+            # over the stages: the rest of the pipelined per-token time is the hops
+            h_loc = torch.zeros(1, cfg.hidden_size, dtype=torch.bfloat16, device=dev)
+            t_in = torch.zeros(1, dtype=torch.int32, device=dev)
+            t_out = torch.zeros(1, dtype=torch.int32, device=dev)
+            eng.stage_prepare([0], [PROMPT_LEN])
+            for _ in range(4):
+                eng.stage_step(1, t_in if plan.is_first else None, h_loc,
+                               t_out if plan.is_last else None)
             ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            x = torch.zeros(1, cfg.hidden_size, dtype=torch.bfloat16, device=dev)
-            sync_all()
-            reps = 50
-            if rank in (0, 1):
-                for i in range(reps + 5):
-                    if i == 5:
-                        torch.cuda.synchronize()
-                        ev0.record(stream)
-                    if rank == 0:
-                        dist.send(x, 1)
-                        dist.recv(x, 1)
-                    else:
-                        dist.recv(x, 0)
-                        dist.send(x, 0)
-                ev1.record(stream)
-                ev1.synchronize()
-                hop_us = ev0.elapsed_time(ev1) * 1000.0 / (2 * reps)
-            else:
-                hop_us = 0.0
-            hop_us = max_over_ranks(hop_us)
+            torch.cuda.synchronize()
+            ev0.record(stream)
+            for _ in range(64):
+                eng.stage_step(1, t_in if plan.is_first else None, h_loc,
+                               t_out if plan.is_last else None)
+            ev1.record(stream)
+            ev1.synchronize()
+            stage_us = torch.tensor([ev0.elapsed_time(ev1) * 1000.0 / 64], dtype=torch.float64,
+                                    device=dev)
+            dist.all_reduce(stage_us)
+            compute_us = float(stage_us.item())
+            hop_us = max(0.0, (step_ms * 1000.0 / GEN_TOKENS - compute_us) / world)
 
             # ---- dominant kernel live on this rank: fused gate/up GEMV, rotating layers
             layers = list(range(plan.first_layer, plan.first_layer + plan.num_layers))
@@ -485,7 +510,10 @@ def run_pipeline(args) -> None:
             ev1.synchronize()
             k_us = ev0.elapsed_time(ev1) * 1000.0 / iters
             k_bytes = eng.linear_bytes(layers[0], 2, 1)
-        per_stage = plan.num_layers * 5 + int(plan.is_first) + 2 * int(plan.is_last) + 1
+        # per stage and token: 5 per layer, embed (first), head (last), position advance,
+        # and with the link a receive and a send kernel
+        per_stage = plan.num_layers * 5 + int(plan.is_first) + 2 * int(plan.is_last) + 1 + \
+            (2 if peer else 0)
         launches = torch.tensor([per_stage * GEN_TOKENS * args.steps], dtype=torch.int64,
                                 device=dev)
         dist.all_reduce(launches)
@@ -511,7 +539,10 @@ def run_pipeline(args) -> None:
                              "peak_source": peaks["source"]},
                 "cpu_baseline": None, "clocks": clk.summary(),
                 "gpu_launches": int(launches.item()), "ttft_s": ttft,
-                "handoff_us": hop_us, "device_status": status,
+                "transport": transport, "handoff_us": hop_us,
+                "handoff_note": "per hop: (pipelined ms per token - sum of the stages' own "
+                                "compute per token) / stages",
+                "stage_compute_us_sum": compute_us, "device_status": status,
                 "tokens": tokens_report(check),
                 "loop_consistent": bool(last_loop == last_e2e),
             }

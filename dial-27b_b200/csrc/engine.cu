@@ -21,6 +21,7 @@
 #include "gemm.h"
 #include "gemv.h"
 #include "layout.h"
+#include "link.h"
 #include "trace.h"
 #include "misc.h"
 
@@ -413,6 +414,13 @@ struct dial_b200_engine {
   DevBuf gemm_part;             // split-K partial sums of small-row GEMM calls
   DevBuf trace;                 // DIAL_B200_TRACE=<csv>: per-CTA timeline of decode steps
   std::string trace_path;
+  // stage link over peer memory (link.h): this stage's inbox (IPC-exported),
+  // counters [hidden received, tokens received, hidden sent, tokens sent], the
+  // opened inboxes of the next stage and (last stage) of the first stage
+  DevBuf link_in, link_cnt;
+  uint8_t* link_next = nullptr;
+  uint8_t* link_first = nullptr;
+  std::map<std::tuple<int64_t, const void*>, std::unique_ptr<Graph>> link_graphs;
   int32_t* h_in = nullptr;   // pinned: [3][max_rows] tokens, sids, positions
   int32_t* h_out = nullptr;  // pinned: [max_rows] tokens + status
   int* status = nullptr;
@@ -1111,6 +1119,9 @@ void dial_b200_engine_destroy(dial_b200_engine* eng) {
   eng->step_graphs.clear();
   eng->loop_graphs.clear();
   eng->stage_graphs.clear();
+  eng->link_graphs.clear();
+  if (eng->link_next) cudaIpcCloseMemHandle(eng->link_next);
+  if (eng->link_first && eng->link_first != eng->link_next) cudaIpcCloseMemHandle(eng->link_first);
   if (eng->h_in) cudaFreeHost(eng->h_in);
   if (eng->h_out) cudaFreeHost(eng->h_out);
   cudaStream_t s = eng->stream;
@@ -1431,6 +1442,132 @@ int dial_b200_stage_step(dial_b200_engine* eng, int64_t rows, const int32_t* tok
                          size_t n) {
   return dial_b200_stage_step_rows(eng, 0, rows, tokens_dev, hidden, tokens_out_dev, stream, err,
                                    n);
+}
+
+int dial_b200_stage_link_handle(dial_b200_engine* eng, void* handle_out, char* err, size_t n) {
+  return guarded(err, n, [&] {
+    DIAL_CHECK(eng && handle_out, "null pointer argument");
+    DIAL_CUDA(cudaSetDevice(eng->device));
+    if (!eng->link_in.p) {
+      eng->link_in.alloc(link_inbox_bytes(eng->max_rows_decode, eng->H));
+      DIAL_CUDA(cudaMemset(eng->link_in.p, 0, eng->link_in.bytes));
+      eng->link_cnt.alloc(4 * sizeof(uint64_t));
+      DIAL_CUDA(cudaMemset(eng->link_cnt.p, 0, eng->link_cnt.bytes));
+    }
+    cudaIpcMemHandle_t h;
+    DIAL_CUDA(cudaIpcGetMemHandle(&h, eng->link_in.p));
+    std::memcpy(handle_out, &h, sizeof(h));
+  });
+}
+
+int dial_b200_stage_link_open(dial_b200_engine* eng, const void* next_handle,
+                              const void* first_handle, char* err, size_t n) {
+  return guarded(err, n, [&] {
+    DIAL_CHECK(eng, "null engine");
+    DIAL_CUDA(cudaSetDevice(eng->device));
+    DIAL_CHECK(eng->link_in.p, "call dial_b200_stage_link_handle first");
+    DIAL_CHECK(!eng->link_next && !eng->link_first, "the stage link is already open");
+    DIAL_CHECK(eng->cfg.has_head || next_handle, "a stage without the head needs the next stage");
+    DIAL_CHECK(!eng->cfg.has_head || eng->cfg.has_embed || first_handle,
+               "the last stage needs the first stage's inbox");
+    auto open = [&](const void* hp) -> uint8_t* {
+      cudaIpcMemHandle_t h;
+      std::memcpy(&h, hp, sizeof(h));
+      void* p = nullptr;
+      DIAL_CUDA(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess));
+      return static_cast<uint8_t*>(p);
+    };
+    if (!eng->cfg.has_head) eng->link_next = open(next_handle);
+    if (eng->cfg.has_head && !eng->cfg.has_embed) eng->link_first = open(first_handle);
+  });
+}
+
+int dial_b200_stage_link_step(dial_b200_engine* eng, int64_t rows, const int32_t* tokens_dev,
+                              void* stream, char* err, size_t n) {
+  return guarded(err, n, [&] {
+    DIAL_CHECK(eng, "null engine");
+    DIAL_CUDA(cudaSetDevice(eng->device));
+    const int M = static_cast<int>(rows);
+    DIAL_CHECK(M >= 1 && M <= eng->max_rows_decode && M <= 256, "rows %d out of range", M);
+    DIAL_CHECK(!(eng->cfg.has_embed && eng->cfg.has_head),
+               "an engine that owns the whole model has no stage link");
+    DIAL_CHECK((eng->cfg.has_head ? eng->link_first : eng->link_next) != nullptr,
+               "the stage link is not open");
+    DIAL_CHECK(eng->cfg.has_embed || !tokens_dev, "only the first stage takes token ids");
+    check_weights(eng, eng->cfg.first_layer, eng->cfg.num_layers);
+    if (eng->cfg.has_head) DIAL_CHECK(eng->lm_head.ready(), "lm_head weights not loaded");
+    // tokens_dev (first stage): this step's tokens come from the caller (the
+    // first step after a prepare or a finish); null: from the last stage
+    const auto key = std::make_tuple(rows, static_cast<const void*>(tokens_dev));
+    auto it = eng->link_graphs.find(key);
+    if (it == eng->link_graphs.end()) {
+      cudaStream_t s = eng->stream;
+      auto g = std::make_unique<Graph>();
+      uint64_t* cnt = eng->link_cnt.as<uint64_t>();
+      const uint8_t* inbox = eng->link_in.as<uint8_t>();
+      const int mr = eng->max_rows_decode;
+      const bool pdl = g_tuning().pdl;
+      DIAL_CUDA(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
+      try {
+        if (eng->cfg.has_embed) {
+          const int32_t* toks = tokens_dev;
+          if (!toks) {
+            DIAL_CUDA(link_recv_launch(inbox, kLinkTokens, mr, cnt + 1, eng->tok_in.p, M * 4,
+                                       eng->status, s));
+            toks = eng->tok_in.as<int32_t>();
+          }
+          DIAL_CUDA(embed_launch(eng->embed.p, toks, M, eng->V, eng->H, eng->hidden.p, eng->H,
+                                 eng->status, s, pdl));
+        } else {
+          DIAL_CUDA(link_recv_launch(inbox, kLinkHidden, mr, cnt + 0, eng->hidden.p,
+                                     static_cast<size_t>(M) * eng->H * 2, eng->status, s));
+        }
+        for (int li = 0; li < eng->cfg.num_layers; ++li)
+          layer_decode(eng, eng->layers[li], eng->hidden.p, M, s);
+        if (eng->cfg.has_head) {
+          head_forward(eng, eng->hidden.p, M, nullptr, eng->tok_out.as<int32_t>(), s);
+          DIAL_CUDA(link_send_launch(eng->link_first, kLinkTokens, mr, cnt + 3, eng->tok_out.p,
+                                     M * 4, eng->status, s, pdl));
+        } else {
+          DIAL_CUDA(link_send_launch(eng->link_next, kLinkHidden, mr, cnt + 2, eng->hidden.p,
+                                     static_cast<size_t>(M) * eng->H * 2, eng->status, s, pdl));
+        }
+        DIAL_CUDA(advance_launch(nullptr, nullptr, eng->pos.as<int32_t>(), M, s, pdl));
+      } catch (...) {
+        cudaGraph_t tmp = nullptr;
+        cudaStreamEndCapture(s, &tmp);
+        if (tmp) cudaGraphDestroy(tmp);
+        throw;
+      }
+      DIAL_CUDA(cudaStreamEndCapture(s, &g->g));
+      DIAL_CUDA(cudaGraphInstantiate(&g->exec, g->g, 0));
+      it = eng->link_graphs.emplace(key, std::move(g)).first;
+    }
+    DIAL_CUDA(cudaGraphLaunch(it->second->exec, static_cast<cudaStream_t>(stream)));
+  });
+}
+
+int dial_b200_stage_link_finish(dial_b200_engine* eng, int64_t rows, int32_t* tokens_host,
+                                void* stream, char* err, size_t n) {
+  return guarded(err, n, [&] {
+    DIAL_CHECK(eng, "null engine");
+    DIAL_CUDA(cudaSetDevice(eng->device));
+    DIAL_CHECK(eng->cfg.has_embed && !eng->cfg.has_head, "only the first stage finishes a run");
+    DIAL_CHECK(eng->link_in.p, "the stage link is not open");
+    const int M = static_cast<int>(rows);
+    DIAL_CHECK(M >= 1 && M <= eng->max_rows_decode, "rows %d out of range", M);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    DIAL_CUDA(link_recv_launch(eng->link_in.as<uint8_t>(), kLinkTokens, eng->max_rows_decode,
+                               eng->link_cnt.as<uint64_t>() + 1, eng->tok_in.p, M * 4, eng->status,
+                               s));
+    if (tokens_host) {
+      DIAL_CUDA(cudaMemcpyAsync(tokens_host, eng->tok_in.p, M * 4, cudaMemcpyDeviceToHost, s));
+      DIAL_CUDA(cudaStreamSynchronize(s));
+      int st = 0;
+      DIAL_CUDA(cudaMemcpy(&st, eng->status, 4, cudaMemcpyDeviceToHost));
+      check_status(eng, st);
+    }
+  });
 }
 
 void* dial_b200_engine_stream(dial_b200_engine* eng) { return eng ? eng->stream : nullptr; }

@@ -104,6 +104,10 @@ _SIGS = {
     "dial_b200_stage_step": (C.c_int, [_vp, _i64, _vp, _vp, _vp, _vp, *_err]),
     "dial_b200_stage_step_rows": (C.c_int, [_vp, _i64, _i64, _vp, _vp, _vp, _vp, *_err]),
     "dial_b200_gdn_scratch_bytes": (_i64, [C.POINTER(GdnShape), _i64]),
+    "dial_b200_stage_link_handle": (C.c_int, [_vp, _vp, *_err]),
+    "dial_b200_stage_link_open": (C.c_int, [_vp, _vp, _vp, *_err]),
+    "dial_b200_stage_link_step": (C.c_int, [_vp, _i64, _vp, _vp, *_err]),
+    "dial_b200_stage_link_finish": (C.c_int, [_vp, _i64, _vp, _vp, *_err]),
     "dial_b200_gdn_forward": (C.c_int, [C.POINTER(GdnShape), _vp, _vp, _vp, _vp, _vp, _vp, _vp,
                                         _vp, _vp, _vp, _i64, _i64, _vp, _vp, _vp, *_err]),
     "dial_b200_engine_create": (C.c_int, [C.POINTER(ModelConfig), C.c_int, C.POINTER(_vp), *_err]),

@@ -282,6 +282,33 @@ class Engine:
         call("dial_b200_stage_step_rows", self._h, row_offset, rows, ptr(tokens), ptr(hidden),
              ptr(tokens_out), self._stream_ptr())
 
+    # ------------------------------------------------------ stage link (peer memory)
+    def stage_link_handle(self) -> bytes:
+        """64-byte CUDA IPC handle of this stage's inbox (allocated on first use)."""
+        buf = (C.c_char * 64)()
+        call("dial_b200_stage_link_handle", self._h, C.cast(buf, C.c_void_p))
+        return bytes(buf)
+
+    def stage_link_open(self, next_handle: bytes | None, first_handle: bytes | None):
+        """Map the next stage's inbox (all but the last stage) and the first
+        stage's inbox (the last stage)."""
+        nb = C.create_string_buffer(next_handle, 64) if next_handle else None
+        fb = C.create_string_buffer(first_handle, 64) if first_handle else None
+        call("dial_b200_stage_link_open", self._h, C.cast(nb, C.c_void_p) if nb else None,
+             C.cast(fb, C.c_void_p) if fb else None)
+
+    def stage_link_step(self, rows: int, tokens: torch.Tensor | None = None):
+        """One linked decode step of this stage on the current stream; the first
+        stage passes the tokens on the first step of a run, None after it."""
+        call("dial_b200_stage_link_step", self._h, rows,
+             C.c_void_p(tokens.data_ptr() if tokens is not None else 0), self._stream_ptr())
+
+    def stage_link_finish(self, rows: int) -> np.ndarray:
+        """First stage: receive the last step's tokens (synchronizes)."""
+        out = np.empty(rows, dtype=np.int32)
+        call("dial_b200_stage_link_finish", self._h, rows, _np_ptr(out), self._stream_ptr())
+        return out
+
     def session_fill_random(self, session: int, length: int, seed: int, std: float = 1.0):
         call("dial_b200_session_fill_random", self._h, session, length, seed,
              _np_ptr(normal_table_bits(std)))

@@ -2,7 +2,8 @@
 
     PYTHONPATH=dial-27b_b200 python -m dial_b200.microbench [--shapes q,gate_up] [--M 1,4,16]
         [--iters 20] [--min-footprint-mb 512]
-    PYTHONPATH=dial-27b_b200 python -m dial_b200.microbench --replay gate_up --layers 4 --M 1
+    PYTHONPATH=dial-27b_b200 python -m dial_b200.microbench --replay gate_up --layers 4 --M 1 \
+        [--model 27b --fmt nvfp4]
 
 Each case builds enough copies of the quantized weight that one rotation
 through them streams more than the L2 cache (126 MB) from HBM, captures the
@@ -114,17 +115,21 @@ def run_prefill(n_prompt: int) -> dict:
 LINEARS = {"qkv": 0, "o": 1, "gate_up": 2, "down": 3}
 
 
-def run_replay(name: str, layers: int, rows: int, iters: int) -> dict:
+def run_replay(name: str, layers: int, rows: int, iters: int, model: str = "8b",
+               fmt: str = "w8a16") -> dict:
     """One decode-step linear of the synthetic Qwen3-8B W8A16 engine (the
     epilogue the decode step uses: fused RMSNorm + SwiGLU for gate_up, RMSNorm
     for qkv, residual add for o and down) replayed `iters` times, rotating over
     `layers` layers so that no launch finds its weights in L2
     (dial_b200_engine_linear_replay).  A small device footprint for profiler
     captures of the exact kernel variant the decode step runs."""
+    from . import _abi
     from .engine import Config, Engine
 
-    cfg = Config(num_hidden_layers=layers, max_seq_len=64, max_sessions=1,
-                 max_tokens=max(rows, 16))
+    fmts = {"w8a16": _abi.FMT_W8A16_ROW, "fp8": _abi.FMT_FP8_BLOCK128, "nvfp4": _abi.FMT_NVFP4_G16}
+    base = Config.dense_27b if model == "27b" else Config
+    cfg = base(num_hidden_layers=layers, max_seq_len=64, max_sessions=1,
+               max_tokens=max(rows, 16), linear_fmt=fmts[fmt])
     eng = Engine(cfg, device=0, has_embed=False, has_head=False)
     eng.load_synthetic(seed=0)
     which = LINEARS[name]
@@ -139,7 +144,8 @@ def run_replay(name: str, layers: int, rows: int, iters: int) -> dict:
     nbytes = eng.linear_bytes(0, which, rows)
     peak, src = measured_hbm_gbs()
     gbs = nbytes / (us * 1e-6) / 1e9
-    return {"linear": name, "rows": rows, "layers": layers, "us": us, "bytes": nbytes,
+    return {"linear": name, "model": model, "fmt": fmt, "rows": rows, "layers": layers, "us": us,
+            "bytes": nbytes,
             "GB_s": gbs, "frac_hbm": gbs / peak, "peak_gbs": peak, "peak_source": src}
 
 
@@ -155,11 +161,16 @@ def main(argv=None):
                     help="instead: replay one decode-step linear (qkv, o, gate_up, down) of a "
                          "--layers-layer synthetic engine, --M rows (first value)")
     ap.add_argument("--layers", type=int, default=4)
+    ap.add_argument("--model", default="8b", choices=["8b", "27b"],
+                    help="--replay: Qwen3-8B shapes or the 27B-class decoder's")
+    ap.add_argument("--fmt", default="w8a16", choices=["w8a16", "fp8", "nvfp4"],
+                    help="--replay: weight format of the engine's layer linears")
     args = ap.parse_args(argv)
     torch.cuda.set_device(0)
     if args.replay:
         rows = int(args.M.split(",")[0])
-        print(json.dumps(run_replay(args.replay, args.layers, rows, args.iters)), flush=True)
+        print(json.dumps(run_replay(args.replay, args.layers, rows, args.iters, args.model,
+                                    args.fmt)), flush=True)
         return
     if args.prefill > 0:
         print(json.dumps(run_prefill(args.prefill)), flush=True)

@@ -153,6 +153,32 @@ class StageRunner:
             tok = self._tok_in
         return tok
 
+    # ------------------------------------------------ peer-memory stage link
+    def link(self):
+        """Open the peer-memory stage link (collective over the group): every
+        rank publishes its inbox's IPC handle, stage s maps stage s + 1's and
+        the last stage maps stage 0's.  Afterwards decode_linked runs the
+        decode loop with no NCCL call and no host synchronisation per token."""
+        p = self.plan
+        mine = self.eng.stage_link_handle()
+        handles = [None] * p.world
+        dist.all_gather_object(handles, mine, group=self.group)
+        self.eng.stage_link_open(None if p.is_last else handles[p.rank + 1],
+                                 handles[0] if p.is_last else None)
+        self.linked = True
+
+    def decode_linked(self, token: torch.Tensor | None, n_steps: int) -> int | None:
+        """`n_steps` bs1 decode tokens over the stage link from position
+        decode_prepare set; stage 0 passes the first token (device int32 [1])
+        and gets the last sampled token id back (host int), others None."""
+        p = self.plan
+        for i in range(n_steps):
+            self.eng.stage_link_step(1, token if (p.is_first and i == 0) else None)
+        self.pos += n_steps
+        if p.is_first:
+            return int(self.eng.stage_link_finish(1)[0])
+        return None
+
     def generate(self, prompt, n_gen: int) -> np.ndarray | None:
         """Greedy generation of `n_gen` tokens after `prompt` (host ids on
         stage 0; ignored elsewhere).  Returns the ids on stage 0, else None."""

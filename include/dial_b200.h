@@ -341,6 +341,32 @@ int dial_b200_stage_step_rows(dial_b200_engine* eng, int64_t row_offset, int64_t
                               const int32_t* tokens_dev, void* hidden, int32_t* tokens_out_dev,
                               void* stream, char* err, size_t err_size);
 
+/* Stage link over peer memory: the in-box hop between pipeline stages on
+ * different GPUs without NCCL (spm/client.rs:391-453 send, spm/worker.rs:
+ * 740-796 receive).  Each stage owns an inbox in its own HBM;
+ * dial_b200_stage_link_handle writes the 64-byte CUDA IPC handle of it, the
+ * processes exchange the handles, and dial_b200_stage_link_open maps the next
+ * stage's inbox (every stage but the last) and the first stage's (the last
+ * stage).  Then dial_b200_stage_link_step is one decode step of this stage as
+ * one CUDA graph on `stream`: [receive the hidden state (or, first stage, the
+ * tokens) from this stage's inbox ->] embed / owned layers / head [-> write
+ * the hidden state (or the sampled tokens) into the next (first) stage's
+ * inbox], positions advanced; the receive waits on device (bounded:
+ * DIAL_ERR_DEVICE after 2 s) and the first layer's weights stream meanwhile.
+ * The first stage passes tokens_dev on the first step of a run (after
+ * dial_b200_stage_prepare or a finish) and NULL after it;
+ * dial_b200_stage_link_finish (first stage) receives the last step's tokens
+ * into tokens_host (synchronizes), so every message sent is received.  The
+ * stages must run on distinct GPUs (a receive waits for another GPU). */
+int dial_b200_stage_link_handle(dial_b200_engine* eng, void* handle_out, char* err,
+                                size_t err_size);
+int dial_b200_stage_link_open(dial_b200_engine* eng, const void* next_handle,
+                              const void* first_handle, char* err, size_t err_size);
+int dial_b200_stage_link_step(dial_b200_engine* eng, int64_t rows, const int32_t* tokens_dev,
+                              void* stream, char* err, size_t err_size);
+int dial_b200_stage_link_finish(dial_b200_engine* eng, int64_t rows, int32_t* tokens_host,
+                                void* stream, char* err, size_t err_size);
+
 /* Copy the loop's current tokens/positions back to host (synchronizes). */
 int dial_b200_decode_loop_state(dial_b200_engine* eng, int64_t rows, int32_t* tokens_host,
                                 int32_t* positions_host, char* err, size_t err_size);

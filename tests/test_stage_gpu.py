@@ -126,3 +126,72 @@ def test_nccl_pipeline_two_gpus_matches_whole_model(cuda, tmp_path):
     mp.start_processes(_nccl_worker, args=(2, _free_port(), prompt, 12, str(out)), nprocs=2,
                        start_method="spawn", join=True)
     np.testing.assert_array_equal(np.load(out), want)
+
+
+def _link_worker(rank, world, port, prompt, n_gen, out_path):
+    sys.path[:0] = [str(ROOT / "dial-27b_b200")]
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    import datetime
+
+    import torch.distributed as dist
+
+    import dial_b200
+    from dial_b200.pipeline import StageRunner, plan_stages
+
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        cfg = _cfg(dial_b200)
+        plan = plan_stages(cfg.num_hidden_layers, world)[rank]
+        eng = dial_b200.Engine(cfg, first_layer=plan.first_layer, num_layers=plan.num_layers,
+                               device=rank)
+        eng.load_synthetic(seed=7)
+        runner = StageRunner(eng, plan, cfg.hidden_size)
+        runner.link()
+        n = len(prompt)
+        toks = torch.as_tensor(prompt, device=f"cuda:{rank}") if plan.is_first else None
+        first = runner.step(toks, n, 0)  # prefill through the NCCL path
+        first_dev = first.clone() if plan.is_first else None
+        # one linked run of n_gen - 1 steps: the tokens stay on the devices
+        runner.decode_prepare(n)
+        last = runner.decode_linked(first_dev, n_gen - 1)
+        # token by token (a run of one step each): every sampled id reaches the host
+        runner.decode_prepare(n)
+        seq, tok = [], first_dev
+        for _ in range(n_gen - 1):
+            t = runner.decode_linked(tok, 1)
+            if plan.is_first:
+                seq.append(t)
+                tok = torch.tensor([t], dtype=torch.int32, device=f"cuda:{rank}")
+        torch.cuda.synchronize()
+        assert dial_b200.device_status() == 0
+        if rank == 0:
+            np.save(out_path, np.asarray([int(first.item())] + seq + [last], np.int32))
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_peer_link_pipeline_two_gpus_matches_whole_model(cuda, tmp_path):
+    """The peer-memory stage link (dial_b200_stage_link_*): a linked run keeps
+    the tokens on the devices and its last token, and a run of one-step runs
+    returns every token, both equal to the whole-model engine's greedy decode."""
+    import torch.multiprocessing as mp
+
+    import dial_b200
+
+    cfg = _cfg(dial_b200)
+    prompt = np.random.default_rng(6).integers(0, cfg.vocab_size, size=9).astype(np.int32)
+    n_gen = 12
+    full = dial_b200.Engine(cfg)
+    full.load_synthetic(seed=7)
+    want, _, _ = full.generate(prompt, n_gen)
+    out = tmp_path / "link.npy"
+    mp.start_processes(_link_worker, args=(2, _free_port(), prompt, n_gen, str(out)), nprocs=2,
+                       start_method="spawn", join=True)
+    got = np.load(out)
+    np.testing.assert_array_equal(got[:n_gen], want)
+    assert got[n_gen] == want[-1]
