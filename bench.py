@@ -394,10 +394,11 @@ def run_pipeline(args) -> None:
             if plan.is_first:
                 first.fill_(int(check[0]))
 
-            # ---- the stage hop: NCCL send/recv, or the peer-memory link
-            # (DIAL_B200_PEER_LINK=1; NCCL again if it cannot open on every rank)
+            # ---- the stage hop: the peer-memory link (default), or NCCL
+            # send/recv (DIAL_B200_PEER_LINK=0, or when the link cannot open on
+            # every rank)
             transport = "nccl"
-            if os.environ.get("DIAL_B200_PEER_LINK", "0") == "1":
+            if os.environ.get("DIAL_B200_PEER_LINK", "1") == "1":
                 transport = "peer"
                 try:
                     runner.link()

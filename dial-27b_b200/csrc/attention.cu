@@ -286,6 +286,9 @@ cudaError_t attn_decode_launch(const AttnDecodeArgs& a, int act, cudaStream_t s,
       a.sh.q_heads % a.sh.kv_heads != 0)
     return cudaErrorInvalidValue;
   if (a.splits > 1 && (!a.part_o || !a.part_ml || !a.counters)) return cudaErrorInvalidValue;
+  // steps of many rows: the tensor-core form when the pool size is known
+  if (a.M > 4 && a.num_blocks > 0 && attn_decode_mma_supported(a))
+    return attn_decode_mma_launch(a, act, s, pdl);
   return act == 0 ? launch_decode_act<__nv_bfloat16>(a, s, pdl)
                   : launch_decode_act<__half>(a, s, pdl);
 }

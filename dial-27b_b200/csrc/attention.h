@@ -61,7 +61,15 @@ struct AttnDecodeArgs {
   int tok_split;
   unsigned long long* trace; // opt-in timeline records (common.cuh), null = off
   int trace_tag;
+  // Pages in each of the kv.k / kv.v pools ([num_blocks][kv_heads][16][128]).
+  // Non-zero selects the tensor-core form (attn_decode_mma.cu) for steps of
+  // more than 4 rows; 0 keeps the CUDA-core forms.
+  int num_blocks;
+  int mma_ring;  // tensor-core form: page slots per warp, 2 (default) or 3
 };
+
+bool attn_decode_mma_supported(const AttnDecodeArgs& a);
+cudaError_t attn_decode_mma_launch(const AttnDecodeArgs& a, int act, cudaStream_t s, bool pdl);
 
 // Scratch bytes needed for (M, splits).
 size_t attn_decode_scratch_bytes(const AttnShape& sh, int M, int splits);

@@ -298,12 +298,16 @@ GemvTuning g_tuning() {
   GemvTuning t;
   if (const char* v = std::getenv("DIAL_B200_GEMV_SLOTS")) t.slots = std::atoi(v);
   if (const char* v = std::getenv("DIAL_B200_GEMV_GRID")) t.grid = std::atoi(v);
+  if (const char* v = std::getenv("DIAL_B200_GEMV_NVFP4_STAGE")) t.nvfp4_stage = std::atoi(v);
   if (const char* v = std::getenv("DIAL_B200_PDL")) t.pdl = std::atoi(v) != 0;
   if (const char* v = std::getenv("DIAL_B200_GEMM_MIN_ROWS")) t.gemm_min_rows = std::atoi(v);
   if (const char* v = std::getenv("DIAL_B200_ATTN_MIN_SPLIT")) t.attn_min_split = std::atoi(v);
   if (const char* v = std::getenv("DIAL_B200_ATTN_TC")) t.attn_tc = std::atoi(v) != 0;
   if (const char* v = std::getenv("DIAL_B200_ATTN_RING")) t.attn_ring = std::atoi(v) != 0;
   if (const char* v = std::getenv("DIAL_B200_ATTN_TOKSPLIT")) t.attn_tok_split = std::atoi(v);
+  if (const char* v = std::getenv("DIAL_B200_ATTN_MMA")) t.attn_mma = std::atoi(v) != 0;
+  if (const char* v = std::getenv("DIAL_B200_ATTN_MMA_MIN_SPLIT")) t.attn_mma_min_split = std::atoi(v);
+  if (const char* v = std::getenv("DIAL_B200_ATTN_MMA_RING")) t.attn_mma_ring = std::atoi(v);
   return t;
 }
 
@@ -706,6 +710,10 @@ AttnDecodeArgs decode_attn_args(dial_b200_engine* e, LayerW& L, int M, int row0 
   // register form packs more CTAs per SM)
   a.page_ring = g_tuning().attn_ring && M <= 4 ? 1 : 0;
   a.tok_split = g_tuning().attn_tok_split;
+  a.num_blocks = g_tuning().attn_mma ? e->cfg.max_sessions * e->max_blocks : 0;
+  if (a.num_blocks && M > 4 && g_tuning().attn_mma_min_split > 0)
+    a.min_split_tokens = g_tuning().attn_mma_min_split;
+  a.mma_ring = g_tuning().attn_mma_ring;
   a.trace = e->trace.as<unsigned long long>();
   return a;
 }
@@ -1098,6 +1106,8 @@ int dial_b200_attention_decode(const dial_b200_attn_shape* sh, const void* qkv, 
     a.status = device_status_word();
     a.page_ring = 1;
     a.tok_split = 1;
+    DIAL_CHECK(sh->num_blocks >= 0, "num_blocks %d is negative", sh->num_blocks);
+    a.num_blocks = sh->num_blocks;
     DIAL_CUDA(attn_decode_launch(a, sh->act, static_cast<cudaStream_t>(stream), false));
   });
 }
@@ -1668,6 +1678,10 @@ int dial_b200_engine_linear_replay(dial_b200_engine* eng, int layer, int which, 
     const float eps = eng->cfg.rms_norm_eps;
     cudaStream_t s = eng->stream;
     const int M = static_cast<int>(rows);
+    // the GEMM scratch of the decode step: rows >= 16 take the tcgen05 GEMM
+    // exactly as layer_decode does
+    const GemmScratch gsv{eng->gemm_scratch.p, eng->gemm_part.as<float>(), eng->gemm_part.bytes};
+    const GemmScratch* gs = &gsv;
     // layer < 0: rotate over every owned layer so that no launch finds its
     // weights in L2
     for (int64_t i = 0; i < iters; ++i) {
@@ -1682,13 +1696,13 @@ int dial_b200_engine_linear_replay(dial_b200_engine* eng, int layer, int which, 
       LayerW& L = eng->layer(layer_i);
       switch (which) {
         case 0: run_linear(L.qkv, eng->hidden.p, eng->H, L.input_norm.p, eps, eng->qkv.p, eng->QKV,
-                           M, kEpiStore, s, eng->status); break;
+                           M, kEpiStore, s, eng->status, gs); break;
         case 1: run_linear(L.o, eng->attn.p, eng->QH * eng->D, nullptr, eps, eng->hidden.p, eng->H,
-                           M, kEpiResidual, s, eng->status); break;
+                           M, kEpiResidual, s, eng->status, gs); break;
         case 2: run_linear(L.gate_up, eng->hidden.p, eng->H, L.post_norm.p, eps, eng->inter.p,
-                           eng->I, M, kEpiSwiglu, s, eng->status); break;
+                           eng->I, M, kEpiSwiglu, s, eng->status, gs); break;
         case 3: run_linear(L.down, eng->inter.p, eng->I, nullptr, eps, eng->hidden.p, eng->H, M,
-                           kEpiResidual, s, eng->status); break;
+                           kEpiResidual, s, eng->status, gs); break;
         default: DIAL_CHECK(false, "unknown linear slot %d", which);
       }
     }

@@ -40,11 +40,35 @@ constexpr int kMaxSlots = 16;
 constexpr int kMaxM = 8;
 constexpr int kSmemBudget = 232448;         // 227 KB opt-in per CTA
 constexpr int kMiscFlag = 32, kMiscKeys = 64, kMiscScratch = 128;  // offsets in the misc area
+constexpr int kRedBufs = 2;  // per-tile partial buffers (tile i uses i % kRedBufs)
 
 struct SmemPlan {
-  int ring_off, x_off, red_off, misc_off, bsc_off, bar_off, total;
+  int ring_off, x_off, red_off, misc_off, bsc_off, epi_off, bar_off, total;
   int slots, xs_stride, bsc_rows_lo, bsc_rows_hi;
+  int sc;   // chunks per ring stage
+  int tpc;  // tiles per CTA at most
 };
+
+// Chunks per ring stage.  int8 / e4m3 / dense: two per consumer warp (their
+// MMAs interleave in chunk_pair_mma).  NVFP4: a stage of 2*nw .. 3*nw chunks
+// taken round-robin (warp w: chunks w, w + nw, w + 2 nw), sized so that a
+// tile's C chunks cost the fewest stage x chunks-per-warp steps: C = 40
+// (K = 5120) then runs as one 40-chunk stage of 2-3 chunks per warp instead
+// of a full 32-chunk stage and an 8-chunk stage that keeps 12 warps idle.
+__host__ __device__ inline int stage_chunks(const DevQLinear& w, int nw) {
+  if (w.fmt != kFmtNvfp4G16) return 2 * nw;
+  const int C = w.C;
+  int best = 2 * nw, best_cost = (C + 2 * nw - 1) / (2 * nw) * 2;
+  for (int sc = 2 * nw + 1; sc <= 3 * nw; ++sc) {
+    const int per_warp = ((C < sc ? C : sc) + nw - 1) / nw;
+    const int cost = (C + sc - 1) / sc * per_warp;
+    if (cost < best_cost) {
+      best = sc;
+      best_cost = cost;
+    }
+  }
+  return best;
+}
 
 // Block-scale row ranges a CTA needs for tiles [t0, t1).
 __host__ __device__ inline void bsc_rows(const DevQLinear& w, int t0, int t1, int& lo0, int& nlo,
@@ -64,15 +88,25 @@ __host__ __device__ inline void bsc_rows(const DevQLinear& w, int t0, int t1, in
   }
 }
 
-__host__ inline SmemPlan make_plan(const DevQLinear& w, int M, int grid, int slots_req, int nw) {
+__host__ inline SmemPlan make_plan(const DevQLinear& w, int M, int grid, int slots_req, int nw,
+                                   int epi = kEpiStore, int sc_req = 0) {
   SmemPlan p{};
-  const int stage = 2 * nw * fmt_chunk_bytes(w.fmt);
+  p.sc = stage_chunks(w, nw);
+  // NVFP4 stage size override (2*nw .. 3*nw chunks)
+  if (w.fmt == kFmtNvfp4G16 && sc_req >= 2 * nw && sc_req <= 3 * nw) p.sc = sc_req;
+  p.tpc = (w.T + grid - 1) / grid;
+  const int stage = p.sc * fmt_chunk_bytes(w.fmt);
   p.xs_stride = w.K_pad + 8;
   const int x_bytes = ((M * p.xs_stride * 2) + 127) / 128 * 128;
-  const int red_bytes = 2 * nw * 32 * 4 * 4;
+  const int red_bytes = kRedBufs * nw * 32 * 4 * 4;
   // misc: xexp [kMaxM] ints | argmax flag | argmax keys [kMaxM] | staging
-  // scratch [2][nw] floats (block reduction of the activation statistics)
-  const int misc_bytes = kMiscScratch + 2 * nw * 4;
+  // scratch [2][nw] floats (block reduction of the activation statistics) |
+  // partial-buffer arrivals [kRedBufs] and completed epilogues [kRedBufs]
+  const int misc_bytes = kMiscScratch + 2 * nw * 4 + 2 * kRedBufs * 4;
+  // epilogue operands of the CTA's tiles, staged with the activations: row
+  // scales [tpc * 16] f32, residual inputs [M][tpc * 16] act
+  const int epi_bytes =
+      (p.tpc * 16 * 4 + (epi == kEpiResidual ? p.tpc * 16 * M * 2 : 0) + 127) / 128 * 128;
   int bsc_bytes = 0;
   if (w.fmt == kFmtFp8Block128) {
     // worst case over CTAs: tiles per CTA <= ceil(T/grid)
@@ -85,7 +119,7 @@ __host__ inline SmemPlan make_plan(const DevQLinear& w, int M, int grid, int slo
     bsc_bytes = (bsc_bytes + 127) / 128 * 128;
   }
   const int bar_bytes = (2 * kMaxSlots + 2) * 8;
-  const int fixed = x_bytes + red_bytes + misc_bytes + bsc_bytes + bar_bytes + 1024;
+  const int fixed = x_bytes + red_bytes + misc_bytes + bsc_bytes + epi_bytes + bar_bytes + 1024;
   int slots = (kSmemBudget - fixed) / stage;
   if (slots > kMaxSlots) slots = kMaxSlots;
   if (slots_req > 0 && slots_req < slots) slots = slots_req;
@@ -95,7 +129,8 @@ __host__ inline SmemPlan make_plan(const DevQLinear& w, int M, int grid, int slo
   p.red_off = p.x_off + x_bytes;
   p.misc_off = p.red_off + red_bytes;
   p.bsc_off = p.misc_off + misc_bytes;
-  p.bar_off = p.bsc_off + bsc_bytes;
+  p.epi_off = p.bsc_off + bsc_bytes;
+  p.bar_off = p.epi_off + epi_bytes;
   p.total = p.bar_off + bar_bytes;
   return p;
 }
@@ -124,12 +159,12 @@ template <typename Act, int FMT, int EPI, bool NORM, int NW>
 __global__ void __launch_bounds__((NW + 1) * 32, 1)
     gemv_kernel(const GemvArgs a, const SmemPlan p) {
   constexpr int kNW = NW;                   // consumer warps
-  constexpr int kStageChunks = 2 * NW;      // two per consumer warp
   using AT = ActTraits<Act>;
   using XT = typename std::conditional<FMT == kFmtDense, Act, __half>::type;
   constexpr bool kScaleX = (FMT != kFmtDense) && std::is_same<Act, __nv_bfloat16>::value;
   constexpr int CB = fmt_chunk_bytes(FMT);
-  constexpr int kStageBytes = kStageChunks * CB;
+  const int SC = p.sc;           // 2 * NW, or 2-3 * NW (NVFP4)
+  const int SBYTES = SC * CB;
 
   extern __shared__ __align__(1024) uint8_t smem[];
   uint8_t* ring = smem + p.ring_off;
@@ -138,6 +173,10 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1)
   int* xexp = reinterpret_cast<int*>(smem + p.misc_off);
   float* scratch = reinterpret_cast<float*>(smem + p.misc_off + kMiscScratch);
   float* bsc = reinterpret_cast<float*>(smem + p.bsc_off);
+  int* arrive = reinterpret_cast<int*>(scratch + 2 * kNW);  // [kRedBufs]
+  int* done = arrive + kRedBufs;                            // [kRedBufs]
+  float* es = reinterpret_cast<float*>(smem + p.epi_off);   // row scales [tpc * 16]
+  Act* eo = reinterpret_cast<Act*>(es + p.tpc * 16);        // residual [M][tpc * 16]
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + p.bar_off);
   uint64_t* empty = full + kMaxSlots;
   uint64_t* sbar = empty + kMaxSlots;
@@ -147,7 +186,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1)
   const int T = a.w.T, C = a.w.C;
   const int t0 = static_cast<int>(static_cast<long long>(T) * blockIdx.x / gridDim.x);
   const int t1 = static_cast<int>(static_cast<long long>(T) * (blockIdx.x + 1) / gridDim.x);
-  const int spt = (C + kStageChunks - 1) / kStageChunks;
+  const int spt = (C + SC - 1) / SC;
   const int NS = p.slots;
 
   int lo0 = 0, nlo = 0, hi0 = 0, nhi = 0;
@@ -160,6 +199,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1)
     }
     mbar_init(sbar, 1);
     fence_mbar_init();
+    for (int b = 0; b < kRedBufs; ++b) arrive[b] = done[b] = 0;
   }
   __syncthreads();
   pdl_launch_dependents();
@@ -191,11 +231,11 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1)
             ok = false;
             break;
           }
-          const int nch = min(kStageChunks, C - s * kStageChunks);
+          const int nch = min(SC, C - s * SC);
           const uint32_t bytes = static_cast<uint32_t>(nch * CB);
           mbar_arrive_expect_tx(&full[slot], bytes);
-          bulk_g2s_hint(ring + static_cast<size_t>(slot) * kStageBytes,
-                        src + static_cast<size_t>(s) * kStageChunks * CB, bytes, &full[slot], pol);
+          bulk_g2s_hint(ring + static_cast<size_t>(slot) * SBYTES,
+                        src + static_cast<size_t>(s) * SC * CB, bytes, &full[slot], pol);
           if (++slot == NS) {
             slot = 0;
             ++round;
@@ -233,6 +273,17 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1)
   }
   pdl_wait();
   if (a.trace) tstamp[1] = global_ns();
+  // epilogue operands of the CTA's tiles (their loads overlap the staging's)
+  const int nrow = (t1 - t0) * 16;
+  for (int r = threadIdx.x; r < nrow; r += kNW * 32)
+    es[r] = a.w.row_scale ? a.w.row_scale[t0 * 16 + r] : 1.f;
+  if constexpr (EPI == kEpiResidual) {
+    for (int e = threadIdx.x; e < nrow * a.M; e += kNW * 32) {
+      const int tt = e / nrow, r = e % nrow, n = t0 * 16 + r;
+      eo[e] = n < a.w.N ? reinterpret_cast<const Act*>(a.out)[static_cast<size_t>(tt) * a.out_ld + n]
+                        : AT::from_f(0.f);
+    }
+  }
   stage_x<Act, XT, NORM, kScaleX, kNW>(a, xs, p.xs_stride, xexp, scratch);
   named_bar_sync(1, kNW * 32);
   if (a.trace) tstamp[2] = global_ns();
@@ -248,25 +299,6 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1)
   bool ok = true;
   int tile_i = 0;
   for (int t = t0; t < t1; ++t, ++tile_i) {
-    // Epilogue operands of this tile (row scales, residual inputs) are loaded
-    // now, so their latency hides behind the tile's stages.
-    float pre_a = 1.f, pre_b = 1.f, pre_o = 0.f;
-    if (threadIdx.x < 128) {
-      const int rr = threadIdx.x >> 3, tt = threadIdx.x & 7;
-      if constexpr (EPI == kEpiSwiglu) {
-        if (threadIdx.x < 64 && a.w.row_scale) {
-          pre_a = a.w.row_scale[t * 16 + rr];
-          pre_b = a.w.row_scale[t * 16 + 8 + rr];
-        }
-      } else {
-        const int n = t * 16 + rr;
-        if (a.w.row_scale) pre_a = a.w.row_scale[t * 16 + rr];
-        if constexpr (EPI == kEpiResidual) {
-          if (tt < a.M && n < a.w.N)
-            pre_o = AT::to_f(reinterpret_cast<const Act*>(a.out)[static_cast<size_t>(tt) * a.out_ld + n]);
-        }
-      }
-    }
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
     float acc2[4] = {0.f, 0.f, 0.f, 0.f};
     float pacc[4][4] = {};
@@ -281,8 +313,8 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1)
     }
     for (int s = 0; s < spt; ++s) {
       if (ok && !mbar_wait(&full[slot], round & 1u, a.status, kStatusFullWaitTimeout)) ok = false;
-      const int nch = min(kStageChunks, C - s * kStageChunks);
-      const uint8_t* st = ring + static_cast<size_t>(slot) * kStageBytes;
+      const int nch = min(SC, C - s * SC);
+      const uint8_t* st = ring + static_cast<size_t>(slot) * SBYTES;
       if (ok) {
         if constexpr (FMT == kFmtFp8Block128) {
           // only a warp with a chunk in this stage reads a block scale: the
@@ -292,9 +324,9 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1)
 #pragma unroll
             for (int j = 0; j < 2; ++j) {
               const int ch = warp * 2 + j;
-              if (ch < nch) chunk_mma<FMT, XT>(st + ch * CB, s * kStageChunks + ch, xrow, lane, tmp);
+              if (ch < nch) chunk_mma<FMT, XT>(st + ch * CB, s * SC + ch, xrow, lane, tmp);
             }
-            const int kb = (s * kStageChunks + warp * 2) / 2;
+            const int kb = (s * SC + warp * 2) / 2;
             const float slo = bsc[rb_lo * a.w.blk_ld + kb];
             const float shi = bsc[rb_hi * a.w.blk_ld + kb];
             acc[0] = fmaf(tmp[0], slo, acc[0]);
@@ -305,19 +337,28 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1)
         } else {
           const int ch0 = warp * 2, ch1 = warp * 2 + 1;
           if constexpr (FMT == kFmtW8A16Row || FMT == kFmtFp8Row) {
-            if (nch == kStageChunks) {
-              chunk_pair_mma<FMT, XT>(st + ch0 * CB, s * kStageChunks + ch0, xrow, lane, pacc);
+            if (nch == SC) {
+              chunk_pair_mma<FMT, XT>(st + ch0 * CB, s * SC + ch0, xrow, lane, pacc);
             } else {
               if (ch0 < nch)
-                chunk_mma<FMT, XT>(st + ch0 * CB, s * kStageChunks + ch0, xrow, lane, acc);
+                chunk_mma<FMT, XT>(st + ch0 * CB, s * SC + ch0, xrow, lane, acc);
               if (ch1 < nch)
-                chunk_mma<FMT, XT>(st + ch1 * CB, s * kStageChunks + ch1, xrow, lane, acc2);
+                chunk_mma<FMT, XT>(st + ch1 * CB, s * SC + ch1, xrow, lane, acc2);
             }
+          } else if constexpr (FMT == kFmtNvfp4G16) {
+            // round-robin: chunks warp, warp + NW (paired MMA chains), warp + 2 NW
+            const int ca = warp, cb = warp + kNW, cc = warp + 2 * kNW;
+            const int kc0 = s * SC;
+            if (cb < nch)
+              chunk_pair_nvfp4<XT>(st + ca * CB, kc0 + ca, st + cb * CB, kc0 + cb, xrow, lane, pacc);
+            else if (ca < nch)
+              chunk_mma<FMT, XT>(st + ca * CB, kc0 + ca, xrow, lane, acc);
+            if (cc < nch) chunk_mma<FMT, XT>(st + cc * CB, kc0 + cc, xrow, lane, acc2);
           } else {
             if (ch0 < nch)
-              chunk_mma<FMT, XT>(st + ch0 * CB, s * kStageChunks + ch0, xrow, lane, acc);
+              chunk_mma<FMT, XT>(st + ch0 * CB, s * SC + ch0, xrow, lane, acc);
             if (ch1 < nch)
-              chunk_mma<FMT, XT>(st + ch1 * CB, s * kStageChunks + ch1, xrow, lane, acc2);
+              chunk_mma<FMT, XT>(st + ch1 * CB, s * SC + ch1, xrow, lane, acc2);
           }
         }
       }
@@ -328,15 +369,44 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1)
         ++round;
       }
     }
-    // ---- cross-warp reduction (double-buffered by tile parity)
-    float* rb = red + (tile_i & 1) * (kNW * 128);
+    // ---- cross-warp reduction: every warp leaves its partial in the tile's
+    // buffer; the last warp to arrive sums them and runs the epilogue while
+    // the others go on streaming (no CTA-wide barrier per tile)
+    const int b = tile_i % kRedBufs;
+    float* rb = red + b * (kNW * 128);
 #pragma unroll
     for (int q = 0; q < 4; ++q)
       acc[q] += acc2[q] + ((pacc[0][q] + pacc[1][q]) + (pacc[2][q] + pacc[3][q]));
+    if (tile_i >= kRedBufs) {
+      // the buffer's previous tile (tile_i - kRedBufs) must have been summed
+      if (lane == 0) {
+        volatile int* d = done + b;
+        const int want = tile_i - kRedBufs + 1;
+        if (*d < want) {
+          const unsigned long long tw = global_ns();
+          while (*d < want) {
+            if (global_ns() - tw > kWaitLimitNs) {
+              set_status(a.status, kStatusReduceWaitTimeout);
+              break;
+            }
+            __nanosleep(32);
+          }
+        }
+      }
+      __syncwarp();
+      __threadfence_block();
+    }
     *reinterpret_cast<float4*>(rb + (warp * 32 + lane) * 4) =
         make_float4(acc[0], acc[1], acc[2], acc[3]);
-    named_bar_sync(1, kNW * 32);
-    const int i = threadIdx.x;
+    __syncwarp();
+    int last = 0;
+    if (lane == 0) {
+      __threadfence_block();
+      last = atomicAdd(&arrive[b], 1) == kNW - 1;
+    }
+    if (!__shfl_sync(0xffffffffu, last, 0)) continue;
+    __syncwarp();
+    __threadfence_block();
     auto gather = [&](int rr, int tt) {
       const int src_lane = (rr & 7) * 4 + (tt >> 1);
       const int reg = ((rr >> 3) << 1) | (tt & 1);
@@ -345,29 +415,30 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1)
       for (int w = 0; w < kNW; ++w) v += rb[(w * 32 + src_lane) * 4 + reg];
       return v;
     };
+    const int nt = t - t0;
     if constexpr (EPI == kEpiSwiglu) {
-      if (i < 64) {
-        const int rr = i >> 3, tt = i & 7;
+      for (int f = lane; f < 8 * a.M; f += 32) {
+        const int rr = f & 7, tt = f >> 3;
         const int j = t * 8 + rr;
-        if (tt < a.M && j < I) {
+        if (j < I) {
           float vg = gather(rr, tt), vu = gather(rr + 8, tt);
           float mul = exp2i(xexp[tt]);
           if constexpr (FMT == kFmtNvfp4G16) mul *= a.w.global_scale;
-          const float sg = mul * pre_a, su = mul * pre_b;
+          const float sg = mul * es[nt * 16 + rr], su = mul * es[nt * 16 + 8 + rr];
           const float gq = AT::round(vg * sg), uq = AT::round(vu * su);
           Act* out = reinterpret_cast<Act*>(a.out) + static_cast<size_t>(tt) * a.out_ld + j;
           *out = AT::from_f(silu_mul_ref<Act>(gq, uq));
         }
       }
     } else {
-      if (i < 128) {
-        const int rr = i >> 3, tt = i & 7;
+      for (int f = lane; f < 16 * a.M; f += 32) {
+        const int rr = f & 15, tt = f >> 4;
         const int n = t * 16 + rr;
-        if (tt < a.M && n < a.w.N) {
+        if (n < a.w.N) {
           float v = gather(rr, tt);
           float mul = exp2i(xexp[tt]);
           if constexpr (FMT == kFmtNvfp4G16) mul *= a.w.global_scale;
-          mul *= pre_a;
+          mul *= es[nt * 16 + rr];
           const float y = AT::round(v * mul);
           if constexpr (EPI == kEpiArgmax) {
             if (a.out)
@@ -376,7 +447,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1)
           } else {
             Act* out = reinterpret_cast<Act*>(a.out) + static_cast<size_t>(tt) * a.out_ld + n;
             if constexpr (EPI == kEpiResidual) {
-              *out = AT::from_f(y + pre_o);
+              *out = AT::from_f(y + AT::to_f(eo[tt * nrow + nt * 16 + rr]));
             } else {
               *out = AT::from_f(y);
             }
@@ -384,10 +455,16 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1)
         }
       }
     }
-  }
-  if (a.trace && threadIdx.x == 0) {
-    tstamp[3] = global_ns();
-    trace_record(a.trace, a.trace_tag, tstamp);
+    __syncwarp();
+    if (lane == 0) {
+      arrive[b] = 0;
+      __threadfence_block();
+      *reinterpret_cast<volatile int*>(done + b) = tile_i + 1;
+      if (a.trace && t == t1 - 1) {
+        tstamp[3] = global_ns();
+        trace_record(a.trace, a.trace_tag, tstamp);
+      }
+    }
   }
   if constexpr (EPI == kEpiArgmax) {
     // CTA best -> global keys; the last CTA to arrive decodes and resets them.
@@ -412,14 +489,15 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1)
 }
 
 template <typename Act, int FMT, int EPI, bool NORM, int NW>
-cudaError_t launch_one(const GemvArgs& a, int slots_req, int grid_req, cudaStream_t stream,
-                       bool pdl) {
+cudaError_t launch_one(const GemvArgs& a, const GemvTuning& t, cudaStream_t stream) {
+  const int slots_req = t.slots, grid_req = t.grid;
+  const bool pdl = t.pdl;
   int dev = 0, sms = 0;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   int grid = grid_req > 0 ? grid_req : sms;
   if (grid > a.w.T) grid = a.w.T;
-  const SmemPlan p = make_plan(a.w, a.M, grid, slots_req, NW);
+  const SmemPlan p = make_plan(a.w, a.M, grid, slots_req, NW, EPI, t.nvfp4_stage);
   if (p.slots < 2) return cudaErrorInvalidConfiguration;
   auto kern = gemv_kernel<Act, FMT, EPI, NORM, NW>;
   cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -443,42 +521,42 @@ cudaError_t launch_one(const GemvArgs& a, int slots_req, int grid_req, cudaStrea
 }
 
 template <typename Act, int FMT, int EPI, bool NORM>
-cudaError_t launch_nw(const GemvArgs& a, int nw, int slots, int grid, cudaStream_t s, bool pdl) {
-  return nw == 16 ? launch_one<Act, FMT, EPI, NORM, 16>(a, slots, grid, s, pdl)
-                  : launch_one<Act, FMT, EPI, NORM, 8>(a, slots, grid, s, pdl);
+cudaError_t launch_nw(const GemvArgs& a, int nw, const GemvTuning& t, cudaStream_t s) {
+  return nw == 16 ? launch_one<Act, FMT, EPI, NORM, 16>(a, t, s)
+                  : launch_one<Act, FMT, EPI, NORM, 8>(a, t, s);
 }
 
 template <typename Act, int FMT>
-cudaError_t dispatch_epi(const GemvArgs& a, int epi, bool norm, int nw, int slots, int grid,
-                         cudaStream_t s, bool pdl) {
+cudaError_t dispatch_epi(const GemvArgs& a, int epi, bool norm, int nw, const GemvTuning& t,
+                         cudaStream_t s) {
   if (epi == kEpiArgmax) {
     if constexpr (FMT == kFmtDense || FMT == kFmtW8A16Row)
-      return norm ? launch_nw<Act, FMT, kEpiArgmax, true>(a, nw, slots, grid, s, pdl)
-                  : launch_nw<Act, FMT, kEpiArgmax, false>(a, nw, slots, grid, s, pdl);
+      return norm ? launch_nw<Act, FMT, kEpiArgmax, true>(a, nw, t, s)
+                  : launch_nw<Act, FMT, kEpiArgmax, false>(a, nw, t, s);
     return cudaErrorInvalidValue;
   }
   if (epi == kEpiStore)
-    return norm ? launch_nw<Act, FMT, kEpiStore, true>(a, nw, slots, grid, s, pdl)
-                : launch_nw<Act, FMT, kEpiStore, false>(a, nw, slots, grid, s, pdl);
+    return norm ? launch_nw<Act, FMT, kEpiStore, true>(a, nw, t, s)
+                : launch_nw<Act, FMT, kEpiStore, false>(a, nw, t, s);
   if (epi == kEpiResidual)
-    return norm ? launch_nw<Act, FMT, kEpiResidual, true>(a, nw, slots, grid, s, pdl)
-                : launch_nw<Act, FMT, kEpiResidual, false>(a, nw, slots, grid, s, pdl);
+    return norm ? launch_nw<Act, FMT, kEpiResidual, true>(a, nw, t, s)
+                : launch_nw<Act, FMT, kEpiResidual, false>(a, nw, t, s);
   if (epi == kEpiSwiglu)
-    return norm ? launch_nw<Act, FMT, kEpiSwiglu, true>(a, nw, slots, grid, s, pdl)
-                : launch_nw<Act, FMT, kEpiSwiglu, false>(a, nw, slots, grid, s, pdl);
+    return norm ? launch_nw<Act, FMT, kEpiSwiglu, true>(a, nw, t, s)
+                : launch_nw<Act, FMT, kEpiSwiglu, false>(a, nw, t, s);
   return cudaErrorInvalidValue;
 }
 
 template <typename Act>
-cudaError_t dispatch_fmt(const GemvArgs& a, int epi, bool norm, int nw, int slots, int grid,
-                         cudaStream_t s, bool pdl) {
+cudaError_t dispatch_fmt(const GemvArgs& a, int epi, bool norm, int nw, const GemvTuning& t,
+                         cudaStream_t s) {
   switch (a.w.fmt) {
-    case kFmtW8A16Row: return dispatch_epi<Act, kFmtW8A16Row>(a, epi, norm, nw, slots, grid, s, pdl);
+    case kFmtW8A16Row: return dispatch_epi<Act, kFmtW8A16Row>(a, epi, norm, nw, t, s);
     case kFmtFp8Block128:
-      return dispatch_epi<Act, kFmtFp8Block128>(a, epi, norm, nw, slots, grid, s, pdl);
-    case kFmtFp8Row: return dispatch_epi<Act, kFmtFp8Row>(a, epi, norm, nw, slots, grid, s, pdl);
-    case kFmtNvfp4G16: return dispatch_epi<Act, kFmtNvfp4G16>(a, epi, norm, nw, slots, grid, s, pdl);
-    case kFmtDense: return dispatch_epi<Act, kFmtDense>(a, epi, norm, nw, slots, grid, s, pdl);
+      return dispatch_epi<Act, kFmtFp8Block128>(a, epi, norm, nw, t, s);
+    case kFmtFp8Row: return dispatch_epi<Act, kFmtFp8Row>(a, epi, norm, nw, t, s);
+    case kFmtNvfp4G16: return dispatch_epi<Act, kFmtNvfp4G16>(a, epi, norm, nw, t, s);
+    case kFmtDense: return dispatch_epi<Act, kFmtDense>(a, epi, norm, nw, t, s);
     default: return cudaErrorInvalidValue;
   }
 }
@@ -506,10 +584,8 @@ cudaError_t gemv_launch(const GemvArgs& args, int act, int epi, bool norm, cudaS
       a.amax_count = args.amax_count + r0;
       a.amax_tok = args.amax_tok + r0;
     }
-    cudaError_t e = act == 0 ? dispatch_fmt<__nv_bfloat16>(a, epi, norm, nw, tune.slots,
-                                                           tune.grid, stream, tune.pdl)
-                             : dispatch_fmt<__half>(a, epi, norm, nw, tune.slots, tune.grid,
-                                                    stream, tune.pdl);
+    cudaError_t e = act == 0 ? dispatch_fmt<__nv_bfloat16>(a, epi, norm, nw, tune, stream)
+                             : dispatch_fmt<__half>(a, epi, norm, nw, tune, stream);
     if (e != cudaSuccess) return e;
   }
   return cudaSuccess;

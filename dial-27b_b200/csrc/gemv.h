@@ -39,11 +39,15 @@ struct GemvTuning {
   int slots = 0;   // ring stages (0 = as many as fit)
   int grid = 0;    // CTAs (0 = one per SM)
   bool pdl = true; // programmatic dependent launch
+  int nvfp4_stage = 0;  // NVFP4 GEMV chunks per ring stage (0: chosen per linear)
   int gemm_min_rows = 16;    // rows from which linears take the tcgen05 GEMM (0 = never)
   int attn_min_split = 0;    // decode attention: context tokens per split at least (0 = 16)
   bool attn_tc = true;       // prefill attention on the tensor cores when supported
   bool attn_ring = false;    // decode attention pages through a shared-memory ring (opt-in)
   int attn_tok_split = 1;  // decode attention: warps split each page's tokens (AttnDecodeArgs)
+  bool attn_mma = true;     // decode attention for many rows on the tensor cores
+  int attn_mma_min_split = 0;  // ... its context tokens per split at least (0: attn_min_split)
+  int attn_mma_ring = 2;       // ... its page slots per warp (2 or 3)
 };
 
 // act: 0 = bf16, 1 = f16.  Launches ceil(M/8) kernels on `stream`.

@@ -142,6 +142,53 @@ __device__ __forceinline__ void chunk_pair_mma(const uint8_t* st, int kc, const 
   }
 }
 
+// Two NVFP4 chunks of one stage (anywhere in it) with their MMAs interleaved
+// into four independent accumulator chains (chunk h -> acc[2h], acc[2h + 1]
+// for the two MMAs of each 32-input step), as chunk_pair_mma does for int8.
+template <typename XT>
+__device__ __forceinline__ void chunk_pair_nvfp4(const uint8_t* st0, int kc0, const uint8_t* st1,
+                                                 int kc1, const XT* xrow, int lane,
+                                                 float (&acc)[4][4]) {
+  const int c = lane & 3;
+  const uint8_t* st[2] = {st0, st1};
+  const XT* xp[2] = {xrow + kc0 * 128 + c * 32, xrow + kc1 * 128 + c * 32};
+  uint4 w0[2], w1[2];
+  __half2 sc0[2][2], sc1[2][2];
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    w0[h] = *reinterpret_cast<const uint4*>(st[h] + lane * 16);
+    w1[h] = *reinterpret_cast<const uint4*>(st[h] + 512 + lane * 16);
+    const uint32_t sg0 = e4m3x2_to_f16x2(*reinterpret_cast<const uint16_t*>(st[h] + 1024 + lane * 2));
+    const uint32_t sg1 =
+        e4m3x2_to_f16x2(*reinterpret_cast<const uint16_t*>(st[h] + 1024 + 64 + lane * 2));
+    sc0[h][0] = __low2half2(*reinterpret_cast<const __half2*>(&sg0));
+    sc0[h][1] = __high2half2(*reinterpret_cast<const __half2*>(&sg0));
+    sc1[h][0] = __low2half2(*reinterpret_cast<const __half2*>(&sg1));
+    sc1[h][1] = __high2half2(*reinterpret_cast<const __half2*>(&sg1));
+  }
+#pragma unroll
+  for (int s = 0; s < 4; ++s) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      uint32_t oa[4], ob[4];
+      e2m1x8_to_f16x2x4((&w0[h].x)[s], oa);
+      e2m1x8_to_f16x2x4((&w1[h].x)[s], ob);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        __half2 ha = __hmul2(*reinterpret_cast<__half2*>(&oa[q]), sc0[h][s >> 1]);
+        __half2 hb = __hmul2(*reinterpret_cast<__half2*>(&ob[q]), sc1[h][s >> 1]);
+        oa[q] = *reinterpret_cast<uint32_t*>(&ha);
+        ob[q] = *reinterpret_cast<uint32_t*>(&hb);
+      }
+      const uint4 xv = *reinterpret_cast<const uint4*>(xp[h] + 8 * s);
+      const uint32_t A0[4] = {oa[0], ob[0], oa[1], ob[1]};
+      const uint32_t A1[4] = {oa[2], ob[2], oa[3], ob[3]};
+      mma_f16(acc[2 * h], A0, xv.x, xv.y);
+      mma_f16(acc[2 * h + 1], A1, xv.z, xv.w);
+    }
+  }
+}
+
 // ------------------------------------------------------------ x staging
 // Stage the M activation rows of a GEMV in shared memory (NW consumer warps,
 // named barrier 1): optional RMSNorm (text.rs:1620-1626 rounding), then f16

@@ -13,6 +13,7 @@ from pathlib import Path
 _HERE = Path(__file__).resolve().parent
 LIB_PATH = Path(os.environ.get("DIAL_B200_LIB", _HERE / "libdial_b200.so"))
 
+ABI_VERSION = 2  # DIAL_B200_ABI_VERSION of the structs below
 DIAL_OK, DIAL_ERR_INVALID, DIAL_ERR_CUDA, DIAL_ERR_DEVICE = 0, 1, 2, 3
 FMT_W8A16_ROW, FMT_FP8_BLOCK128, FMT_FP8_ROW, FMT_NVFP4_G16, FMT_DENSE = 0, 1, 2, 3, 4
 ACT_BF16, ACT_F16, ACT_F32 = 0, 1, 2
@@ -41,6 +42,7 @@ class AttnShape(C.Structure):
         ("max_pos", C.c_int32),
         ("eps", C.c_float),
         ("act", C.c_int32),
+        ("num_blocks", C.c_int32),
     ]
 
 
@@ -141,6 +143,10 @@ for _name, (_res, _args) in _SIGS.items():
     _f = getattr(lib, _name)
     _f.restype = _res
     _f.argtypes = _args
+
+if lib.dial_b200_abi_version() != ABI_VERSION:
+    raise ImportError(f"{LIB_PATH} has ABI version {lib.dial_b200_abi_version()}, this binding "
+                      f"expects {ABI_VERSION}: rebuild it with `python dial-27b_b200/build.py`")
 
 
 def call(name: str, *args):

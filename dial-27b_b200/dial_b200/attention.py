@@ -21,8 +21,10 @@ def _p(t: torch.Tensor):
 
 
 def make_shape(q_heads: int, kv_heads: int, max_blocks: int, max_pos: int, eps: float = 1e-6,
-               dtype: torch.dtype = torch.bfloat16) -> AttnShape:
-    return AttnShape(q_heads, kv_heads, 128, max_blocks, max_pos, eps, _ACT[dtype])
+               dtype: torch.dtype = torch.bfloat16, num_blocks: int = 0) -> AttnShape:
+    """num_blocks: pages in each KV pool; > 0 lets steps of more than 4 rows
+    take the tensor-core form."""
+    return AttnShape(q_heads, kv_heads, 128, max_blocks, max_pos, eps, _ACT[dtype], num_blocks)
 
 
 def scratch_bytes(sh: AttnShape, rows: int, splits: int) -> int:

@@ -160,9 +160,14 @@ class StageRunner:
         the last stage maps stage 0's.  Afterwards decode_linked runs the
         decode loop with no NCCL call and no host synchronisation per token."""
         p = self.plan
-        mine = self.eng.stage_link_handle()
+        try:
+            mine = self.eng.stage_link_handle()
+        except Exception:  # noqa: BLE001  (every rank still joins the exchange below)
+            mine = None
         handles = [None] * p.world
         dist.all_gather_object(handles, mine, group=self.group)
+        if any(h is None for h in handles):
+            raise RuntimeError("a stage could not export its link inbox")
         self.eng.stage_link_open(None if p.is_last else handles[p.rank + 1],
                                  handles[0] if p.is_last else None)
         self.linked = True

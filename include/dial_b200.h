@@ -30,7 +30,8 @@
 extern "C" {
 #endif
 
-#define DIAL_B200_ABI_VERSION 1u
+/* 2: dial_b200_attn_shape gained num_blocks */
+#define DIAL_B200_ABI_VERSION 2u
 
 /* status codes */
 #define DIAL_OK 0
@@ -114,6 +115,10 @@ typedef struct {
   int32_t max_pos;    /* rows of the cos/sin tables */
   float eps;          /* q/k RMSNorm epsilon */
   int32_t act;        /* DIAL_ACT_BF16 or DIAL_ACT_F16 */
+  int32_t num_blocks; /* pages in each of k_pages / v_pages; with more than 4
+                         rows a positive value selects the tensor-core form
+                         (mma.sync over TMA-staged pages), 0 the CUDA-core
+                         forms; dial_b200_attention_decode_noalloc ignores it */
 } dial_b200_attn_shape;
 
 /* Bytes of scratch dial_b200_attention_decode needs for `rows` rows and

@@ -95,11 +95,14 @@ def assert_attn_close(got, ref, act):
     assert np.mean(d <= 2 * ulp(np.maximum(np.abs(ref), rms), act)) >= 0.99
 
 
-def run(case, cuda, splits, calls=1):
+def run(case, cuda, splits, calls=1, num_blocks=0):
+    """num_blocks > 0 passes the pool size (the tensor-core form for more
+    than 4 rows)."""
     from dial_b200 import attention as A
 
     dt = torch.bfloat16 if case.act == "bf16" else torch.float16
-    sh = A.make_shape(case.QH, case.KVH, case.max_blocks, case.max_pos, case.eps, dt)
+    sh = A.make_shape(case.QH, case.KVH, case.max_blocks, case.max_pos, case.eps, dt,
+                      num_blocks=num_blocks)
     dev = case.device(cuda)
     nbytes = A.scratch_bytes(sh, case.rows, splits)
     scratch = torch.zeros(max(nbytes, 16), dtype=torch.uint8, device=cuda) if splits > 1 else None

@@ -44,7 +44,7 @@ def test_library_exports_every_declared_symbol():
 def test_abi_version_without_gpu():
     from dial_b200 import _abi
 
-    assert _abi.lib.dial_b200_abi_version() == 1
+    assert _abi.lib.dial_b200_abi_version() == _abi.ABI_VERSION == 2
 
 
 def test_null_handles_are_rejected_without_device_work():

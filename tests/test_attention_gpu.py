@@ -49,6 +49,42 @@ def test_attention_decode_many_rows_f16_long_context(cuda):
     np.testing.assert_array_equal(a, b)
 
 
+@pytest.mark.parametrize("qh,kvh,dtype", [(32, 8, "bf16"), (40, 8, "bf16"), (8, 8, "bf16"),
+                                          (16, 8, "f16"), (8, 1, "f16")])
+@pytest.mark.parametrize("splits", [1, 4, 16])
+def test_attention_decode_tensor_core_form(cuda, qh, kvh, dtype, splits):
+    """More than 4 rows with the pool size given take the tensor-core form
+    (attn_decode_mma.cu: TMA-staged pages, mma.sync scores and P.V with the
+    probabilities split into two act terms): group sizes 1, 2, 4, 5 and 8,
+    one-token, page-edge and long contexts, the new token's row patched into
+    its landed page, the appended K/V, and a repeat call bit for bit."""
+    import dial_b200
+
+    case = PagedCase(qh, kvh, [0, 1, 15, 16, 17, 200, 777, 1023], seed=qh + 7 * kvh + splits,
+                     dtype=dtype)
+    (a, b), dev, _ = run(case, cuda, splits, calls=2, num_blocks=case.rows * case.max_blocks)
+    assert dial_b200.device_status() == 0
+    ref, kref, vref = case.oracle()
+    assert_attn_close(a, ref, dtype)
+    np.testing.assert_array_equal(a, b)
+    k, v = case.new_kv(dev["k_pages"], dev["v_pages"])
+    np.testing.assert_array_equal(v, vref)
+    assert np.all(np.abs(k - kref) <= ulp(kref, dtype))
+
+
+def test_attention_decode_tensor_core_form_matches_cuda_core_form(cuda):
+    """Both many-row forms against each other on one long-context case: the
+    tensor-core form's two-term probabilities keep it as close to the
+    CUDA-core form's f32 probabilities as either is to the oracle."""
+    case = PagedCase(32, 8, [1000, 513, 64, 0, 250, 1023, 31, 600], seed=21)
+    (tc,), _, _ = run(case, cuda, 16, num_blocks=case.rows * case.max_blocks)
+    (cc,), _, _ = run(case, cuda, 16)
+    ref, _, _ = case.oracle()
+    assert_attn_close(tc, ref, "bf16")
+    d = np.abs(tc - cc)
+    assert np.mean(d <= ulp(np.maximum(np.abs(cc), 1e-3), "bf16")) >= 0.99
+
+
 def test_attention_decode_repeat_calls_agree(cuda):
     """Scratch counters reset themselves: a second call (which re-appends the
     same K/V) reproduces the first bit for bit."""
