@@ -43,11 +43,13 @@ constexpr int OFF_V = OFF_K + 2 * TILE;       // [2] value tiles
 constexpr int OFF_P = OFF_V + 2 * TILE;       // probabilities
 constexpr int OFF_XCH = OFF_P + TILE;        // row max exchange [2 parities][2 halves][128]
 constexpr int OFF_BAR = OFF_XCH + 2 * 2 * 128 * 4;
-// qbar, kvfull[2], kvfree[2], sbar, pready, obar, fin
-constexpr int NBAR = 9;
+// qbar, kfull[2], kfree[2], vfull[2], vfree[2], sbar[2], pready, obar, fin
+constexpr int NBAR = 14;
 constexpr int OFF_TMEM = OFF_BAR + NBAR * 8;
 constexpr int SMEM_BYTES = OFF_TMEM + 16 + 1024;
-constexpr int kTmemCols = 256;  // S in [0,128), O in [128,256)
+// S double-buffered in [0,128) and [128,256), O in [256,384): Q K^T of block
+// j+1 runs on the tensor core while the softmax warps work on block j
+constexpr int kTmemCols = 512;
 constexpr int kStatusAttnTc = 0x501;
 
 // f32 accumulator, bf16 A and B, K-major A; B K-major (S = Q K^T) or
@@ -147,16 +149,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
   uint64_t* qbar = bars;
-  uint64_t* kvfull = bars + 1;  // [2]
-  uint64_t* kvfree = bars + 3;  // [2]
-  uint64_t* sbar = bars + 5;
-  uint64_t* pready = bars + 6;
-  uint64_t* obar = bars + 7;
-  uint64_t* fin = bars + 8;  // the MMA thread's own "all my MMAs are done"
+  uint64_t* kfull = bars + 1;   // [2] key tile landed
+  uint64_t* kfree = bars + 3;   // [2] key tile read by Q K^T
+  uint64_t* vfull = bars + 5;   // [2] value tile landed
+  uint64_t* vfree = bars + 7;   // [2] value tile read by P V
+  uint64_t* sbar = bars + 9;    // [2] S buffer of block j written
+  uint64_t* pready = bars + 11;
+  uint64_t* obar = bars + 12;
+  uint64_t* fin = bars + 13;  // the MMA thread's own "all my MMAs are done"
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + OFF_TMEM);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int q0 = blockIdx.x * kQ;  // first query row of the CTA
+  // the causally longest query blocks first: the short ones fill the tail
+  const int q0 = (gridDim.x - 1 - blockIdx.x) * kQ;  // first query row of the CTA
   const int h = blockIdx.y, kvh = h / nrep;
   const int KVH = a.sh.kv_heads;
   // keys [0, last] are visible to some query of the block
@@ -167,10 +172,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (tid == 0) {
     mbar_init(qbar, 1);
     for (int b = 0; b < 2; ++b) {
-      mbar_init(&kvfull[b], 1);
-      mbar_init(&kvfree[b], 1);
+      mbar_init(&kfull[b], 1);
+      mbar_init(&kfree[b], 1);
+      mbar_init(&vfull[b], 1);
+      mbar_init(&vfree[b], 1);
+      mbar_init(&sbar[b], 1);
     }
-    mbar_init(sbar, 1);
     mbar_init(pready, 2 * kQ);  // every softmax thread of both halves
     mbar_init(obar, 1);
     mbar_init(fin, 1);
@@ -186,7 +193,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tS = tmem, tO = tmem + 128;
+  const uint32_t tO = tmem + 256;  // S of block j: tmem + (j & 1) * 128
 
   if (warp == 4) {
     // ------------------------------------------------------------ loads
@@ -194,21 +201,35 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_arrive_expect_tx(qbar, TILE);
       tma2d(smem + OFF_Q, &maps.q, h * kHeadDim, q0, qbar);
       tma2d(smem + OFF_Q + HALF, &maps.q, h * kHeadDim + 64, q0, qbar);
+      // K of block j as soon as Q K^T of block j-2 has read its buffer, V as
+      // soon as P V of block j-2 has
       for (int j = 0; j < nkb; ++j) {
         const int b = j & 1;
-        if (j >= 2 && !mbar_wait(&kvfree[b], static_cast<uint32_t>(j / 2 - 1) & 1u, a.status,
-                                 kStatusAttnTc))
-          break;
-        mbar_arrive_expect_tx(&kvfull[b], 2 * TILE);
+        int rows[kKB / kPageTokens];
+#pragma unroll
         for (int pg = 0; pg < kKB / kPageTokens; ++pg) {
           const int page = min(j * (kKB / kPageTokens) + pg, a.sh.max_blocks - 1);
-          const int row = (a.block_table[page] * KVH + kvh) * kPageTokens;
+          rows[pg] = (a.block_table[page] * KVH + kvh) * kPageTokens;
+        }
+        if (j >= 2 && !mbar_wait(&kfree[b], static_cast<uint32_t>(j / 2 - 1) & 1u, a.status,
+                                 kStatusAttnTc))
+          break;
+        mbar_arrive_expect_tx(&kfull[b], TILE);
+#pragma unroll
+        for (int pg = 0; pg < kKB / kPageTokens; ++pg) {
           uint8_t* kt = smem + OFF_K + b * TILE + pg * 2048;
+          tma2d(kt, &maps.k, 0, rows[pg], &kfull[b]);
+          tma2d(kt + HALF, &maps.k, 64, rows[pg], &kfull[b]);
+        }
+        if (j >= 2 && !mbar_wait(&vfree[b], static_cast<uint32_t>(j / 2 - 1) & 1u, a.status,
+                                 kStatusAttnTc))
+          break;
+        mbar_arrive_expect_tx(&vfull[b], TILE);
+#pragma unroll
+        for (int pg = 0; pg < kKB / kPageTokens; ++pg) {
           uint8_t* vt = smem + OFF_V + b * TILE + pg * 2048;
-          tma2d(kt, &maps.k, 0, row, &kvfull[b]);
-          tma2d(kt + HALF, &maps.k, 64, row, &kvfull[b]);
-          tma2d(vt, &maps.v, 0, row, &kvfull[b]);
-          tma2d(vt + HALF, &maps.v, 64, row, &kvfull[b]);
+          tma2d(vt, &maps.v, 0, rows[pg], &vfull[b]);
+          tma2d(vt + HALF, &maps.v, 64, rows[pg], &vfull[b]);
         }
       }
     }
@@ -217,6 +238,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       const uint32_t sq = smem_u32(smem + OFF_Q), sp = smem_u32(smem + OFF_P);
       bool ok = mbar_wait(qbar, 0, a.status, kStatusAttnTc);
+      auto issue_s = [&](int jj) {
+        // S[jj & 1] = Q K^T over 128 dims: 8 steps of 16
+        const uint32_t sk = smem_u32(smem + OFF_K + (jj & 1) * TILE);
+        const uint32_t ts = tmem + static_cast<uint32_t>(jj & 1) * 128;
+#pragma unroll
+        for (int k16 = 0; k16 < kHeadDim / 16; ++k16) {
+          const uint32_t off = (k16 >> 2) * HALF + (k16 & 3) * 32;
+          mma(ts, kmajor_desc(sq + off), kmajor_desc(sk + off), idesc(false), k16 > 0 ? 1u : 0u);
+        }
+        commit(&kfree[jj & 1]);
+        commit(&sbar[jj & 1]);
+      };
       auto issue_pv = [&](int jj) {
         // O += P V over 128 keys: 8 steps of 16 keys
         const uint32_t sv = smem_u32(smem + OFF_V + (jj & 1) * TILE);
@@ -226,36 +259,36 @@ __global__ void __launch_bounds__(kThreads, 1)
           mma(tO, kmajor_desc(pa), mnmajor_desc(sv + k16 * 2048), idesc(true),
               (jj > 0 || k16 > 0) ? 1u : 0u);
         }
-        commit(&kvfree[jj & 1]);
+        commit(&vfree[jj & 1]);
         commit(obar);
       };
+      if (ok && mbar_wait(&kfull[0], 0, a.status, kStatusAttnTc)) {
+        fence_after();
+        issue_s(0);
+      } else {
+        ok = false;
+      }
       for (int j = 0; j < nkb && ok; ++j) {
-        if (!mbar_wait(&kvfull[j & 1], static_cast<uint32_t>(j / 2) & 1u, a.status,
-                       kStatusAttnTc)) {
-          ok = false;
-          break;
-        }
-        if (j > 0) {
-          // the softmax of block j-1 has read S, written P and rescaled O
-          if (!mbar_wait(pready, static_cast<uint32_t>(j - 1) & 1u, a.status, kStatusAttnTc)) {
+        if (j + 1 < nkb) {
+          // Q K^T of block j+1 overlaps the softmax of block j: its S buffer
+          // was last read by the softmax of block j-1 (waited for below)
+          if (!mbar_wait(&kfull[(j + 1) & 1], static_cast<uint32_t>((j + 1) / 2) & 1u, a.status,
+                         kStatusAttnTc)) {
             ok = false;
             break;
           }
           fence_after();
-          issue_pv(j - 1);
+          issue_s(j + 1);
         }
-        // S = Q K^T over 128 dims: 8 steps of 16
-        const uint32_t sk = smem_u32(smem + OFF_K + (j & 1) * TILE);
-#pragma unroll
-        for (int k16 = 0; k16 < kHeadDim / 16; ++k16) {
-          const uint32_t off = (k16 >> 2) * HALF + (k16 & 3) * 32;
-          mma(tS, kmajor_desc(sq + off), kmajor_desc(sk + off), idesc(false), k16 > 0 ? 1u : 0u);
+        // the softmax of block j has read S, written P and rescaled O
+        if (!mbar_wait(pready, static_cast<uint32_t>(j) & 1u, a.status, kStatusAttnTc) ||
+            !mbar_wait(&vfull[j & 1], static_cast<uint32_t>(j / 2) & 1u, a.status,
+                       kStatusAttnTc)) {
+          ok = false;
+          break;
         }
-        commit(sbar);
-      }
-      if (ok && mbar_wait(pready, static_cast<uint32_t>(nkb - 1) & 1u, a.status, kStatusAttnTc)) {
         fence_after();
-        issue_pv(nkb - 1);
+        issue_pv(j);
       }
       // nothing may still write TMEM when it is freed (a barrier of its own:
       // an extra phase on obar could run ahead of the softmax warps' waits)
@@ -278,8 +311,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool ok = true;
     int exchanged = 0;  // pair barriers passed; both warps of a pair pass nkb + 1
     for (int j = 0; j < nkb; ++j) {
-      const bool okw = __all_sync(0xffffffffu, ok && mbar_wait(sbar, static_cast<uint32_t>(j) & 1u,
-                                                               a.status, kStatusAttnTc));
+      const bool okw = __all_sync(
+          0xffffffffu, ok && mbar_wait(&sbar[j & 1], static_cast<uint32_t>(j / 2) & 1u, a.status,
+                                       kStatusAttnTc));
       if (!okw) {
         ok = false;
         break;
@@ -290,7 +324,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int cb = 0; cb < KH / 16; ++cb) {
         uint32_t v[16];
-        ld16(tS + lane_off + half * KH + cb * 16, v);
+        ld16(tmem + static_cast<uint32_t>(j & 1) * 128 + lane_off + half * KH + cb * 16, v);
 #pragma unroll
         for (int e = 0; e < 16; ++e) {
           const int kpos = j * kKB + half * KH + cb * 16 + e;

@@ -26,7 +26,6 @@ enum DevStatus : int {
   kStatusEmptyWaitTimeout = 0x102,  // producer gave up waiting for a free ring slot
   kStatusDrainTimeout = 0x103,      // in-flight copies did not land during error drain
   kStatusBadArgs = 0x104,
-  kStatusReduceWaitTimeout = 0x105,  // GEMV: a tile's partial buffer stayed busy
   kStatusAttnCounter = 0x201,
   kStatusAttnRing = 0x202,          // decode-attention page ring wait timed out
   kStatusLinkTimeout = 0x301,       // a stage link receive waited past the bound

@@ -299,6 +299,7 @@ GemvTuning g_tuning() {
   if (const char* v = std::getenv("DIAL_B200_GEMV_SLOTS")) t.slots = std::atoi(v);
   if (const char* v = std::getenv("DIAL_B200_GEMV_GRID")) t.grid = std::atoi(v);
   if (const char* v = std::getenv("DIAL_B200_GEMV_NVFP4_STAGE")) t.nvfp4_stage = std::atoi(v);
+  if (const char* v = std::getenv("DIAL_B200_GEMV_STREAMK")) t.gemv_stream_k = std::atoi(v);
   if (const char* v = std::getenv("DIAL_B200_PDL")) t.pdl = std::atoi(v) != 0;
   if (const char* v = std::getenv("DIAL_B200_GEMM_MIN_ROWS")) t.gemm_min_rows = std::atoi(v);
   if (const char* v = std::getenv("DIAL_B200_ATTN_MIN_SPLIT")) t.attn_min_split = std::atoi(v);
@@ -319,7 +320,20 @@ struct GemmScratch {
   void* stage = nullptr;
   float* part = nullptr;
   size_t part_bytes = 0;
+  float* sk_part = nullptr;  // stage-balanced GEMV split: per-CTA part sums
+  int* sk_cnt = nullptr;     // ... and per-tile arrival counters (zero between launches)
 };
+
+constexpr size_t kSkBytes =
+    static_cast<size_t>(kGemvSkMaxCtas) * 2 * 128 * 4 + static_cast<size_t>(kGemvSkMaxTiles) * 4;
+
+// The stage-balanced GEMV split for this linear (gemv_stream_k 1: the
+// issue-bound NVFP4 / FP8 formats, 2: every format).
+bool stream_k_for(const Linear& L) {
+  const int mode = g_tuning().gemv_stream_k;
+  return mode >= 2 || (mode == 1 && (L.d.fmt == kFmtNvfp4G16 || L.d.fmt == kFmtFp8Block128 ||
+                                     L.d.fmt == kFmtFp8Row));
+}
 
 // Calls of M >= gemm_min_rows rows on a supported weight take the tcgen05
 // GEMM when staging scratch is given; everything else the decode GEMV.
@@ -369,6 +383,10 @@ void run_linear(const Linear& L, const void* x, int x_ld, const void* norm_w, fl
   a.status = status;
   a.trace = trace;
   a.trace_tag = trace_tag;
+  if (scratch && scratch->sk_part && stream_k_for(L)) {
+    a.sk_part = scratch->sk_part;
+    a.sk_cnt = scratch->sk_cnt;
+  }
   DIAL_CUDA(gemv_launch(a, L.act, epi, norm_w != nullptr, s, g_tuning()));
 }
 
@@ -416,6 +434,13 @@ struct dial_b200_engine {
   DevBuf amax_key, amax_count;  // head argmax keys / arrival counters, zero between steps
   DevBuf gemm_scratch;          // prefill GEMM activation staging (max_tokens rows)
   DevBuf gemm_part;             // split-K partial sums of small-row GEMM calls
+  DevBuf gemv_sk;               // stage-balanced GEMV split scratch (kSkBytes, zeroed)
+  GemmScratch scratch() {
+    GemmScratch g{gemm_scratch.p, gemm_part.as<float>(), gemm_part.bytes};
+    g.sk_part = gemv_sk.as<float>();
+    g.sk_cnt = reinterpret_cast<int*>(gemv_sk.as<uint8_t>() + kGemvSkMaxCtas * 2 * 128 * 4);
+    return g;
+  }
   DevBuf trace;                 // DIAL_B200_TRACE=<csv>: per-CTA timeline of decode steps
   std::string trace_path;
   // stage link over peer memory (link.h): this stage's inbox (IPC-exported),
@@ -562,6 +587,8 @@ void engine_init(dial_b200_engine* e, const dial_b200_model_config& c, int devic
     const int kpad = (kmax + 63) / 64 * 64;
     e->gemm_scratch.alloc(gemm_scratch_bytes(static_cast<int>(T), kpad));
     if (T >= 16) e->gemm_part.alloc(kGemmPartBytes);
+    e->gemv_sk.alloc(kSkBytes);
+    DIAL_CUDA(cudaMemset(e->gemv_sk.p, 0, e->gemv_sk.bytes));
   }
   if (c.has_head) {
     e->amax_key.alloc(static_cast<size_t>(T) * 8);
@@ -723,7 +750,7 @@ AttnDecodeArgs decode_attn_args(dial_b200_engine* e, LayerW& L, int M, int row0 
 void layer_decode(dial_b200_engine* e, LayerW& L, void* hidden, int M, cudaStream_t s,
                   int row0 = 0) {
   const float eps = e->cfg.rms_norm_eps;
-  const GemmScratch gsv{e->gemm_scratch.p, e->gemm_part.as<float>(), e->gemm_part.bytes};
+  const GemmScratch gsv = e->scratch();
   const GemmScratch* gs = &gsv;
   unsigned long long* tr = e->trace.as<unsigned long long>();
   const int tag = static_cast<int>(&L - e->layers.data() + e->cfg.first_layer) << 8;
@@ -743,7 +770,7 @@ void layer_decode(dial_b200_engine* e, LayerW& L, void* hidden, int M, cudaStrea
 void layer_prefill(dial_b200_engine* e, LayerW& L, void* hidden, int M, int session, int p0,
                    cudaStream_t s) {
   const float eps = e->cfg.rms_norm_eps;
-  const GemmScratch gsv{e->gemm_scratch.p, e->gemm_part.as<float>(), e->gemm_part.bytes};
+  const GemmScratch gsv = e->scratch();
   const GemmScratch* gs = &gsv;
   run_linear(L.qkv, hidden, e->H, L.input_norm.p, eps, e->qkv.p, e->QKV, M, kEpiStore, s, e->status,
              gs);
@@ -1680,7 +1707,7 @@ int dial_b200_engine_linear_replay(dial_b200_engine* eng, int layer, int which, 
     const int M = static_cast<int>(rows);
     // the GEMM scratch of the decode step: rows >= 16 take the tcgen05 GEMM
     // exactly as layer_decode does
-    const GemmScratch gsv{eng->gemm_scratch.p, eng->gemm_part.as<float>(), eng->gemm_part.bytes};
+    const GemmScratch gsv = eng->scratch();
     const GemmScratch* gs = &gsv;
     // layer < 0: rotate over every owned layer so that no launch finds its
     // weights in L2

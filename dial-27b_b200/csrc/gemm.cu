@@ -48,9 +48,16 @@ struct Cfg {
   static constexpr int BK = BK_;  // K per ring stage
   static constexpr int NATOM = BK / 64;
   static constexpr int CHUNK = BK == 128 ? 1152 : 1024;  // bytes per 16-row weight chunk
-  // load ring: 64-token tiles (calls of few rows) trade activation space for
-  // weight stages in flight
-  static constexpr int STAGES = (BM == 256 || BK == 128) ? 3 : (BN <= 64 ? 9 : 5);
+  // Three rings: weight bytes (RSTAGES, freed by the dequant warps once the
+  // bytes are in their registers), activation tiles (BSTAGES, freed by the
+  // MMAs) and dequantized weights (ASTAGES, freed by the MMAs).  The weight
+  // stream is thus not held back by MMA completion: with few token rows it
+  // keeps up to RSTAGES stages of weight bytes in flight per CTA.
+  // (64-token tiles: the activation ring is the deep one, since each of its
+  // loads is an L2 round trip issued only after the MMAs of its slot's
+  // previous tile completed)
+  static constexpr int RSTAGES = BM == 256 ? 4 : BK == 128 ? 6 : 8;
+  static constexpr int BSTAGES = (BM == 256 || BK == 128) ? 3 : BN <= 64 ? 12 : 4;
   static constexpr int ASTAGES = (BM == 256 || BK == 128) ? 2 : 4;  // dequantized-weight ring
   static constexpr int A_HALF = 128 * BK * 2;  // one 128-row MMA operand
   static constexpr int A_BYTES = BM * BK * 2;
@@ -59,10 +66,12 @@ struct Cfg {
   static constexpr int RAW_BYTES = (BM / 16) * CHUNK;
   static constexpr int OFF_A = 0;
   static constexpr int OFF_B = OFF_A + ASTAGES * A_BYTES;
-  static constexpr int OFF_RAW = OFF_B + STAGES * B_BYTES;
-  // barriers: full, lfree [STAGES]; aready, afree [ASTAGES]; accfull
-  static constexpr int OFF_BAR = (OFF_RAW + STAGES * RAW_BYTES + 15) / 16 * 16;
-  static constexpr int OFF_TMEM = OFF_BAR + (2 * STAGES + 2 * ASTAGES + 1) * 8;
+  static constexpr int OFF_RAW = OFF_B + BSTAGES * B_BYTES;
+  // barriers: wfull, wfree [RSTAGES]; bfull, bfree [BSTAGES]; aready, afree
+  // [ASTAGES]; accfull
+  static constexpr int OFF_BAR = (OFF_RAW + RSTAGES * RAW_BYTES + 15) / 16 * 16;
+  static constexpr int OFF_TMEM =
+      OFF_BAR + (2 * RSTAGES + 2 * BSTAGES + 2 * ASTAGES + 1) * 8;
   static constexpr int OFF_XEXP = OFF_TMEM + 16;
   static constexpr int SMEM_BYTES = OFF_XEXP + BN * 4 + 1024;  // + room to align to 1024
   static constexpr int kTmemCols = (BM / 128) * BN;  // one BN-column accumulator per half
@@ -273,7 +282,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmap, const GemmArgs a) {
   using AT = ActTraits<Act>;
   using G = Cfg<BM_, BN_, BK_>;
-  constexpr int BM = G::BM, BN = G::BN, BK = G::BK, STAGES = G::STAGES, ASTAGES = G::ASTAGES;
+  constexpr int BM = G::BM, BN = G::BN, BK = G::BK, ASTAGES = G::ASTAGES;
+  constexpr int RST = G::RSTAGES, BST = G::BSTAGES;
   constexpr int CHUNK = G::CHUNK, NATOM = G::NATOM, B_ATOM = G::B_ATOM;
   constexpr int A_BYTES = G::A_BYTES, A_HALF = G::A_HALF, B_BYTES = G::B_BYTES;
   constexpr int RAW_BYTES = G::RAW_BYTES, OFF_A = G::OFF_A, OFF_B = G::OFF_B;
@@ -282,9 +292,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + OFF_BAR);  // loads landed
-  uint64_t* lfree = full + STAGES;       // load slot consumed by dequant (8) and MMA (1)
-  uint64_t* aready = lfree + STAGES;     // dequantized weights written (8 warps)
+  uint64_t* wfull = reinterpret_cast<uint64_t*>(smem + OFF_BAR);  // weight bytes landed
+  uint64_t* wfree = wfull + RST;         // weight slot read by the 8 dequant warps
+  uint64_t* bfull = wfree + RST;         // activation tile landed
+  uint64_t* bfree = bfull + BST;         // activation tile read by the MMAs
+  uint64_t* aready = bfree + BST;        // dequantized weights written (8 warps)
   uint64_t* afree = aready + ASTAGES;    // MMAs reading them finished
   uint64_t* accfull = afree + ASTAGES;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + OFF_TMEM);
@@ -300,9 +312,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int C = a.w.C;
 
   if (tid == 0) {
-    for (int s = 0; s < STAGES; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&lfree[s], 9);
+    for (int s = 0; s < RST; ++s) {
+      mbar_init(&wfull[s], 1);
+      mbar_init(&wfree[s], 8);
+    }
+    for (int s = 0; s < BST; ++s) {
+      mbar_init(&bfull[s], 1);
+      mbar_init(&bfree[s], 1);
     }
     for (int s = 0; s < ASTAGES; ++s) {
       mbar_init(&aready[s], 8);
@@ -327,30 +343,47 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 0) {
-    // ------------------------------------------------------------ producer
+    // ---------------------------------------------------- weight producer
     if (lane == 0) {
       int it = 0;
       for (; it < NK; ++it) {
-        const int kb = KB0 + it, s = it % STAGES;
-        if (it >= STAGES &&
-            !mbar_wait(&lfree[s], static_cast<uint32_t>(it / STAGES - 1) & 1u, a.status,
+        const int kb = KB0 + it, s = it % RST;
+        if (it >= RST &&
+            !mbar_wait(&wfree[s], static_cast<uint32_t>(it / RST - 1) & 1u, a.status,
                        kStatusGemmWait))
           break;
-        mbar_arrive_expect_tx(&full[s], B_BYTES + RAW_BYTES);
-#pragma unroll
-        for (int at = 0; at < NATOM; ++at)
-          tma_load_2d(smem + OFF_B + s * B_BYTES + at * B_ATOM, &tmap, kb * BK + at * 64, tok0,
-                      &full[s]);
+        mbar_arrive_expect_tx(&wfull[s], RAW_BYTES);
         uint8_t* raw = smem + OFF_RAW + s * RAW_BYTES;
 #pragma unroll
         for (int c = 0; c < BM / 16; ++c) {
           const size_t t = static_cast<size_t>(blk) * (BM / 16) + c;
-          bulk_g2s(raw + c * CHUNK, a.w.tiles + (t * C + kb) * CHUNK, CHUNK, &full[s]);
+          bulk_g2s(raw + c * CHUNK, a.w.tiles + (t * C + kb) * CHUNK, CHUNK, &wfull[s]);
         }
       }
       // every copy issued must land before the CTA retires
-      for (int j = it > STAGES ? it - STAGES : 0; j < it; ++j)
-        if (!mbar_wait(&full[j % STAGES], static_cast<uint32_t>(j / STAGES) & 1u, a.status,
+      for (int j = it > RST ? it - RST : 0; j < it; ++j)
+        if (!mbar_wait(&wfull[j % RST], static_cast<uint32_t>(j / RST) & 1u, a.status,
+                       kStatusGemmWait))
+          break;
+    }
+  } else if (warp == 3) {
+    // ------------------------------------------------ activation producer
+    if (lane == 0) {
+      int it = 0;
+      for (; it < NK; ++it) {
+        const int kb = KB0 + it, s = it % BST;
+        if (it >= BST &&
+            !mbar_wait(&bfree[s], static_cast<uint32_t>(it / BST - 1) & 1u, a.status,
+                       kStatusGemmWait))
+          break;
+        mbar_arrive_expect_tx(&bfull[s], B_BYTES);
+#pragma unroll
+        for (int at = 0; at < NATOM; ++at)
+          tma_load_2d(smem + OFF_B + s * B_BYTES + at * B_ATOM, &tmap, kb * BK + at * 64, tok0,
+                      &bfull[s]);
+      }
+      for (int j = it > BST ? it - BST : 0; j < it; ++j)
+        if (!mbar_wait(&bfull[j % BST], static_cast<uint32_t>(j / BST) & 1u, a.status,
                        kStatusGemmWait))
           break;
     }
@@ -358,11 +391,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---------------------------------------------------------------- MMA
     if (lane == 0) {
       for (int it = 0; it < NK; ++it) {
-        const int s = it % STAGES, sa_i = it % ASTAGES;
+        const int s = it % BST, sa_i = it % ASTAGES;
         if (!mbar_wait(&aready[sa_i], static_cast<uint32_t>(it / ASTAGES) & 1u, a.status,
                        kStatusGemmWait))
           break;
-        if (!mbar_wait(&full[s], static_cast<uint32_t>(it / STAGES) & 1u, a.status,
+        if (!mbar_wait(&bfull[s], static_cast<uint32_t>(it / BST) & 1u, a.status,
                        kStatusGemmWait))
           break;
         tc_fence_after();
@@ -378,7 +411,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc_mma(tmem + BN, sw128_desc(sa + A_HALF + ka), db, G::kIdesc, acc);
         }
         tc_commit(&afree[sa_i]);
-        tc_commit(&lfree[s]);
+        tc_commit(&bfree[s]);
       }
       tc_commit(accfull);
       // the accumulator (and TMEM) stays in use until every MMA has finished
@@ -395,8 +428,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int r = dt >> 1, part = dt & 1;
       const int c = r >> 4, rr = r & 15;
       for (int it = 0; it < NK; ++it) {
-        const int s = it % STAGES, sa_i = it % ASTAGES;
-        if (!mbar_wait(&full[s], static_cast<uint32_t>(it / STAGES) & 1u, a.status,
+        const int s = it % RST, sa_i = it % ASTAGES;
+        if (!mbar_wait(&wfull[s], static_cast<uint32_t>(it / RST) & 1u, a.status,
                        kStatusGemmWait))
           break;
         const uint8_t* ch = smem + OFF_RAW + s * RAW_BYTES + c * CHUNK;
@@ -404,7 +437,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint4 n1 = *reinterpret_cast<const uint4*>(ch + rr * 64 + part * 32 + 16);
         const uint32_t scw = *reinterpret_cast<const uint32_t*>(ch + 1024 + rr * 8 + part * 4);
         __syncwarp();
-        if (lane == 0) mbar_arrive(&lfree[s]);
+        if (lane == 0) mbar_arrive(&wfree[s]);
         if (it >= ASTAGES &&
             !mbar_wait(&afree[sa_i], static_cast<uint32_t>(it / ASTAGES - 1) & 1u, a.status,
                        kStatusGemmWait))
@@ -453,10 +486,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       bsc_row = a.w.blk_scale + static_cast<size_t>(orig / 128) * a.w.blk_ld;
     }
     for (int it = 0; it < NK; ++it) {
-      const int kb = KB0 + it, s = it % STAGES, sa_i = it % ASTAGES;
+      const int kb = KB0 + it, s = it % RST, sa_i = it % ASTAGES;
       float bscale = 1.f;
       if constexpr (FMT == kFmtFp8Block128) bscale = __ldg(bsc_row + (kb >> 1));
-      if (!mbar_wait(&full[s], static_cast<uint32_t>(it / STAGES) & 1u, a.status,
+      if (!mbar_wait(&wfull[s], static_cast<uint32_t>(it / RST) & 1u, a.status,
                      kStatusGemmWait))
         break;
       const uint4* src = reinterpret_cast<const uint4*>(smem + OFF_RAW + s * RAW_BYTES +
@@ -465,7 +498,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int i = 0; i < NV; ++i) wv[i] = src[i];
       __syncwarp();
-      if (lane == 0) mbar_arrive(&lfree[s]);  // raw bytes are in registers
+      if (lane == 0) mbar_arrive(&wfree[s]);  // raw bytes are in registers
       if (it >= ASTAGES &&
           !mbar_wait(&afree[sa_i], static_cast<uint32_t>(it / ASTAGES - 1) & 1u, a.status,
                      kStatusGemmWait))
@@ -650,15 +683,31 @@ bool use_big_tiles(const GemmArgs& a) {
   return fits && 2 * static_cast<long long>((a.M + 255) / 256) * (a.w.T / 16) >= sm_count();
 }
 
-// K splits for a 128 x 128-tile launch: as many as keep the grid within the
-// SMs (at most 8, at least 4 k-steps each, partials within the workspace).
+// K splits for a 128-row-tile launch: the count (1..8, at least 4 k-steps
+// each, partials within the workspace) that minimises the weight stream over
+// the SM waves it fills plus the f32 partials written and read back.
+// Measured basis: one CTA per SM; a half-empty last wave leaves its SMs idle.
 int k_splits(const GemmArgs& a, int bn) {
   if (!a.part) return 1;
+  const int sms = sm_count();
   const long long base = static_cast<long long>((a.M + bn - 1) / bn) * (a.w.T / 8);
-  int ks = static_cast<int>(std::min<long long>(8, sm_count() / std::max(1ll, base)));
-  ks = std::min(ks, a.w.C / 4);
-  while (ks > 1 && static_cast<size_t>(ks) * a.M * a.w.N * 4 > a.part_bytes) --ks;
-  return std::max(ks, 1);
+  const double wbytes =
+      static_cast<double>(a.w.N) * a.w.K * (a.w.fmt == kFmtNvfp4G16 ? 0.5625 : 1.0);
+  int best = 1;
+  double best_cost = 0.0;
+  for (int ks = 1; ks <= 8; ++ks) {
+    if (ks > 1 && (a.w.C / ks < 4 || static_cast<size_t>(ks) * a.M * a.w.N * 4 > a.part_bytes))
+      break;
+    const long long ctas = base * ks;
+    const long long waves = (ctas + sms - 1) / sms;
+    const double fill = static_cast<double>(ctas) / (static_cast<double>(sms) * waves);
+    const double cost = wbytes / fill + (ks > 1 ? 8.0 * ks * a.M * a.w.N : 0.0);
+    if (ks == 1 || cost < best_cost * 0.999) {
+      best = ks;
+      best_cost = cost;
+    }
+  }
+  return best;
 }
 
 template <typename Act, int FMT>

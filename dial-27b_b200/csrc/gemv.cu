@@ -40,13 +40,11 @@ constexpr int kMaxSlots = 16;
 constexpr int kMaxM = 8;
 constexpr int kSmemBudget = 232448;         // 227 KB opt-in per CTA
 constexpr int kMiscFlag = 32, kMiscKeys = 64, kMiscScratch = 128;  // offsets in the misc area
-constexpr int kRedBufs = 2;  // per-tile partial buffers (tile i uses i % kRedBufs)
 
 struct SmemPlan {
-  int ring_off, x_off, red_off, misc_off, bsc_off, epi_off, bar_off, total;
+  int ring_off, x_off, red_off, misc_off, bsc_off, bar_off, total;
   int slots, xs_stride, bsc_rows_lo, bsc_rows_hi;
-  int sc;   // chunks per ring stage
-  int tpc;  // tiles per CTA at most
+  int sc;  // chunks per ring stage
 };
 
 // Chunks per ring stage.  int8 / e4m3 / dense: two per consumer warp (their
@@ -89,28 +87,23 @@ __host__ __device__ inline void bsc_rows(const DevQLinear& w, int t0, int t1, in
 }
 
 __host__ inline SmemPlan make_plan(const DevQLinear& w, int M, int grid, int slots_req, int nw,
-                                   int epi = kEpiStore, int sc_req = 0) {
+                                   int sc_req = 0) {
   SmemPlan p{};
   p.sc = stage_chunks(w, nw);
   // NVFP4 stage size override (2*nw .. 3*nw chunks)
   if (w.fmt == kFmtNvfp4G16 && sc_req >= 2 * nw && sc_req <= 3 * nw) p.sc = sc_req;
-  p.tpc = (w.T + grid - 1) / grid;
   const int stage = p.sc * fmt_chunk_bytes(w.fmt);
   p.xs_stride = w.K_pad + 8;
   const int x_bytes = ((M * p.xs_stride * 2) + 127) / 128 * 128;
-  const int red_bytes = kRedBufs * nw * 32 * 4 * 4;
+  const int red_bytes = 2 * nw * 32 * 4 * 4;
   // misc: xexp [kMaxM] ints | argmax flag | argmax keys [kMaxM] | staging
-  // scratch [2][nw] floats (block reduction of the activation statistics) |
-  // partial-buffer arrivals [kRedBufs] and completed epilogues [kRedBufs]
-  const int misc_bytes = kMiscScratch + 2 * nw * 4 + 2 * kRedBufs * 4;
-  // epilogue operands of the CTA's tiles, staged with the activations: row
-  // scales [tpc * 16] f32, residual inputs [M][tpc * 16] act
-  const int epi_bytes =
-      (p.tpc * 16 * 4 + (epi == kEpiResidual ? p.tpc * 16 * M * 2 : 0) + 127) / 128 * 128;
+  // scratch [2][nw] floats (block reduction of the activation statistics)
+  const int misc_bytes = kMiscScratch + 2 * nw * 4;
   int bsc_bytes = 0;
   if (w.fmt == kFmtFp8Block128) {
     // worst case over CTAs: tiles per CTA <= ceil(T/grid)
-    const int tpc = (w.T + grid - 1) / grid;
+    // (one more tile when the stage-balanced split starts mid-tile)
+    const int tpc = (w.T + grid - 1) / grid + 1;
     const int rows_lo = w.swiglu ? (8 * tpc + 127) / 128 + 1 : (16 * tpc + 127) / 128 + 1;
     const int rows_hi = w.swiglu ? rows_lo : 0;
     p.bsc_rows_lo = rows_lo;
@@ -119,7 +112,7 @@ __host__ inline SmemPlan make_plan(const DevQLinear& w, int M, int grid, int slo
     bsc_bytes = (bsc_bytes + 127) / 128 * 128;
   }
   const int bar_bytes = (2 * kMaxSlots + 2) * 8;
-  const int fixed = x_bytes + red_bytes + misc_bytes + bsc_bytes + epi_bytes + bar_bytes + 1024;
+  const int fixed = x_bytes + red_bytes + misc_bytes + bsc_bytes + bar_bytes + 1024;
   int slots = (kSmemBudget - fixed) / stage;
   if (slots > kMaxSlots) slots = kMaxSlots;
   if (slots_req > 0 && slots_req < slots) slots = slots_req;
@@ -129,8 +122,7 @@ __host__ inline SmemPlan make_plan(const DevQLinear& w, int M, int grid, int slo
   p.red_off = p.x_off + x_bytes;
   p.misc_off = p.red_off + red_bytes;
   p.bsc_off = p.misc_off + misc_bytes;
-  p.epi_off = p.bsc_off + bsc_bytes;
-  p.bar_off = p.epi_off + epi_bytes;
+  p.bar_off = p.bsc_off + bsc_bytes;
   p.total = p.bar_off + bar_bytes;
   return p;
 }
@@ -173,10 +165,6 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1)
   int* xexp = reinterpret_cast<int*>(smem + p.misc_off);
   float* scratch = reinterpret_cast<float*>(smem + p.misc_off + kMiscScratch);
   float* bsc = reinterpret_cast<float*>(smem + p.bsc_off);
-  int* arrive = reinterpret_cast<int*>(scratch + 2 * kNW);  // [kRedBufs]
-  int* done = arrive + kRedBufs;                            // [kRedBufs]
-  float* es = reinterpret_cast<float*>(smem + p.epi_off);   // row scales [tpc * 16]
-  Act* eo = reinterpret_cast<Act*>(es + p.tpc * 16);        // residual [M][tpc * 16]
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + p.bar_off);
   uint64_t* empty = full + kMaxSlots;
   uint64_t* sbar = empty + kMaxSlots;
@@ -184,9 +172,17 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   unsigned long long tstamp[4] = {a.trace ? global_ns() : 0ull, 0ull, 0ull, 0ull};
   const int T = a.w.T, C = a.w.C;
-  const int t0 = static_cast<int>(static_cast<long long>(T) * blockIdx.x / gridDim.x);
-  const int t1 = static_cast<int>(static_cast<long long>(T) * (blockIdx.x + 1) / gridDim.x);
   const int spt = (C + SC - 1) / SC;
+  // this CTA's stages [u0, u1) of the U = T * spt (whole tiles unless the
+  // stage-balanced split is on) and the tiles [t0, t1) they touch
+  const bool sk = a.sk_part != nullptr;
+  const long long U = static_cast<long long>(T) * spt;
+  auto unit0 = [&](int b) {
+    return sk ? static_cast<int>(U * b / gridDim.x)
+              : static_cast<int>(static_cast<long long>(T) * b / gridDim.x) * spt;
+  };
+  const int u0 = unit0(blockIdx.x), u1 = unit0(blockIdx.x + 1);
+  const int t0 = u0 / spt, t1 = u1 > u0 ? (u1 - 1) / spt + 1 : t0;
   const int NS = p.slots;
 
   int lo0 = 0, nlo = 0, hi0 = 0, nhi = 0;
@@ -199,7 +195,6 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1)
     }
     mbar_init(sbar, 1);
     fence_mbar_init();
-    for (int b = 0; b < kRedBufs; ++b) arrive[b] = done[b] = 0;
   }
   __syncthreads();
   pdl_launch_dependents();
@@ -225,7 +220,8 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1)
       bool ok = true;
       for (int t = t0; t < t1 && ok; ++t) {
         const uint8_t* src = a.w.tiles + static_cast<size_t>(t) * C * CB;
-        for (int s = 0; s < spt; ++s, ++it) {
+        const int s_end = t == t1 - 1 ? u1 - t * spt : spt;
+        for (int s = t == t0 ? u0 - t * spt : 0; s < s_end; ++s, ++it) {
           if (round > 0 && !mbar_wait(&empty[slot], (round - 1) & 1u, a.status,
                                       kStatusEmptyWaitTimeout)) {
             ok = false;
@@ -258,6 +254,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1)
 
   // -------------------------------------------------------------- consumers
   int* sflag = reinterpret_cast<int*>(smem + p.misc_off + kMiscFlag);
+  int* skflag = sflag + 1;  // stage-balanced split: this CTA finishes the tile
   unsigned long long* skey = reinterpret_cast<unsigned long long*>(smem + p.misc_off + kMiscKeys);
   if constexpr (EPI == kEpiArgmax) {
     if (threadIdx.x < kMaxM) skey[threadIdx.x] = 0ull;
@@ -273,17 +270,6 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1)
   }
   pdl_wait();
   if (a.trace) tstamp[1] = global_ns();
-  // epilogue operands of the CTA's tiles (their loads overlap the staging's)
-  const int nrow = (t1 - t0) * 16;
-  for (int r = threadIdx.x; r < nrow; r += kNW * 32)
-    es[r] = a.w.row_scale ? a.w.row_scale[t0 * 16 + r] : 1.f;
-  if constexpr (EPI == kEpiResidual) {
-    for (int e = threadIdx.x; e < nrow * a.M; e += kNW * 32) {
-      const int tt = e / nrow, r = e % nrow, n = t0 * 16 + r;
-      eo[e] = n < a.w.N ? reinterpret_cast<const Act*>(a.out)[static_cast<size_t>(tt) * a.out_ld + n]
-                        : AT::from_f(0.f);
-    }
-  }
   stage_x<Act, XT, NORM, kScaleX, kNW>(a, xs, p.xs_stride, xexp, scratch);
   named_bar_sync(1, kNW * 32);
   if (a.trace) tstamp[2] = global_ns();
@@ -299,6 +285,25 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1)
   bool ok = true;
   int tile_i = 0;
   for (int t = t0; t < t1; ++t, ++tile_i) {
+    // Epilogue operands of this tile (row scales, residual inputs) are loaded
+    // now, so their latency hides behind the tile's stages.
+    float pre_a = 1.f, pre_b = 1.f, pre_o = 0.f;
+    if (threadIdx.x < 128) {
+      const int rr = threadIdx.x >> 3, tt = threadIdx.x & 7;
+      if constexpr (EPI == kEpiSwiglu) {
+        if (threadIdx.x < 64 && a.w.row_scale) {
+          pre_a = a.w.row_scale[t * 16 + rr];
+          pre_b = a.w.row_scale[t * 16 + 8 + rr];
+        }
+      } else {
+        const int n = t * 16 + rr;
+        if (a.w.row_scale) pre_a = a.w.row_scale[t * 16 + rr];
+        if constexpr (EPI == kEpiResidual) {
+          if (tt < a.M && n < a.w.N)
+            pre_o = AT::to_f(reinterpret_cast<const Act*>(a.out)[static_cast<size_t>(tt) * a.out_ld + n]);
+        }
+      }
+    }
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
     float acc2[4] = {0.f, 0.f, 0.f, 0.f};
     float pacc[4][4] = {};
@@ -311,7 +316,8 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1)
         rb_lo = rb_hi = (16 * t) / 128 - lo0;
       }
     }
-    for (int s = 0; s < spt; ++s) {
+    const int s_begin = t == t0 ? u0 - t * spt : 0, s_end = t == t1 - 1 ? u1 - t * spt : spt;
+    for (int s = s_begin; s < s_end; ++s) {
       if (ok && !mbar_wait(&full[slot], round & 1u, a.status, kStatusFullWaitTimeout)) ok = false;
       const int nch = min(SC, C - s * SC);
       const uint8_t* st = ring + static_cast<size_t>(slot) * SBYTES;
@@ -369,44 +375,15 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1)
         ++round;
       }
     }
-    // ---- cross-warp reduction: every warp leaves its partial in the tile's
-    // buffer; the last warp to arrive sums them and runs the epilogue while
-    // the others go on streaming (no CTA-wide barrier per tile)
-    const int b = tile_i % kRedBufs;
-    float* rb = red + b * (kNW * 128);
+    // ---- cross-warp reduction (double-buffered by tile parity)
+    float* rb = red + (tile_i & 1) * (kNW * 128);
 #pragma unroll
     for (int q = 0; q < 4; ++q)
       acc[q] += acc2[q] + ((pacc[0][q] + pacc[1][q]) + (pacc[2][q] + pacc[3][q]));
-    if (tile_i >= kRedBufs) {
-      // the buffer's previous tile (tile_i - kRedBufs) must have been summed
-      if (lane == 0) {
-        volatile int* d = done + b;
-        const int want = tile_i - kRedBufs + 1;
-        if (*d < want) {
-          const unsigned long long tw = global_ns();
-          while (*d < want) {
-            if (global_ns() - tw > kWaitLimitNs) {
-              set_status(a.status, kStatusReduceWaitTimeout);
-              break;
-            }
-            __nanosleep(32);
-          }
-        }
-      }
-      __syncwarp();
-      __threadfence_block();
-    }
     *reinterpret_cast<float4*>(rb + (warp * 32 + lane) * 4) =
         make_float4(acc[0], acc[1], acc[2], acc[3]);
-    __syncwarp();
-    int last = 0;
-    if (lane == 0) {
-      __threadfence_block();
-      last = atomicAdd(&arrive[b], 1) == kNW - 1;
-    }
-    if (!__shfl_sync(0xffffffffu, last, 0)) continue;
-    __syncwarp();
-    __threadfence_block();
+    named_bar_sync(1, kNW * 32);
+    const int i = threadIdx.x;
     auto gather = [&](int rr, int tt) {
       const int src_lane = (rr & 7) * 4 + (tt >> 1);
       const int reg = ((rr >> 3) << 1) | (tt & 1);
@@ -415,30 +392,61 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1)
       for (int w = 0; w < kNW; ++w) v += rb[(w * 32 + src_lane) * 4 + reg];
       return v;
     };
-    const int nt = t - t0;
+    // A tile shared with neighbouring CTAs (stage-balanced split): each part
+    // leaves its 16 x 8 sums in its CTA's slot; the last part to arrive adds
+    // them in CTA order and runs the epilogue.
+    const bool whole = s_begin == 0 && s_end == spt;
+    int b_first = blockIdx.x, b_last = blockIdx.x;
+    auto slot_of = [&](int b) {
+      return a.sk_part + (b * 2 + (t == unit0(b) / spt ? 0 : 1)) * 128;
+    };
+    if (!whole) {
+      auto owner = [&](int u) {  // the CTA whose stage range holds unit u
+        int b = static_cast<int>(static_cast<long long>(u) * gridDim.x / U);
+        while (b + 1 < static_cast<int>(gridDim.x) && unit0(b + 1) <= u) ++b;
+        while (b > 0 && unit0(b) > u) --b;
+        return b;
+      };
+      b_first = owner(t * spt);
+      b_last = owner(t * spt + spt - 1);
+      if (i < 128) __stcg(slot_of(blockIdx.x) + i, gather(i >> 3, i & 7));
+      __threadfence();
+      named_bar_sync(1, kNW * 32);
+      if (i == 0) *skflag = atomicAdd(a.sk_cnt + t, 1) == b_last - b_first;
+      named_bar_sync(1, kNW * 32);
+      if (!*skflag) continue;
+      __threadfence();
+      if (i == 0) a.sk_cnt[t] = 0;
+    }
+    auto getv = [&](int rr, int tt) {
+      if (whole) return gather(rr, tt);
+      float v = 0.f;
+      for (int b = b_first; b <= b_last; ++b) v += __ldcg(slot_of(b) + rr * 8 + tt);
+      return v;
+    };
     if constexpr (EPI == kEpiSwiglu) {
-      for (int f = lane; f < 8 * a.M; f += 32) {
-        const int rr = f & 7, tt = f >> 3;
+      if (i < 64) {
+        const int rr = i >> 3, tt = i & 7;
         const int j = t * 8 + rr;
-        if (j < I) {
-          float vg = gather(rr, tt), vu = gather(rr + 8, tt);
+        if (tt < a.M && j < I) {
+          float vg = getv(rr, tt), vu = getv(rr + 8, tt);
           float mul = exp2i(xexp[tt]);
           if constexpr (FMT == kFmtNvfp4G16) mul *= a.w.global_scale;
-          const float sg = mul * es[nt * 16 + rr], su = mul * es[nt * 16 + 8 + rr];
+          const float sg = mul * pre_a, su = mul * pre_b;
           const float gq = AT::round(vg * sg), uq = AT::round(vu * su);
           Act* out = reinterpret_cast<Act*>(a.out) + static_cast<size_t>(tt) * a.out_ld + j;
           *out = AT::from_f(silu_mul_ref<Act>(gq, uq));
         }
       }
     } else {
-      for (int f = lane; f < 16 * a.M; f += 32) {
-        const int rr = f & 15, tt = f >> 4;
+      if (i < 128) {
+        const int rr = i >> 3, tt = i & 7;
         const int n = t * 16 + rr;
-        if (n < a.w.N) {
-          float v = gather(rr, tt);
+        if (tt < a.M && n < a.w.N) {
+          float v = getv(rr, tt);
           float mul = exp2i(xexp[tt]);
           if constexpr (FMT == kFmtNvfp4G16) mul *= a.w.global_scale;
-          mul *= es[nt * 16 + rr];
+          mul *= pre_a;
           const float y = AT::round(v * mul);
           if constexpr (EPI == kEpiArgmax) {
             if (a.out)
@@ -447,7 +455,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1)
           } else {
             Act* out = reinterpret_cast<Act*>(a.out) + static_cast<size_t>(tt) * a.out_ld + n;
             if constexpr (EPI == kEpiResidual) {
-              *out = AT::from_f(y + AT::to_f(eo[tt * nrow + nt * 16 + rr]));
+              *out = AT::from_f(y + pre_o);
             } else {
               *out = AT::from_f(y);
             }
@@ -455,16 +463,10 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1)
         }
       }
     }
-    __syncwarp();
-    if (lane == 0) {
-      arrive[b] = 0;
-      __threadfence_block();
-      *reinterpret_cast<volatile int*>(done + b) = tile_i + 1;
-      if (a.trace && t == t1 - 1) {
-        tstamp[3] = global_ns();
-        trace_record(a.trace, a.trace_tag, tstamp);
-      }
-    }
+  }
+  if (a.trace && threadIdx.x == 0) {
+    tstamp[3] = global_ns();
+    trace_record(a.trace, a.trace_tag, tstamp);
   }
   if constexpr (EPI == kEpiArgmax) {
     // CTA best -> global keys; the last CTA to arrive decodes and resets them.
@@ -497,8 +499,11 @@ cudaError_t launch_one(const GemvArgs& a, const GemvTuning& t, cudaStream_t stre
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   int grid = grid_req > 0 ? grid_req : sms;
   if (grid > a.w.T) grid = a.w.T;
-  const SmemPlan p = make_plan(a.w, a.M, grid, slots_req, NW, EPI, t.nvfp4_stage);
+  const SmemPlan p = make_plan(a.w, a.M, grid, slots_req, NW, t.nvfp4_stage);
   if (p.slots < 2) return cudaErrorInvalidConfiguration;
+  GemvArgs ak = a;
+  if (ak.sk_part && (grid > kGemvSkMaxCtas || a.w.T > kGemvSkMaxTiles || !gemv_stream_k_pays(a.w, grid)))
+    ak.sk_part = nullptr;
   auto kern = gemv_kernel<Act, FMT, EPI, NORM, NW>;
   cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          kSmemBudget);
@@ -517,7 +522,7 @@ cudaError_t launch_one(const GemvArgs& a, const GemvTuning& t, cudaStream_t stre
   attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, kern, a, p);
+  return cudaLaunchKernelEx(&cfg, kern, ak, p);
 }
 
 template <typename Act, int FMT, int EPI, bool NORM>
