@@ -299,7 +299,6 @@ GemvTuning g_tuning() {
   if (const char* v = std::getenv("DIAL_B200_GEMV_SLOTS")) t.slots = std::atoi(v);
   if (const char* v = std::getenv("DIAL_B200_GEMV_GRID")) t.grid = std::atoi(v);
   if (const char* v = std::getenv("DIAL_B200_GEMV_NVFP4_STAGE")) t.nvfp4_stage = std::atoi(v);
-  if (const char* v = std::getenv("DIAL_B200_GEMV_STREAMK")) t.gemv_stream_k = std::atoi(v);
   if (const char* v = std::getenv("DIAL_B200_PDL")) t.pdl = std::atoi(v) != 0;
   if (const char* v = std::getenv("DIAL_B200_GEMM_MIN_ROWS")) t.gemm_min_rows = std::atoi(v);
   if (const char* v = std::getenv("DIAL_B200_ATTN_MIN_SPLIT")) t.attn_min_split = std::atoi(v);
@@ -320,20 +319,7 @@ struct GemmScratch {
   void* stage = nullptr;
   float* part = nullptr;
   size_t part_bytes = 0;
-  float* sk_part = nullptr;  // stage-balanced GEMV split: per-CTA part sums
-  int* sk_cnt = nullptr;     // ... and per-tile arrival counters (zero between launches)
 };
-
-constexpr size_t kSkBytes =
-    static_cast<size_t>(kGemvSkMaxCtas) * 2 * 128 * 4 + static_cast<size_t>(kGemvSkMaxTiles) * 4;
-
-// The stage-balanced GEMV split for this linear (gemv_stream_k 1: the
-// issue-bound NVFP4 / FP8 formats, 2: every format).
-bool stream_k_for(const Linear& L) {
-  const int mode = g_tuning().gemv_stream_k;
-  return mode >= 2 || (mode == 1 && (L.d.fmt == kFmtNvfp4G16 || L.d.fmt == kFmtFp8Block128 ||
-                                     L.d.fmt == kFmtFp8Row));
-}
 
 // Calls of M >= gemm_min_rows rows on a supported weight take the tcgen05
 // GEMM when staging scratch is given; everything else the decode GEMV.
@@ -383,10 +369,6 @@ void run_linear(const Linear& L, const void* x, int x_ld, const void* norm_w, fl
   a.status = status;
   a.trace = trace;
   a.trace_tag = trace_tag;
-  if (scratch && scratch->sk_part && stream_k_for(L)) {
-    a.sk_part = scratch->sk_part;
-    a.sk_cnt = scratch->sk_cnt;
-  }
   DIAL_CUDA(gemv_launch(a, L.act, epi, norm_w != nullptr, s, g_tuning()));
 }
 
@@ -434,13 +416,7 @@ struct dial_b200_engine {
   DevBuf amax_key, amax_count;  // head argmax keys / arrival counters, zero between steps
   DevBuf gemm_scratch;          // prefill GEMM activation staging (max_tokens rows)
   DevBuf gemm_part;             // split-K partial sums of small-row GEMM calls
-  DevBuf gemv_sk;               // stage-balanced GEMV split scratch (kSkBytes, zeroed)
-  GemmScratch scratch() {
-    GemmScratch g{gemm_scratch.p, gemm_part.as<float>(), gemm_part.bytes};
-    g.sk_part = gemv_sk.as<float>();
-    g.sk_cnt = reinterpret_cast<int*>(gemv_sk.as<uint8_t>() + kGemvSkMaxCtas * 2 * 128 * 4);
-    return g;
-  }
+  GemmScratch scratch() { return GemmScratch{gemm_scratch.p, gemm_part.as<float>(), gemm_part.bytes}; }
   DevBuf trace;                 // DIAL_B200_TRACE=<csv>: per-CTA timeline of decode steps
   std::string trace_path;
   // stage link over peer memory (link.h): this stage's inbox (IPC-exported),
@@ -587,8 +563,6 @@ void engine_init(dial_b200_engine* e, const dial_b200_model_config& c, int devic
     const int kpad = (kmax + 63) / 64 * 64;
     e->gemm_scratch.alloc(gemm_scratch_bytes(static_cast<int>(T), kpad));
     if (T >= 16) e->gemm_part.alloc(kGemmPartBytes);
-    e->gemv_sk.alloc(kSkBytes);
-    DIAL_CUDA(cudaMemset(e->gemv_sk.p, 0, e->gemv_sk.bytes));
   }
   if (c.has_head) {
     e->amax_key.alloc(static_cast<size_t>(T) * 8);

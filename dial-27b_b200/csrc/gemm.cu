@@ -41,6 +41,19 @@ constexpr int kStatusGemmWait = 0x401;
 // K per stage is one weight chunk: 64 (int8 / e4m3) or 128 (NVFP4, 1152-byte
 // chunks with their group scales).  Operand tiles are K-major with 64-column
 // (128-byte) swizzle atoms: A [half][atom][128 rows][128 B], B [atom][BN][128 B].
+// Ring depths of the 128 x 64 tiles (calls of at most 64 rows).
+#ifndef DIAL_B200_GEMM_RST_SMALL
+#define DIAL_B200_GEMM_RST_SMALL 8
+#endif
+#ifndef DIAL_B200_GEMM_BST_SMALL
+#define DIAL_B200_GEMM_BST_SMALL 12
+#endif
+#ifndef DIAL_B200_GEMM_AST_SMALL
+#define DIAL_B200_GEMM_AST_SMALL 4
+#endif
+constexpr int kRstSmall = DIAL_B200_GEMM_RST_SMALL, kBstSmall = DIAL_B200_GEMM_BST_SMALL,
+              kAstSmall = DIAL_B200_GEMM_AST_SMALL;
+
 template <int BM_, int BN_, int BK_ = 64>
 struct Cfg {
   static constexpr int BM = BM_;  // weight rows per CTA
@@ -56,9 +69,10 @@ struct Cfg {
   // (64-token tiles: the activation ring is the deep one, since each of its
   // loads is an L2 round trip issued only after the MMAs of its slot's
   // previous tile completed)
-  static constexpr int RSTAGES = BM == 256 ? 4 : BK == 128 ? 6 : 8;
-  static constexpr int BSTAGES = (BM == 256 || BK == 128) ? 3 : BN <= 64 ? 12 : 4;
-  static constexpr int ASTAGES = (BM == 256 || BK == 128) ? 2 : 4;  // dequantized-weight ring
+  static constexpr int RSTAGES = BM == 256 ? 4 : BK == 128 ? 6 : BN <= 64 ? kRstSmall : 8;
+  static constexpr int BSTAGES = (BM == 256 || BK == 128) ? 3 : BN <= 64 ? kBstSmall : 4;
+  static constexpr int ASTAGES =  // dequantized-weight ring
+      (BM == 256 || BK == 128) ? 2 : BN <= 64 ? kAstSmall : 4;
   static constexpr int A_HALF = 128 * BK * 2;  // one 128-row MMA operand
   static constexpr int A_BYTES = BM * BK * 2;
   static constexpr int B_ATOM = BN * 128;
@@ -314,7 +328,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (tid == 0) {
     for (int s = 0; s < RST; ++s) {
       mbar_init(&wfull[s], 1);
-      mbar_init(&wfree[s], 8);
+      mbar_init(&wfree[s], a.couple ? 9 : 8);
     }
     for (int s = 0; s < BST; ++s) {
       mbar_init(&bfull[s], 1);
@@ -412,6 +426,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tc_commit(&afree[sa_i]);
         tc_commit(&bfree[s]);
+        if (a.couple) tc_commit(&wfree[it % RST]);
       }
       tc_commit(accfull);
       // the accumulator (and TMEM) stays in use until every MMA has finished
@@ -797,6 +812,9 @@ cudaError_t gemm_w8a16_launch(const GemmArgs& a, int act, int epi, cudaStream_t 
   if (epi == kEpiSwiglu && !a.w.swiglu) return cudaErrorInvalidValue;
   EncodeTiledFn enc = encode_fn();
   if (!enc) return cudaErrorNotSupported;
+  GemmArgs a2 = a;
+  a2.couple = 1;
+  if (const char* v = std::getenv("DIAL_B200_GEMM_COUPLE")) a2.couple = std::atoi(v);
   CUtensorMap map;
   const cuuint64_t dims[2] = {static_cast<cuuint64_t>(a.w.K_pad), static_cast<cuuint64_t>(a.M)};
   const cuuint64_t strides[1] = {static_cast<cuuint64_t>(a.w.K_pad) * 2};
@@ -810,8 +828,8 @@ cudaError_t gemm_w8a16_launch(const GemmArgs& a, int act, int epi, cudaStream_t 
           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
     return cudaErrorInvalidValue;
   const int ks = big ? 1 : k_splits(a, bn);
-  return act == 0 ? launch_act<__nv_bfloat16>(map, a, epi, big, ks, bn, s)
-                  : launch_act<__half>(map, a, epi, big, ks, bn, s);
+  return act == 0 ? launch_act<__nv_bfloat16>(map, a2, epi, big, ks, bn, s)
+                  : launch_act<__half>(map, a2, epi, big, ks, bn, s);
 }
 
 }  // namespace dialb200

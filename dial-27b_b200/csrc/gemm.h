@@ -27,6 +27,7 @@ struct GemmArgs {
   // the epilogue.  Null: one pass over K.
   float* part;
   size_t part_bytes;
+  int couple;  // diagnostic: weight slots also wait for the MMAs of their k-step
 };
 
 // True when the weight can take the tensor-core path: W8A16, FP8 (row or

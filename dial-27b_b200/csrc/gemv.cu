@@ -102,8 +102,7 @@ __host__ inline SmemPlan make_plan(const DevQLinear& w, int M, int grid, int slo
   int bsc_bytes = 0;
   if (w.fmt == kFmtFp8Block128) {
     // worst case over CTAs: tiles per CTA <= ceil(T/grid)
-    // (one more tile when the stage-balanced split starts mid-tile)
-    const int tpc = (w.T + grid - 1) / grid + 1;
+    const int tpc = (w.T + grid - 1) / grid;
     const int rows_lo = w.swiglu ? (8 * tpc + 127) / 128 + 1 : (16 * tpc + 127) / 128 + 1;
     const int rows_hi = w.swiglu ? rows_lo : 0;
     p.bsc_rows_lo = rows_lo;
@@ -172,17 +171,9 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   unsigned long long tstamp[4] = {a.trace ? global_ns() : 0ull, 0ull, 0ull, 0ull};
   const int T = a.w.T, C = a.w.C;
+  const int t0 = static_cast<int>(static_cast<long long>(T) * blockIdx.x / gridDim.x);
+  const int t1 = static_cast<int>(static_cast<long long>(T) * (blockIdx.x + 1) / gridDim.x);
   const int spt = (C + SC - 1) / SC;
-  // this CTA's stages [u0, u1) of the U = T * spt (whole tiles unless the
-  // stage-balanced split is on) and the tiles [t0, t1) they touch
-  const bool sk = a.sk_part != nullptr;
-  const long long U = static_cast<long long>(T) * spt;
-  auto unit0 = [&](int b) {
-    return sk ? static_cast<int>(U * b / gridDim.x)
-              : static_cast<int>(static_cast<long long>(T) * b / gridDim.x) * spt;
-  };
-  const int u0 = unit0(blockIdx.x), u1 = unit0(blockIdx.x + 1);
-  const int t0 = u0 / spt, t1 = u1 > u0 ? (u1 - 1) / spt + 1 : t0;
   const int NS = p.slots;
 
   int lo0 = 0, nlo = 0, hi0 = 0, nhi = 0;
@@ -220,8 +211,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1)
       bool ok = true;
       for (int t = t0; t < t1 && ok; ++t) {
         const uint8_t* src = a.w.tiles + static_cast<size_t>(t) * C * CB;
-        const int s_end = t == t1 - 1 ? u1 - t * spt : spt;
-        for (int s = t == t0 ? u0 - t * spt : 0; s < s_end; ++s, ++it) {
+        for (int s = 0; s < spt; ++s, ++it) {
           if (round > 0 && !mbar_wait(&empty[slot], (round - 1) & 1u, a.status,
                                       kStatusEmptyWaitTimeout)) {
             ok = false;
@@ -254,7 +244,6 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1)
 
   // -------------------------------------------------------------- consumers
   int* sflag = reinterpret_cast<int*>(smem + p.misc_off + kMiscFlag);
-  int* skflag = sflag + 1;  // stage-balanced split: this CTA finishes the tile
   unsigned long long* skey = reinterpret_cast<unsigned long long*>(smem + p.misc_off + kMiscKeys);
   if constexpr (EPI == kEpiArgmax) {
     if (threadIdx.x < kMaxM) skey[threadIdx.x] = 0ull;
@@ -316,8 +305,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1)
         rb_lo = rb_hi = (16 * t) / 128 - lo0;
       }
     }
-    const int s_begin = t == t0 ? u0 - t * spt : 0, s_end = t == t1 - 1 ? u1 - t * spt : spt;
-    for (int s = s_begin; s < s_end; ++s) {
+    for (int s = 0; s < spt; ++s) {
       if (ok && !mbar_wait(&full[slot], round & 1u, a.status, kStatusFullWaitTimeout)) ok = false;
       const int nch = min(SC, C - s * SC);
       const uint8_t* st = ring + static_cast<size_t>(slot) * SBYTES;
@@ -392,44 +380,12 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1)
       for (int w = 0; w < kNW; ++w) v += rb[(w * 32 + src_lane) * 4 + reg];
       return v;
     };
-    // A tile shared with neighbouring CTAs (stage-balanced split): each part
-    // leaves its 16 x 8 sums in its CTA's slot; the last part to arrive adds
-    // them in CTA order and runs the epilogue.
-    const bool whole = s_begin == 0 && s_end == spt;
-    int b_first = blockIdx.x, b_last = blockIdx.x;
-    auto slot_of = [&](int b) {
-      return a.sk_part + (b * 2 + (t == unit0(b) / spt ? 0 : 1)) * 128;
-    };
-    if (!whole) {
-      auto owner = [&](int u) {  // the CTA whose stage range holds unit u
-        int b = static_cast<int>(static_cast<long long>(u) * gridDim.x / U);
-        while (b + 1 < static_cast<int>(gridDim.x) && unit0(b + 1) <= u) ++b;
-        while (b > 0 && unit0(b) > u) --b;
-        return b;
-      };
-      b_first = owner(t * spt);
-      b_last = owner(t * spt + spt - 1);
-      if (i < 128) __stcg(slot_of(blockIdx.x) + i, gather(i >> 3, i & 7));
-      __threadfence();
-      named_bar_sync(1, kNW * 32);
-      if (i == 0) *skflag = atomicAdd(a.sk_cnt + t, 1) == b_last - b_first;
-      named_bar_sync(1, kNW * 32);
-      if (!*skflag) continue;
-      __threadfence();
-      if (i == 0) a.sk_cnt[t] = 0;
-    }
-    auto getv = [&](int rr, int tt) {
-      if (whole) return gather(rr, tt);
-      float v = 0.f;
-      for (int b = b_first; b <= b_last; ++b) v += __ldcg(slot_of(b) + rr * 8 + tt);
-      return v;
-    };
     if constexpr (EPI == kEpiSwiglu) {
       if (i < 64) {
         const int rr = i >> 3, tt = i & 7;
         const int j = t * 8 + rr;
         if (tt < a.M && j < I) {
-          float vg = getv(rr, tt), vu = getv(rr + 8, tt);
+          float vg = gather(rr, tt), vu = gather(rr + 8, tt);
           float mul = exp2i(xexp[tt]);
           if constexpr (FMT == kFmtNvfp4G16) mul *= a.w.global_scale;
           const float sg = mul * pre_a, su = mul * pre_b;
@@ -443,7 +399,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1)
         const int rr = i >> 3, tt = i & 7;
         const int n = t * 16 + rr;
         if (tt < a.M && n < a.w.N) {
-          float v = getv(rr, tt);
+          float v = gather(rr, tt);
           float mul = exp2i(xexp[tt]);
           if constexpr (FMT == kFmtNvfp4G16) mul *= a.w.global_scale;
           mul *= pre_a;
@@ -501,9 +457,6 @@ cudaError_t launch_one(const GemvArgs& a, const GemvTuning& t, cudaStream_t stre
   if (grid > a.w.T) grid = a.w.T;
   const SmemPlan p = make_plan(a.w, a.M, grid, slots_req, NW, t.nvfp4_stage);
   if (p.slots < 2) return cudaErrorInvalidConfiguration;
-  GemvArgs ak = a;
-  if (ak.sk_part && (grid > kGemvSkMaxCtas || a.w.T > kGemvSkMaxTiles || !gemv_stream_k_pays(a.w, grid)))
-    ak.sk_part = nullptr;
   auto kern = gemv_kernel<Act, FMT, EPI, NORM, NW>;
   cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          kSmemBudget);
@@ -522,7 +475,7 @@ cudaError_t launch_one(const GemvArgs& a, const GemvTuning& t, cudaStream_t stre
   attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, kern, ak, p);
+  return cudaLaunchKernelEx(&cfg, kern, a, p);
 }
 
 template <typename Act, int FMT, int EPI, bool NORM>

@@ -33,33 +33,13 @@ struct GemvArgs {
   int32_t* amax_tok;
   unsigned long long* trace;  // opt-in timeline records (common.cuh), null = off
   int trace_tag;
-  // Stage-balanced split (non-null, engine-owned, zero on entry and left
-  // zero): CTA b streams stages [U b / G, U (b+1) / G) of the U = T * stages
-  // per tile, so a tile may be shared by neighbouring CTAs; each leaves its
-  // part's 16 x M sums in sk_part [G][2][128] and the last of a tile's parts
-  // to arrive (sk_cnt [T]) adds them in CTA order and runs the epilogue.
-  float* sk_part;
-  int* sk_cnt;
 };
-
-// Scratch bounds of the stage-balanced split: sk_part [kGemvSkMaxCtas][2][128]
-// f32, sk_cnt [kGemvSkMaxTiles] int.
-constexpr int kGemvSkMaxCtas = 256, kGemvSkMaxTiles = 1 << 16;
-
-// Stream the stages of a linear across CTAs (stream-K) instead of whole tiles
-// when whole tiles leave the busiest CTA more than 10 % above the mean.
-inline bool gemv_stream_k_pays(const DevQLinear& w, int grid) {
-  if (w.T < 1 || grid < 1) return false;
-  const int tpc = (w.T + grid - 1) / grid;
-  return static_cast<long long>(tpc) * grid * 10 > static_cast<long long>(w.T) * 11;
-}
 
 struct GemvTuning {
   int slots = 0;   // ring stages (0 = as many as fit)
   int grid = 0;    // CTAs (0 = one per SM)
   bool pdl = true; // programmatic dependent launch
   int nvfp4_stage = 0;  // NVFP4 GEMV chunks per ring stage (0: chosen per linear)
-  int gemv_stream_k = 1;  // stage-balanced GEMV split: 0 off, 1 NVFP4 / FP8, 2 all formats
   int gemm_min_rows = 16;    // rows from which linears take the tcgen05 GEMM (0 = never)
   int attn_min_split = 0;    // decode attention: context tokens per split at least (0 = 16)
   bool attn_tc = true;       // prefill attention on the tensor cores when supported
