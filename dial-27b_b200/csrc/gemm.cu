@@ -32,7 +32,6 @@
 namespace dialb200 {
 namespace {
 
-constexpr int kThreads = 384;
 constexpr int kEpiPartial = 8;  // split-K: scaled f32 partial sums into GemmArgs::part
 constexpr int kStatusGemmWait = 0x401;
 
@@ -41,19 +40,6 @@ constexpr int kStatusGemmWait = 0x401;
 // K per stage is one weight chunk: 64 (int8 / e4m3) or 128 (NVFP4, 1152-byte
 // chunks with their group scales).  Operand tiles are K-major with 64-column
 // (128-byte) swizzle atoms: A [half][atom][128 rows][128 B], B [atom][BN][128 B].
-// Ring depths of the 128 x 64 tiles (calls of at most 64 rows).
-#ifndef DIAL_B200_GEMM_RST_SMALL
-#define DIAL_B200_GEMM_RST_SMALL 8
-#endif
-#ifndef DIAL_B200_GEMM_BST_SMALL
-#define DIAL_B200_GEMM_BST_SMALL 12
-#endif
-#ifndef DIAL_B200_GEMM_AST_SMALL
-#define DIAL_B200_GEMM_AST_SMALL 4
-#endif
-constexpr int kRstSmall = DIAL_B200_GEMM_RST_SMALL, kBstSmall = DIAL_B200_GEMM_BST_SMALL,
-              kAstSmall = DIAL_B200_GEMM_AST_SMALL;
-
 template <int BM_, int BN_, int BK_ = 64>
 struct Cfg {
   static constexpr int BM = BM_;  // weight rows per CTA
@@ -61,23 +47,29 @@ struct Cfg {
   static constexpr int BK = BK_;  // K per ring stage
   static constexpr int NATOM = BK / 64;
   static constexpr int CHUNK = BK == 128 ? 1152 : 1024;  // bytes per 16-row weight chunk
-  // Three rings: weight bytes (RSTAGES, freed by the dequant warps once the
-  // bytes are in their registers), activation tiles (BSTAGES, freed by the
-  // MMAs) and dequantized weights (ASTAGES, freed by the MMAs).  The weight
-  // stream is thus not held back by MMA completion: with few token rows it
-  // keeps up to RSTAGES stages of weight bytes in flight per CTA.
-  // (64-token tiles: the activation ring is the deep one, since each of its
-  // loads is an L2 round trip issued only after the MMAs of its slot's
-  // previous tile completed)
-  static constexpr int RSTAGES = BM == 256 ? 4 : BK == 128 ? 6 : BN <= 64 ? kRstSmall : 8;
-  static constexpr int BSTAGES = (BM == 256 || BK == 128) ? 3 : BN <= 64 ? kBstSmall : 4;
-  static constexpr int ASTAGES =  // dequantized-weight ring
-      (BM == 256 || BK == 128) ? 2 : BN <= 64 ? kAstSmall : 4;
+  // Three rings: weight bytes (RSTAGES stages of RK k-steps, one bulk copy of
+  // RK contiguous chunks per 16-row tile; freed by the dequant warps), the
+  // activation tiles (BSTAGES, 2-D TMA, freed by the MMAs) and the dequantized
+  // weights (ASTAGES, freed by the MMAs).  Every bulk copy, TMA and tcgen05
+  // instruction costs its issuing thread about 70-80 cycles (measured with
+  // clock64 around them), so the per-k-step issue work is spread out: RK
+  // k-steps per copy, two weight-producer threads for 256-row tiles, and two
+  // MMA threads for 128-row tiles (even / odd k-steps into two accumulators,
+  // added in the epilogue).
+  static constexpr int RK = (BM == 128 && BK == 64) ? 4 : 2;
+  static constexpr bool MMA2 = BM == 128;
+  static constexpr int NPROD = BM == 256 ? 2 : 1;
+  static constexpr int THREADS = MMA2 ? 416 : 384;
+  static constexpr int RSTAGES = BM == 256 ? 2 : BK == 128 ? 3 : BN <= 64 ? 3 : 2;
+  static constexpr int BSTAGES = BM == 256 ? 3 : BK == 128 ? 2 : BN <= 64 ? 6 : 4;
+  static constexpr int ASTAGES = (BM == 256 || BK == 128) ? 2 : 4;  // dequantized-weight ring
+  static_assert(!MMA2 || (BSTAGES % 2 == 0 && ASTAGES % 2 == 0),
+                "two MMA threads own alternate ring slots");
   static constexpr int A_HALF = 128 * BK * 2;  // one 128-row MMA operand
   static constexpr int A_BYTES = BM * BK * 2;
   static constexpr int B_ATOM = BN * 128;
   static constexpr int B_BYTES = BN * BK * 2;
-  static constexpr int RAW_BYTES = (BM / 16) * CHUNK;
+  static constexpr int RAW_BYTES = (BM / 16) * CHUNK * RK;
   static constexpr int OFF_A = 0;
   static constexpr int OFF_B = OFF_A + ASTAGES * A_BYTES;
   static constexpr int OFF_RAW = OFF_B + BSTAGES * B_BYTES;
@@ -88,7 +80,8 @@ struct Cfg {
       OFF_BAR + (2 * RSTAGES + 2 * BSTAGES + 2 * ASTAGES + 1) * 8;
   static constexpr int OFF_XEXP = OFF_TMEM + 16;
   static constexpr int SMEM_BYTES = OFF_XEXP + BN * 4 + 1024;  // + room to align to 1024
-  static constexpr int kTmemCols = (BM / 128) * BN;  // one BN-column accumulator per half
+  // one BN-column accumulator per 128-row half, or per MMA thread
+  static constexpr int kTmemCols = MMA2 ? 2 * BN : (BM / 128) * BN;
   // instruction descriptor: f32 accumulator, f16 A and B, both K-major, N = BN, M = 128
   static constexpr uint32_t kIdesc = (1u << 4) | (static_cast<uint32_t>(BN >> 3) << 17) |
                                      (static_cast<uint32_t>(128 >> 4) << 24);
@@ -292,7 +285,7 @@ __global__ void __launch_bounds__(256) prep_row_kernel(const GemmArgs a) {
 
 // ------------------------------------------------------------------ gemm
 template <typename Act, int FMT, int EPI, int BM_, int BN_, int BK_>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(Cfg<BM_, BN_, BK_>::THREADS, 1)
     w8a16_gemm_kernel(const __grid_constant__ CUtensorMap tmap, const GemmArgs a) {
   using AT = ActTraits<Act>;
   using G = Cfg<BM_, BN_, BK_>;
@@ -300,7 +293,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr int RST = G::RSTAGES, BST = G::BSTAGES;
   constexpr int CHUNK = G::CHUNK, NATOM = G::NATOM, B_ATOM = G::B_ATOM;
   constexpr int A_BYTES = G::A_BYTES, A_HALF = G::A_HALF, B_BYTES = G::B_BYTES;
-  constexpr int RAW_BYTES = G::RAW_BYTES, OFF_A = G::OFF_A, OFF_B = G::OFF_B;
+  constexpr int RAW_BYTES = G::RAW_BYTES, OFF_A = G::OFF_A, OFF_B = G::OFF_B, RK = G::RK;
+  constexpr bool MMA2 = G::MMA2;
+  constexpr int NPROD = G::NPROD;
   constexpr int OFF_RAW = G::OFF_RAW, OFF_BAR = G::OFF_BAR, OFF_TMEM = G::OFF_TMEM;
   constexpr int OFF_XEXP = G::OFF_XEXP, kTmemCols = G::kTmemCols;
   extern __shared__ uint8_t smem_raw[];
@@ -327,8 +322,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (tid == 0) {
     for (int s = 0; s < RST; ++s) {
-      mbar_init(&wfull[s], 1);
-      mbar_init(&wfree[s], a.couple ? 9 : 8);
+      mbar_init(&wfull[s], NPROD);
+      mbar_init(&wfree[s], 8 + (a.couple ? 1 : 0));
     }
     for (int s = 0; s < BST; ++s) {
       mbar_init(&bfull[s], 1);
@@ -338,7 +333,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&aready[s], 8);
       mbar_init(&afree[s], 1);
     }
-    mbar_init(accfull, 1);
+    mbar_init(accfull, MMA2 ? 2 : 1);
     fence_mbar_init();
   }
   if (warp == 2) {
@@ -356,27 +351,33 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 0) {
-    // ---------------------------------------------------- weight producer
+  if (warp == 0 || (NPROD == 2 && warp == 2)) {
+    // ------------------------------------------------- weight producer(s)
+    // producer p copies tiles [p T/NPROD, (p+1) T/NPROD) of the block; weight
+    // stage r holds k-steps [r RK, r RK + nk)
     if (lane == 0) {
+      constexpr int TPP = (BM / 16) / NPROD;  // 16-row tiles per producer
+      const int c0 = (warp == 0 ? 0 : 1) * TPP;
+      const int NR = (NK + RK - 1) / RK;
       int it = 0;
-      for (; it < NK; ++it) {
-        const int kb = KB0 + it, s = it % RST;
+      for (; it < NR; ++it) {
+        const int kb = KB0 + it * RK, s = it % RST, nk = min(RK, NK - it * RK);
         if (it >= RST &&
-            !mbar_wait(&wfree[s], static_cast<uint32_t>(it / RST - 1) & 1u, a.status,
+            !mbar_wait_sleep(&wfree[s], static_cast<uint32_t>(it / RST - 1) & 1u, a.status,
                        kStatusGemmWait))
           break;
-        mbar_arrive_expect_tx(&wfull[s], RAW_BYTES);
+        mbar_arrive_expect_tx(&wfull[s], static_cast<uint32_t>(TPP * nk * CHUNK));
         uint8_t* raw = smem + OFF_RAW + s * RAW_BYTES;
 #pragma unroll
-        for (int c = 0; c < BM / 16; ++c) {
+        for (int c = c0; c < c0 + TPP; ++c) {
           const size_t t = static_cast<size_t>(blk) * (BM / 16) + c;
-          bulk_g2s(raw + c * CHUNK, a.w.tiles + (t * C + kb) * CHUNK, CHUNK, &wfull[s]);
+          bulk_g2s(raw + c * RK * CHUNK, a.w.tiles + (t * C + kb) * CHUNK,
+                   static_cast<uint32_t>(nk * CHUNK), &wfull[s]);
         }
       }
       // every copy issued must land before the CTA retires
       for (int j = it > RST ? it - RST : 0; j < it; ++j)
-        if (!mbar_wait(&wfull[j % RST], static_cast<uint32_t>(j / RST) & 1u, a.status,
+        if (!mbar_wait_sleep(&wfull[j % RST], static_cast<uint32_t>(j / RST) & 1u, a.status,
                        kStatusGemmWait))
           break;
     }
@@ -387,7 +388,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (; it < NK; ++it) {
         const int kb = KB0 + it, s = it % BST;
         if (it >= BST &&
-            !mbar_wait(&bfree[s], static_cast<uint32_t>(it / BST - 1) & 1u, a.status,
+            !mbar_wait_sleep(&bfree[s], static_cast<uint32_t>(it / BST - 1) & 1u, a.status,
                        kStatusGemmWait))
           break;
         mbar_arrive_expect_tx(&bfull[s], B_BYTES);
@@ -397,19 +398,23 @@ __global__ void __launch_bounds__(kThreads, 1)
                       &bfull[s]);
       }
       for (int j = it > BST ? it - BST : 0; j < it; ++j)
-        if (!mbar_wait(&bfull[j % BST], static_cast<uint32_t>(j / BST) & 1u, a.status,
+        if (!mbar_wait_sleep(&bfull[j % BST], static_cast<uint32_t>(j / BST) & 1u, a.status,
                        kStatusGemmWait))
           break;
     }
-  } else if (warp == 1) {
-    // ---------------------------------------------------------------- MMA
+  } else if (warp == 1 || (MMA2 && warp == 12)) {
+    // -------------------------------------------------------------- MMA
+    // MMA2: thread `par` takes k-steps par, par + 2, ... into accumulator par
     if (lane == 0) {
-      for (int it = 0; it < NK; ++it) {
+      constexpr int STEP = MMA2 ? 2 : 1;
+      const int par = warp == 1 ? 0 : 1;
+      const uint32_t tacc = tmem + (MMA2 ? static_cast<uint32_t>(par * BN) : 0u);
+      for (int it = par; it < NK; it += STEP) {
         const int s = it % BST, sa_i = it % ASTAGES;
-        if (!mbar_wait(&aready[sa_i], static_cast<uint32_t>(it / ASTAGES) & 1u, a.status,
+        if (!mbar_wait_sleep(&aready[sa_i], static_cast<uint32_t>(it / ASTAGES) & 1u, a.status,
                        kStatusGemmWait))
           break;
-        if (!mbar_wait(&bfull[s], static_cast<uint32_t>(it / BST) & 1u, a.status,
+        if (!mbar_wait_sleep(&bfull[s], static_cast<uint32_t>(it / BST) & 1u, a.status,
                        kStatusGemmWait))
           break;
         tc_fence_after();
@@ -417,20 +422,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t sb = smem_u32(smem + OFF_B + s * B_BYTES);
 #pragma unroll
         for (int k16 = 0; k16 < BK / 16; ++k16) {
-          const uint32_t acc = (it | k16) != 0 ? 1u : 0u;
+          const uint32_t acc = (it != par || k16 != 0) ? 1u : 0u;
           const uint32_t ka = (k16 >> 2) * 16384 + (k16 & 3) * 32;  // atom, 16-col step
           const uint64_t db = sw128_desc(sb + (k16 >> 2) * B_ATOM + (k16 & 3) * 32);
-          tc_mma(tmem, sw128_desc(sa + ka), db, G::kIdesc, acc);  // rows 0..127
+          tc_mma(tacc, sw128_desc(sa + ka), db, G::kIdesc, acc);  // rows 0..127
           if constexpr (BM == 256)  // rows 128..255 into the second accumulator
             tc_mma(tmem + BN, sw128_desc(sa + A_HALF + ka), db, G::kIdesc, acc);
         }
         tc_commit(&afree[sa_i]);
         tc_commit(&bfree[s]);
-        if (a.couple) tc_commit(&wfree[it % RST]);
+        if (a.couple && (it % RK == RK - 1 || it == NK - 1)) tc_commit(&wfree[(it / RK) % RST]);
       }
       tc_commit(accfull);
-      // the accumulator (and TMEM) stays in use until every MMA has finished
-      mbar_wait(accfull, 0, a.status, kStatusGemmWait);
+      // the accumulators (and TMEM) stay in use until every MMA has finished
+      mbar_wait_sleep(accfull, 0, a.status, kStatusGemmWait);
     }
   } else if (warp >= 4) {
     // ------------------------------------------------------------ dequant
@@ -443,18 +448,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int r = dt >> 1, part = dt & 1;
       const int c = r >> 4, rr = r & 15;
       for (int it = 0; it < NK; ++it) {
-        const int s = it % RST, sa_i = it % ASTAGES;
-        if (!mbar_wait(&wfull[s], static_cast<uint32_t>(it / RST) & 1u, a.status,
+        const int rs = it / RK, s = rs % RST, sa_i = it % ASTAGES;
+        if (!mbar_wait_sleep(&wfull[s], static_cast<uint32_t>(rs / RST) & 1u, a.status,
                        kStatusGemmWait))
           break;
-        const uint8_t* ch = smem + OFF_RAW + s * RAW_BYTES + c * CHUNK;
+        const uint8_t* ch = smem + OFF_RAW + s * RAW_BYTES + (c * RK + it % RK) * CHUNK;
         const uint4 n0 = *reinterpret_cast<const uint4*>(ch + rr * 64 + part * 32);
         const uint4 n1 = *reinterpret_cast<const uint4*>(ch + rr * 64 + part * 32 + 16);
         const uint32_t scw = *reinterpret_cast<const uint32_t*>(ch + 1024 + rr * 8 + part * 4);
         __syncwarp();
-        if (lane == 0) mbar_arrive(&wfree[s]);
+        // the weight stage is free once its last k-step's bytes are in registers
+        if (lane == 0 && (it % RK == RK - 1 || it == NK - 1)) mbar_arrive(&wfree[s]);
         if (it >= ASTAGES &&
-            !mbar_wait(&afree[sa_i], static_cast<uint32_t>(it / ASTAGES - 1) & 1u, a.status,
+            !mbar_wait_sleep(&afree[sa_i], static_cast<uint32_t>(it / ASTAGES - 1) & 1u, a.status,
                        kStatusGemmWait))
           break;
         const uint32_t s01 = e4m3x2_to_f16x2(static_cast<uint16_t>(scw & 0xffffu));
@@ -501,21 +507,22 @@ __global__ void __launch_bounds__(kThreads, 1)
       bsc_row = a.w.blk_scale + static_cast<size_t>(orig / 128) * a.w.blk_ld;
     }
     for (int it = 0; it < NK; ++it) {
-      const int kb = KB0 + it, s = it % RST, sa_i = it % ASTAGES;
+      const int kb = KB0 + it, rs = it / RK, s = rs % RST, sa_i = it % ASTAGES;
       float bscale = 1.f;
       if constexpr (FMT == kFmtFp8Block128) bscale = __ldg(bsc_row + (kb >> 1));
-      if (!mbar_wait(&wfull[s], static_cast<uint32_t>(it / RST) & 1u, a.status,
+      if (!mbar_wait_sleep(&wfull[s], static_cast<uint32_t>(rs / RST) & 1u, a.status,
                      kStatusGemmWait))
         break;
-      const uint4* src = reinterpret_cast<const uint4*>(smem + OFF_RAW + s * RAW_BYTES +
-                                                        c * CHUNK + row * 64 + part * BPT);
+      const uint4* src = reinterpret_cast<const uint4*>(
+          smem + OFF_RAW + s * RAW_BYTES + (c * RK + it % RK) * CHUNK + row * 64 + part * BPT);
       uint4 wv[NV];
 #pragma unroll
       for (int i = 0; i < NV; ++i) wv[i] = src[i];
       __syncwarp();
-      if (lane == 0) mbar_arrive(&wfree[s]);  // raw bytes are in registers
+      // raw bytes are in registers; the weight stage is free after its last k-step
+      if (lane == 0 && (it % RK == RK - 1 || it == NK - 1)) mbar_arrive(&wfree[s]);
       if (it >= ASTAGES &&
-          !mbar_wait(&afree[sa_i], static_cast<uint32_t>(it / ASTAGES - 1) & 1u, a.status,
+          !mbar_wait_sleep(&afree[sa_i], static_cast<uint32_t>(it / ASTAGES - 1) & 1u, a.status,
                      kStatusGemmWait))
         break;
       uint8_t* arow = smem + OFF_A + sa_i * A_BYTES + h * A_HALF + (rh >> 3) * 1024 + (rh & 7) * 128;
@@ -558,7 +565,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---------------------------------------------------------- epilogue
     // the whole warp takes the same branch (tcgen05.ld is warp-collective)
     const bool acc_ok =
-        __all_sync(0xffffffffu, mbar_wait(accfull, 0, a.status, kStatusGemmWait));
+        __all_sync(0xffffffffu, mbar_wait_sleep(accfull, 0, a.status, kStatusGemmWait));
     const int hh = (warp - 4) >> 2;  // accumulator half (rows 0-127 or 128-255)
     if (acc_ok && hh < BM / 128) {
       tc_fence_after();
@@ -572,6 +579,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int cb = 0; cb < BN / 16; ++cb) {
         uint32_t v[16];
         tmem_ld16(tmem + (static_cast<uint32_t>(32 * q) << 16) + hh * BN + cb * 16, v);
+        if constexpr (MMA2) {
+          // the odd k-steps' accumulator (none when the split has one k-step)
+          if (NK > 1) {
+            uint32_t v2[16];
+            tmem_ld16(tmem + (static_cast<uint32_t>(32 * q) << 16) + BN + cb * 16, v2);
+#pragma unroll
+            for (int jj = 0; jj < 16; ++jj)
+              v[jj] = __float_as_uint(__uint_as_float(v[jj]) + __uint_as_float(v2[jj]));
+          }
+        }
 #pragma unroll
         for (int jj = 0; jj < 16; ++jj) {
           const int tk = cb * 16 + jj, tok = tok0 + tk;
@@ -633,7 +650,7 @@ cudaError_t launch_gemm(const CUtensorMap& map, const GemmArgs& a, cudaStream_t 
       cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, G::SMEM_BYTES);
   if (e != cudaSuccess) return e;
   const dim3 grid((a.M + BN - 1) / BN, a.w.T / (BM / 16), ks);
-  kern<<<grid, kThreads, G::SMEM_BYTES, s>>>(map, a);
+  kern<<<grid, G::THREADS, G::SMEM_BYTES, s>>>(map, a);
   return cudaGetLastError();
 }
 
