@@ -56,12 +56,14 @@ struct Cfg {
   // k-steps per copy, two weight-producer threads for 256-row tiles, and two
   // MMA threads for 128-row tiles (even / odd k-steps into two accumulators,
   // added in the epilogue).
-  static constexpr int RK = (BM == 128 && BK == 64) ? 4 : 2;
+  static constexpr int RK = (BM == 128 && BK == 64) ? 4 : BM == 256 ? 1 : 2;
   static constexpr bool MMA2 = BM == 128;
   static constexpr int NPROD = BM == 256 ? 2 : 1;
-  static constexpr int THREADS = MMA2 ? 416 : 384;
+  // dequant warps: 8, or 16 for 256-row tiles (twice the bytes per k-step)
+  static constexpr int DQW = BM == 256 ? 16 : 8;
+  static constexpr int THREADS = 128 + 32 * DQW + (MMA2 ? 32 : 0);
   static constexpr int RSTAGES = BM == 256 ? 2 : BK == 128 ? 3 : BN <= 64 ? 3 : 2;
-  static constexpr int BSTAGES = BM == 256 ? 3 : BK == 128 ? 2 : BN <= 64 ? 6 : 4;
+  static constexpr int BSTAGES = BM == 256 ? 4 : BK == 128 ? 2 : BN <= 64 ? 6 : 4;
   static constexpr int ASTAGES = (BM == 256 || BK == 128) ? 2 : 4;  // dequantized-weight ring
   static_assert(!MMA2 || (BSTAGES % 2 == 0 && ASTAGES % 2 == 0),
                 "two MMA threads own alternate ring slots");
@@ -323,14 +325,14 @@ __global__ void __launch_bounds__(Cfg<BM_, BN_, BK_>::THREADS, 1)
   if (tid == 0) {
     for (int s = 0; s < RST; ++s) {
       mbar_init(&wfull[s], NPROD);
-      mbar_init(&wfree[s], 8 + (a.couple ? 1 : 0));
+      mbar_init(&wfree[s], G::DQW + (a.couple ? 1 : 0));
     }
     for (int s = 0; s < BST; ++s) {
       mbar_init(&bfull[s], 1);
       mbar_init(&bfree[s], 1);
     }
     for (int s = 0; s < ASTAGES; ++s) {
-      mbar_init(&aready[s], 8);
+      mbar_init(&aready[s], G::DQW);
       mbar_init(&afree[s], 1);
     }
     mbar_init(accfull, MMA2 ? 2 : 1);
@@ -402,7 +404,7 @@ __global__ void __launch_bounds__(Cfg<BM_, BN_, BK_>::THREADS, 1)
                        kStatusGemmWait))
           break;
     }
-  } else if (warp == 1 || (MMA2 && warp == 12)) {
+  } else if (warp == 1 || (MMA2 && warp == 4 + G::DQW)) {
     // -------------------------------------------------------------- MMA
     // MMA2: thread `par` takes k-steps par, par + 2, ... into accumulator par
     if (lane == 0) {
@@ -456,9 +458,14 @@ __global__ void __launch_bounds__(Cfg<BM_, BN_, BK_>::THREADS, 1)
         const uint4 n0 = *reinterpret_cast<const uint4*>(ch + rr * 64 + part * 32);
         const uint4 n1 = *reinterpret_cast<const uint4*>(ch + rr * 64 + part * 32 + 16);
         const uint32_t scw = *reinterpret_cast<const uint32_t*>(ch + 1024 + rr * 8 + part * 4);
-        __syncwarp();
-        // the weight stage is free once its last k-step's bytes are in registers
-        if (lane == 0 && (it % RK == RK - 1 || it == NK - 1)) mbar_arrive(&wfree[s]);
+        // the weight stage is free once its last k-step's bytes are in registers;
+        // the proxy fence orders these generic reads before the bulk copy that
+        // refills the slot (an async-proxy write)
+        if (it % RK == RK - 1 || it == NK - 1) {
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&wfree[s]);
+        }
         if (it >= ASTAGES &&
             !mbar_wait_sleep(&afree[sa_i], static_cast<uint32_t>(it / ASTAGES - 1) & 1u, a.status,
                        kStatusGemmWait))
@@ -490,7 +497,7 @@ __global__ void __launch_bounds__(Cfg<BM_, BN_, BK_>::THREADS, 1)
       }
     } else {
     // thread dt converts BPT bytes: part `part` of row `row` of 16-row chunk c
-    constexpr int BPT = BM / 4;        // 64 (BM 256) or 32 (BM 128) bytes
+    constexpr int BPT = BM * 64 / (32 * G::DQW);  // 32 bytes
     constexpr int TPR = 64 / BPT;      // threads per 64-byte row
     constexpr int NV = BPT / 16;       // 16-byte loads per thread
     const int dt = tid - 128;
@@ -518,9 +525,14 @@ __global__ void __launch_bounds__(Cfg<BM_, BN_, BK_>::THREADS, 1)
       uint4 wv[NV];
 #pragma unroll
       for (int i = 0; i < NV; ++i) wv[i] = src[i];
-      __syncwarp();
-      // raw bytes are in registers; the weight stage is free after its last k-step
-      if (lane == 0 && (it % RK == RK - 1 || it == NK - 1)) mbar_arrive(&wfree[s]);
+      // raw bytes are in registers; the weight stage is free after its last
+      // k-step, once the proxy fence orders these generic reads before the
+      // bulk copy that refills the slot (an async-proxy write)
+      if (it % RK == RK - 1 || it == NK - 1) {
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&wfree[s]);
+      }
       if (it >= ASTAGES &&
           !mbar_wait_sleep(&afree[sa_i], static_cast<uint32_t>(it / ASTAGES - 1) & 1u, a.status,
                      kStatusGemmWait))
@@ -830,7 +842,10 @@ cudaError_t gemm_w8a16_launch(const GemmArgs& a, int act, int epi, cudaStream_t 
   EncodeTiledFn enc = encode_fn();
   if (!enc) return cudaErrorNotSupported;
   GemmArgs a2 = a;
-  a2.couple = 1;
+  // weight slots are released once the dequant warps hold the bytes and have
+  // fenced their reads against the refill (DIAL_B200_GEMM_COUPLE=1: also wait
+  // for the k-step's MMAs)
+  a2.couple = 0;
   if (const char* v = std::getenv("DIAL_B200_GEMM_COUPLE")) a2.couple = std::atoi(v);
   CUtensorMap map;
   const cuuint64_t dims[2] = {static_cast<cuuint64_t>(a.w.K_pad), static_cast<cuuint64_t>(a.M)};
