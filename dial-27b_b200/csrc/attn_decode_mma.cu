@@ -71,10 +71,6 @@ __device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t (&r)[4]) {
                : "r"(addr));
 }
 
-__device__ __forceinline__ void fence_proxy_async_smem() {
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
-
 // D(rows 0-7) += A(rows 0-7) . B for m16n8k16 with rows 8-15 of A zero:
 // only c0 / c1 (row g) are kept; rows 8-15 of D go to dead registers.
 template <typename Act>
@@ -303,6 +299,8 @@ __global__ void __launch_bounds__(kMW * 32, mma_min_ctas<RING>()) attn_decode_mm
       mma_rows8<Act>(o[2 * db + 1][0], o[2 * db + 1][1], h0, h1, b[2], b[3]);
       mma_rows8<Act>(o[2 * db + 1][0], o[2 * db + 1][1], l0, l1, b[2], b[3]);
     }
+    // the slot's ldmatrix reads before the TMA that refills it
+    fence_proxy_async_smem();
     __syncwarp();
     if (issued < mine) issue(issued++);
   }

@@ -472,6 +472,7 @@ __device__ void attn_item(const AttnDecodeArgs& a, int m, int kvh, int split, in
           kr[j] = *reinterpret_cast<const uint2*>(kp + j * kHeadDim * 2 + lane * 8);
           vr[j] = *reinterpret_cast<const uint2*>(vp + j * kHeadDim * 2 + lane * 8);
         }
+        fence_proxy_async_smem();  // these reads before the copy that refills the slot
         __syncwarp();
         if (lane == 0) mbar_arrive(&rempty[slot]);
       } else if (b0 != tok0) {

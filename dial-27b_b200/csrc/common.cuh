@@ -140,6 +140,13 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* s
   }
 }
 
+// Orders this thread's generic shared-memory accesses before later
+// async-proxy ones (a bulk or TMA copy that refills a ring slot the thread
+// has just read, or an MMA that reads what it has just written).
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
 // ------------------------------------------------------ bulk async copies
 // 1-D global -> shared copy on the TMA engine, completing on an mbarrier.
 // Both addresses 16-byte aligned, size a multiple of 16.

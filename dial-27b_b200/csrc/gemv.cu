@@ -356,6 +356,8 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1)
           }
         }
       }
+      // this warp's reads of the stage before the bulk copy that refills it
+      fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[slot]);
       if (++slot == NS) {
