@@ -107,14 +107,50 @@ __device__ __forceinline__ void ld16(uint32_t taddr, uint32_t (&v)[16]) {
       : "r"(taddr));
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
-__device__ __forceinline__ void st16(uint32_t taddr, const uint32_t (&v)[16]) {
+// tcgen05.ld of 16 columns without the wait: several loads share one wait
+__device__ __forceinline__ void ld16_async(uint32_t taddr, uint32_t* v) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+      "%11, %12, %13, %14, %15}, [%16];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
+        "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]),
+        "=r"(v[14]), "=r"(v[15])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void ld_wait() {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+// (lo, hi) f32 -> bf16x2, round to nearest even
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+// bf16x2 product, rounded once to bf16: the exact product of two bf16 values
+// fits an f32, so this equals round(round(a) * b) formed in f32
+__device__ __forceinline__ uint32_t mul_bf16x2(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+__device__ __forceinline__ uint32_t max_bf16x2(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("max.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+__device__ __forceinline__ float ex2_approx(float x) {
+  float r;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
+
+__device__ __forceinline__ void st16_async(uint32_t taddr, const uint32_t* v) {
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
       "%11, %12, %13, %14, %15, %16};" ::"r"(taddr),
       "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
       "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]),
       "r"(v[15]));
-  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
 // ------------------------------------------------------------ q rotation
@@ -304,6 +340,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int qi = q0 + r;
     const int qpos = a.p0 + qi;
     const float scale = AT::round(1.0f / sqrtf(static_cast<float>(kHeadDim)));
+    const uint32_t scale2 = pack_bf16x2(scale, scale);
+    constexpr uint32_t kBf16NegInf = 0xFF80u;
+    constexpr float kLog2e = 1.4426950408889634f;
     const uint32_t lane_off = static_cast<uint32_t>(32 * quarter) << 16;
     float* xch = reinterpret_cast<float*>(smem + OFF_XCH);  // [parity][half][row]
     auto pair_sync = [&]() { named_bar_sync(1 + quarter, 64); };
@@ -320,21 +359,40 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       fence_after();
       constexpr int KH = kKB / 2;  // keys of this half
-      float s[KH];
+      // scores of this row's half block as bf16 pairs (key 2i low, 2i+1 high)
+      uint32_t sp[KH / 2];
+      {
+        uint32_t v[KH];
 #pragma unroll
-      for (int cb = 0; cb < KH / 16; ++cb) {
-        uint32_t v[16];
-        ld16(tmem + static_cast<uint32_t>(j & 1) * 128 + lane_off + half * KH + cb * 16, v);
+        for (int cb = 0; cb < KH / 16; ++cb)
+          ld16_async(tmem + static_cast<uint32_t>(j & 1) * 128 + lane_off + half * KH + cb * 16,
+                     v + cb * 16);
+        ld_wait();
+        const int kbase = j * kKB + half * KH;
+        // every key of this half block visible to every row of the warp
+        const bool open = kbase + KH - 1 <= a.p0 + q0 + quarter * 32 &&
+                          q0 + quarter * 32 + 32 <= a.M;
+        if (open) {
 #pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          const int kpos = j * kKB + half * KH + cb * 16 + e;
-          const float sc = AT::round(AT::round(__uint_as_float(v[e])) * scale);
-          s[cb * 16 + e] = (kpos <= qpos && qi < a.M) ? sc : -INFINITY;
+          for (int i = 0; i < KH / 2; ++i)
+            sp[i] = mul_bf16x2(pack_bf16x2(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1])),
+                               scale2);
+        } else {
+#pragma unroll
+          for (int i = 0; i < KH / 2; ++i) {
+            const uint32_t b = mul_bf16x2(
+                pack_bf16x2(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1])), scale2);
+            const bool row_ok = qi < a.M;
+            const uint32_t lo = (row_ok && kbase + 2 * i <= qpos) ? (b & 0xFFFFu) : kBf16NegInf;
+            const uint32_t hi = (row_ok && kbase + 2 * i + 1 <= qpos) ? (b >> 16) : kBf16NegInf;
+            sp[i] = lo | (hi << 16);
+          }
         }
       }
-      float bm = -INFINITY;
+      uint32_t bm2 = sp[0];
 #pragma unroll
-      for (int i = 0; i < KH; ++i) bm = fmaxf(bm, s[i]);
+      for (int i = 1; i < KH / 2; ++i) bm2 = max_bf16x2(bm2, sp[i]);
+      float bm = fmaxf(__uint_as_float(bm2 << 16), __uint_as_float(bm2 & 0xFFFF0000u));
       // the row's block max: exchange with the other half (buffers by block
       // parity: a warp cannot be two blocks ahead of its partner)
       float* xj = xch + (j & 1) * 256;
@@ -343,15 +401,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       ++exchanged;
       bm = fmaxf(bm, xj[(half ^ 1) * 128 + r]);
       const float m_new = fmaxf(m_run, bm);
-      // exponentials through the hardware exp2 (__expf): its relative error
-      // (about 1e-6 here) is far below the bf16 rounding P receives
+      // exponentials through the hardware exp2: its relative error (about
+      // 1e-6 here) is far below the bf16 rounding P receives
       const float alpha = (m_run == -INFINITY) ? 0.f : __expf(m_run - m_new);
+      // p = 2^(s log2 e - m log2 e); a fully masked row (m = -inf) gets p = 0
+      const float mb = (m_new == -INFINITY) ? 0.f : m_new * kLog2e;
       float psum = 0.f;
+      uint32_t pp[KH / 2];
 #pragma unroll
-      for (int i = 0; i < KH; ++i) {
-        const float p = (m_new == -INFINITY) ? 0.f : __expf(s[i] - m_new);
-        s[i] = p;
-        psum += p;
+      for (int i = 0; i < KH / 2; ++i) {
+        const float p0 = ex2_approx(fmaf(__uint_as_float(sp[i] << 16), kLog2e, -mb));
+        const float p1 = ex2_approx(fmaf(__uint_as_float(sp[i] & 0xFFFF0000u), kLog2e, -mb));
+        psum += p0 + p1;
+        pp[i] = pack_bf16x2(p0, p1);
       }
       l_run = l_run * alpha + psum;
       m_run = m_new;
@@ -368,27 +430,24 @@ __global__ void __launch_bounds__(kThreads, 1)
         // tcgen05.ld/st are warp-collective (.sync.aligned): the whole warp
         // rescales its 32 rows, or none does when no row's max moved (alpha 1)
         if (__any_sync(0xffffffffu, alpha != 1.f)) {
+          uint32_t v[kHeadDim / 2];  // this half's 64 dims: four loads, one wait
+          const uint32_t col = tO + lane_off + half * (kHeadDim / 2);
 #pragma unroll
-          for (int cb = 0; cb < kHeadDim / 32; ++cb) {  // this half's 64 dims
-            uint32_t v[16];
-            const uint32_t col = tO + lane_off + half * (kHeadDim / 2) + cb * 16;
-            ld16(col, v);
+          for (int cb = 0; cb < kHeadDim / 32; ++cb) ld16_async(col + cb * 16, v + cb * 16);
+          ld_wait();
 #pragma unroll
-            for (int e = 0; e < 16; ++e) v[e] = __float_as_uint(__uint_as_float(v[e]) * alpha);
-            st16(col, v);
-          }
+          for (int e = 0; e < kHeadDim / 2; ++e) v[e] = __float_as_uint(__uint_as_float(v[e]) * alpha);
+#pragma unroll
+          for (int cb = 0; cb < kHeadDim / 32; ++cb) st16_async(col + cb * 16, v + cb * 16);
+          asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
         }
       }
       // P row r as bf16 into the K-major swizzled tile: 16-byte chunk c holds keys 8c..8c+7
       uint8_t* prow = smem + OFF_P + (r >> 3) * 1024 + (r & 7) * 128;
 #pragma unroll
-      for (int jj = 0; jj < KH / 8; ++jj) {  // this half's 8 chunks of 8 keys
-        uint4 o;
-        __nv_bfloat16* hv = reinterpret_cast<__nv_bfloat16*>(&o);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) hv[e] = __float2bfloat16_rn(s[jj * 8 + e]);
-        *reinterpret_cast<uint4*>(prow + half * HALF + ((jj ^ (r & 7)) << 4)) = o;
-      }
+      for (int jj = 0; jj < KH / 8; ++jj)  // this half's 8 chunks of 8 keys
+        *reinterpret_cast<uint4*>(prow + half * HALF + ((jj ^ (r & 7)) << 4)) =
+            make_uint4(pp[4 * jj], pp[4 * jj + 1], pp[4 * jj + 2], pp[4 * jj + 3]);
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       fence_before();
       mbar_arrive(pready);

@@ -579,50 +579,123 @@ __global__ void __launch_bounds__(Cfg<BM_, BN_, BK_>::THREADS, 1)
     const bool acc_ok =
         __all_sync(0xffffffffu, mbar_wait_sleep(accfull, 0, a.status, kStatusGemmWait));
     const int hh = (warp - 4) >> 2;  // accumulator half (rows 0-127 or 128-255)
-    if (acc_ok && hh < BM / 128) {
-      tc_fence_after();
+    // Output columns of this block: BM rows, or BM / 2 SwiGLU columns.
+    constexpr int OW = EPI == kEpiSwiglu ? BM / 2 : BM;
+    const int col0 = blk * OW;
+    const int ntok = min(BN, a.M - tok0);
+    // Staged epilogue (residual and SwiGLU): the block's output tile
+    // [ntok][OW] is assembled in the activation ring (idle once every MMA has
+    // finished: each of its TMA loads was consumed by an MMA), so that the
+    // residual is read and the output written with coalesced 16-byte accesses
+    // instead of one dependent 2-byte access per thread and token.  Plain
+    // stores measured faster written directly (no barrier, nothing to wait for).
+    const bool staged = (EPI == kEpiResidual || EPI == kEpiSwiglu) && (a.out_ld % 8) == 0 &&
+                        (reinterpret_cast<uintptr_t>(a.out) & 15) == 0 &&
+                        col0 + OW <= (EPI == kEpiSwiglu ? a.w.N / 2 : a.w.N);
+    static_assert(OW <= BST * BK, "output tile must fit the activation ring");
+    if (hh < BM / 128) {
       const int q = warp & 3;          // TMEM lane quarter this warp may read
       const int rr = hh * 128 + 32 * q + lane;  // row of the block
       float rs = a.w.row_scale ? a.w.row_scale[static_cast<size_t>(blk) * BM + rr] : 1.f;
       if constexpr (FMT == kFmtNvfp4G16) rs *= a.w.global_scale;
       const int n = blk * BM + rr;
       const int tr = rr & 15;  // row inside the 16-row tile
-      const int jcol = (blk * (BM / 16) + (rr >> 4)) * 8 + (tr & 7);  // SwiGLU output column
-      for (int cb = 0; cb < BN / 16; ++cb) {
-        uint32_t v[16];
-        tmem_ld16(tmem + (static_cast<uint32_t>(32 * q) << 16) + hh * BN + cb * 16, v);
-        if constexpr (MMA2) {
-          // the odd k-steps' accumulator (none when the split has one k-step)
-          if (NK > 1) {
-            uint32_t v2[16];
-            tmem_ld16(tmem + (static_cast<uint32_t>(32 * q) << 16) + BN + cb * 16, v2);
-#pragma unroll
-            for (int jj = 0; jj < 16; ++jj)
-              v[jj] = __float_as_uint(__uint_as_float(v[jj]) + __uint_as_float(v2[jj]));
-          }
+      // SwiGLU output column (the fused gate/up tile holds gate rows 8t.. in
+      // rows 0-7 and up rows in 8-15)
+      const int jl = (rr >> 4) * 8 + (tr & 7);
+      const int jcol = col0 + jl;
+      Act* T = reinterpret_cast<Act*>(smem + OFF_B);  // [BN][OW] when staged
+      constexpr int VPR = OW / 8;                      // 16-byte vectors per token row
+      const int et = tid - 128;                        // 0 .. BM-1
+      if (staged && EPI == kEpiResidual) {
+#pragma unroll 8
+        for (int i = et; i < ntok * VPR; i += BM) {
+          const int tk = i / VPR, v = i % VPR;
+          reinterpret_cast<uint4*>(T + tk * OW)[v] = *reinterpret_cast<const uint4*>(
+              reinterpret_cast<const Act*>(a.out) + static_cast<size_t>(tok0 + tk) * a.out_ld +
+              col0 + v * 8);
         }
+      }
+      if (staged) named_bar_sync(1, BM);
+      if (acc_ok) {
+        tc_fence_after();
+        for (int cb = 0; cb < BN / 16; ++cb) {
+          uint32_t v[16];
+          tmem_ld16(tmem + (static_cast<uint32_t>(32 * q) << 16) + hh * BN + cb * 16, v);
+          if constexpr (MMA2) {
+            // the odd k-steps' accumulator (none when the split has one k-step)
+            if (NK > 1) {
+              uint32_t v2[16];
+              tmem_ld16(tmem + (static_cast<uint32_t>(32 * q) << 16) + BN + cb * 16, v2);
 #pragma unroll
-        for (int jj = 0; jj < 16; ++jj) {
-          const int tk = cb * 16 + jj, tok = tok0 + tk;
-          if constexpr (EPI == kEpiPartial) {
-            // this split's scaled partial sum, rounded once the splits are added
-            if (tok < a.M && n < a.w.N)
-              a.part[(static_cast<size_t>(blockIdx.z) * a.M + tok) * a.w.N + n] =
-                  __uint_as_float(v[jj]) * (exp2i(sxexp[tk]) * rs);
-            continue;
-          }
-          const float y = AT::round(__uint_as_float(v[jj]) * (exp2i(sxexp[tk]) * rs));
-          if constexpr (EPI == kEpiSwiglu) {
-            const float yu = __shfl_down_sync(0xffffffffu, y, 8);
-            if (tr < 8 && tok < a.M && jcol < a.w.N / 2)
-              reinterpret_cast<Act*>(a.out)[static_cast<size_t>(tok) * a.out_ld + jcol] =
-                  AT::from_f(silu_mul_ref<Act>(y, yu));
-          } else {
-            if (tok < a.M && n < a.w.N) {
-              Act* o = reinterpret_cast<Act*>(a.out) + static_cast<size_t>(tok) * a.out_ld + n;
-              *o = EPI == kEpiResidual ? AT::from_f(y + AT::to_f(*o)) : AT::from_f(y);
+              for (int jj = 0; jj < 16; ++jj)
+                v[jj] = __float_as_uint(__uint_as_float(v[jj]) + __uint_as_float(v2[jj]));
             }
           }
+          if constexpr (EPI == kEpiPartial) {
+#pragma unroll
+            for (int jj = 0; jj < 16; ++jj) {
+              const int tk = cb * 16 + jj, tok = tok0 + tk;
+              // this split's scaled partial sum, rounded once the splits are added
+              if (tok < a.M && n < a.w.N)
+                a.part[(static_cast<size_t>(blockIdx.z) * a.M + tok) * a.w.N + n] =
+                    __uint_as_float(v[jj]) * (exp2i(sxexp[tk]) * rs);
+            }
+          } else if (staged) {
+            if constexpr (EPI == kEpiSwiglu) {
+              // tokens in pairs: the gate lane forms the even token's output,
+              // its up partner (lane ^ 8) the odd token's
+              const bool gate = tr < 8;
+#pragma unroll
+              for (int jj = 0; jj < 16; jj += 2) {
+                const int tk = cb * 16 + jj;
+                const float y0 = AT::round(__uint_as_float(v[jj]) * (exp2i(sxexp[tk]) * rs));
+                const float y1 =
+                    AT::round(__uint_as_float(v[jj + 1]) * (exp2i(sxexp[tk + 1]) * rs));
+                const float recv = __shfl_xor_sync(0xffffffffu, gate ? y1 : y0, 8);
+                const float g = gate ? y0 : recv, u = gate ? recv : y1;
+                const int tko = tk + (gate ? 0 : 1);
+                if (tko < ntok) T[tko * OW + jl] = AT::from_f(silu_mul_ref<Act>(g, u));
+              }
+            } else {
+#pragma unroll
+              for (int jj = 0; jj < 16; ++jj) {
+                const int tk = cb * 16 + jj;
+                if (tk < ntok) {
+                  const float y = AT::round(__uint_as_float(v[jj]) * (exp2i(sxexp[tk]) * rs));
+                  Act* t = T + tk * OW + rr;
+                  *t = EPI == kEpiResidual ? AT::from_f(y + AT::to_f(*t)) : AT::from_f(y);
+                }
+              }
+            }
+          } else {
+#pragma unroll
+            for (int jj = 0; jj < 16; ++jj) {
+              const int tk = cb * 16 + jj, tok = tok0 + tk;
+              const float y = AT::round(__uint_as_float(v[jj]) * (exp2i(sxexp[tk]) * rs));
+              if constexpr (EPI == kEpiSwiglu) {
+                const float yu = __shfl_down_sync(0xffffffffu, y, 8);
+                if (tr < 8 && tok < a.M && jcol < a.w.N / 2)
+                  reinterpret_cast<Act*>(a.out)[static_cast<size_t>(tok) * a.out_ld + jcol] =
+                      AT::from_f(silu_mul_ref<Act>(y, yu));
+              } else {
+                if (tok < a.M && n < a.w.N) {
+                  Act* o = reinterpret_cast<Act*>(a.out) + static_cast<size_t>(tok) * a.out_ld + n;
+                  *o = EPI == kEpiResidual ? AT::from_f(y + AT::to_f(*o)) : AT::from_f(y);
+                }
+              }
+            }
+          }
+        }
+      }
+      if (staged) {
+        named_bar_sync(1, BM);
+#pragma unroll 8
+        for (int i = et; i < ntok * VPR; i += BM) {
+          const int tk = i / VPR, v = i % VPR;
+          *reinterpret_cast<uint4*>(reinterpret_cast<Act*>(a.out) +
+                                    static_cast<size_t>(tok0 + tk) * a.out_ld + col0 + v * 8) =
+              reinterpret_cast<const uint4*>(T + tk * OW)[v];
         }
       }
     }
