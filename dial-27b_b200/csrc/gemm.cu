@@ -578,7 +578,12 @@ __global__ void __launch_bounds__(Cfg<BM_, BN_, BK_>::THREADS, 1)
     // the whole warp takes the same branch (tcgen05.ld is warp-collective)
     const bool acc_ok =
         __all_sync(0xffffffffu, mbar_wait_sleep(accfull, 0, a.status, kStatusGemmWait));
-    const int hh = (warp - 4) >> 2;  // accumulator half (rows 0-127 or 128-255)
+    // Every dequant warp takes part: warp 4 + ew reads TMEM lane quarter
+    // ew % 4 of accumulator half hh, for token part cp of NCP.
+    constexpr int NH = BM / 128, NCP = G::DQW / 4 / NH, EPT = G::DQW * 32;
+    static_assert(NCP >= 1 && (BN / 16) % NCP == 0, "epilogue token split");
+    const int ew = warp - 4;
+    const int hh = (ew >> 2) % NH, cp = (ew >> 2) / NH;
     // Output columns of this block: BM rows, or BM / 2 SwiGLU columns.
     constexpr int OW = EPI == kEpiSwiglu ? BM / 2 : BM;
     const int col0 = blk * OW;
@@ -593,7 +598,7 @@ __global__ void __launch_bounds__(Cfg<BM_, BN_, BK_>::THREADS, 1)
                         (reinterpret_cast<uintptr_t>(a.out) & 15) == 0 &&
                         col0 + OW <= (EPI == kEpiSwiglu ? a.w.N / 2 : a.w.N);
     static_assert(OW <= BST * BK, "output tile must fit the activation ring");
-    if (hh < BM / 128) {
+    if (ew < G::DQW) {
       const int q = warp & 3;          // TMEM lane quarter this warp may read
       const int rr = hh * 128 + 32 * q + lane;  // row of the block
       float rs = a.w.row_scale ? a.w.row_scale[static_cast<size_t>(blk) * BM + rr] : 1.f;
@@ -606,20 +611,21 @@ __global__ void __launch_bounds__(Cfg<BM_, BN_, BK_>::THREADS, 1)
       const int jcol = col0 + jl;
       Act* T = reinterpret_cast<Act*>(smem + OFF_B);  // [BN][OW] when staged
       constexpr int VPR = OW / 8;                      // 16-byte vectors per token row
-      const int et = tid - 128;                        // 0 .. BM-1
+      const int et = tid - 128;                        // 0 .. EPT-1
       if (staged && EPI == kEpiResidual) {
 #pragma unroll 8
-        for (int i = et; i < ntok * VPR; i += BM) {
+        for (int i = et; i < ntok * VPR; i += EPT) {
           const int tk = i / VPR, v = i % VPR;
           reinterpret_cast<uint4*>(T + tk * OW)[v] = *reinterpret_cast<const uint4*>(
               reinterpret_cast<const Act*>(a.out) + static_cast<size_t>(tok0 + tk) * a.out_ld +
               col0 + v * 8);
         }
       }
-      if (staged) named_bar_sync(1, BM);
+      if (staged) named_bar_sync(1, EPT);
       if (acc_ok) {
         tc_fence_after();
-        for (int cb = 0; cb < BN / 16; ++cb) {
+        constexpr int CBP = BN / 16 / NCP;  // 16-token column blocks per part
+        for (int cb = cp * CBP; cb < (cp + 1) * CBP; ++cb) {
           uint32_t v[16];
           tmem_ld16(tmem + (static_cast<uint32_t>(32 * q) << 16) + hh * BN + cb * 16, v);
           if constexpr (MMA2) {
@@ -689,9 +695,9 @@ __global__ void __launch_bounds__(Cfg<BM_, BN_, BK_>::THREADS, 1)
         }
       }
       if (staged) {
-        named_bar_sync(1, BM);
+        named_bar_sync(1, EPT);
 #pragma unroll 8
-        for (int i = et; i < ntok * VPR; i += BM) {
+        for (int i = et; i < ntok * VPR; i += EPT) {
           const int tk = i / VPR, v = i % VPR;
           *reinterpret_cast<uint4*>(reinterpret_cast<Act*>(a.out) +
                                     static_cast<size_t>(tok0 + tk) * a.out_ld + col0 + v * 8) =
