@@ -864,7 +864,8 @@ cudaError_t launch_fmt(const CUtensorMap& map, const GemmArgs& a, int epi, bool 
 
 template <typename Act>
 cudaError_t launch_act(const CUtensorMap& map, const GemmArgs& a, int epi, bool big, int ks,
-                       int bn, cudaStream_t s) {
+                       int bn, cudaStream_t s, const CUtensorMap* tail_map = nullptr,
+                       const GemmArgs* tail = nullptr) {
   const int prep_blocks = (a.M + kPrepRows - 1) / kPrepRows;
   if (a.M < 256) {  // few rows: a CTA per row keeps more of each row's loads in flight
     if (a.norm_w)
@@ -886,6 +887,11 @@ cudaError_t launch_act(const CUtensorMap& map, const GemmArgs& a, int epi, bool 
       case kFmtNvfp4G16: return launch_split<Act, kFmtNvfp4G16, 128>(map, a, epi, ks, bn, s);
       default: return cudaErrorInvalidValue;
     }
+  }
+  if (tail) {  // rows past the full waves of 256 x 256 tiles: 128 x 128 tiles (W8A16)
+    e = launch_fmt<Act, kFmtW8A16Row>(map, a, epi, true, 256, s);
+    if (e != cudaSuccess) return e;
+    return launch_fmt<Act, kFmtW8A16Row>(*tail_map, *tail, epi, false, 128, s);
   }
   switch (a.w.fmt) {
     case kFmtW8A16Row: return launch_fmt<Act, kFmtW8A16Row>(map, a, epi, big, bn, s);
@@ -939,6 +945,47 @@ cudaError_t gemm_w8a16_launch(const GemmArgs& a, int act, int epi, cudaStream_t 
           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
     return cudaErrorInvalidValue;
   const int ks = big ? 1 : k_splits(a, bn);
+  // Wave tail: when the 256 x 256 tiles fill W whole SM waves and leave a
+  // last wave less than half full, the weight blocks of that last wave run
+  // instead as 128 x 128 tiles in a second launch (a quarter of the work per
+  // CTA, so the tail costs about a third of a wave instead of a whole one).
+  // W8A16 only: its row scales and 1 KB chunks slice by tile.
+  int tail_blocks = 0;
+  if (big && a.w.fmt == kFmtW8A16Row && a.w.T % 16 == 0) {
+    const char* v = std::getenv("DIAL_B200_GEMM_TAIL");
+    if (!v || std::atoi(v) != 0) {
+      const long long nt = (a.M + 255) / 256, nb = a.w.T / 16, sms = sm_count();
+      const long long waves = nt * nb / sms, rem = nt * nb % sms;
+      const long long nb_full = waves * sms / nt;
+      // the tail's 128 x 128 tiles must fit one wave (measured: QKV at 2048
+      // tokens, whose tail would take 1.3 waves, went 126 -> 131 us; gate/up
+      // went 363 -> 342 us)
+      const long long tail_ctas = 2 * (nb - nb_full) * ((a.M + 127) / 128);
+      if (waves >= 1 && rem > 0 && 2 * rem <= sms && nb_full >= 1 && nb_full < nb &&
+          tail_ctas <= sms)
+        tail_blocks = static_cast<int>(nb - nb_full);
+    }
+  }
+  if (tail_blocks > 0) {
+    const int t0 = a.w.T - 16 * tail_blocks;  // first tile of the tail
+    GemmArgs head = a2, tail = a2;
+    head.w.T = t0;
+    head.w.N = 16 * t0;
+    tail.w.T = a.w.T - t0;
+    tail.w.N = 16 * tail.w.T;
+    tail.w.tiles = a.w.tiles + static_cast<size_t>(t0) * a.w.C * 1024;
+    tail.w.row_scale = a.w.row_scale + static_cast<size_t>(t0) * 16;
+    tail.out = reinterpret_cast<char*>(a.out) +
+               static_cast<size_t>(epi == kEpiSwiglu ? 8 * t0 : 16 * t0) * 2;  // 2-byte activations
+    CUtensorMap tmap;
+    const cuuint32_t tbox[2] = {64, 128};
+    if (enc(&tmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, a.xh, dims, strides, tbox, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return cudaErrorInvalidValue;
+    return act == 0 ? launch_act<__nv_bfloat16>(map, head, epi, true, 1, 256, s, &tmap, &tail)
+                    : launch_act<__half>(map, head, epi, true, 1, 256, s, &tmap, &tail);
+  }
   return act == 0 ? launch_act<__nv_bfloat16>(map, a2, epi, big, ks, bn, s)
                   : launch_act<__half>(map, a2, epi, big, ks, bn, s);
 }
