@@ -17,6 +17,7 @@
 // groups of 4 query heads take the token-split form instead: each warp reads
 // a quarter of every page and scores it for all 4 heads, so every K/V row is
 // loaded once per CTA rather than once per warp.
+#include <atomic>
 #include <cmath>
 
 #include "attention.h"
@@ -159,7 +160,7 @@ __global__ void kv_append_kernel(const AttnPrefillArgs a) {
   load4(qkv + (QH + kvh) * kD + lane * 4, k);
   load4(qkv + (QH + KVH + kvh) * kD + lane * 4, v);
   norm_rope<Act>(k, reinterpret_cast<const Act*>(a.k_norm_w), a.sh.eps, cos_row, sin_row, lane);
-  const int blk = a.block_table[pos / kPageTokens];
+  const int blk = checked_block(a, a.block_table[pos / kPageTokens]);
   const size_t off =
       ((static_cast<size_t>(blk) * KVH + kvh) * kPageTokens + (pos % kPageTokens)) * kD + lane * 4;
   store4(reinterpret_cast<Act*>(a.kv.k) + off, k);
@@ -186,7 +187,14 @@ constexpr auto cluster_kernel() {
 template <typename Act, int NREP, int CL, bool RING, bool TS = false>
 bool launch_cluster(const AttnDecodeArgs& a, cudaStream_t s, bool pdl, cudaError_t& err) {
   auto kern = cluster_kernel<Act, NREP, CL, RING, TS>();
-  static int usable = -1;  // per instantiation: checked once per process
+  // per instantiation and device: checked once (racing first calls compute
+  // the same answer); devices past the table are checked on every call
+  constexpr int kMaxDev = 64;
+  static std::atomic<int> usable_by_dev[kMaxDev];  // 0 unknown, 1 usable, 2 not
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::atomic<int>* slot = dev >= 0 && dev < kMaxDev ? &usable_by_dev[dev] : nullptr;
+  int usable = slot ? slot->load(std::memory_order_relaxed) : 0;
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(a.sh.kv_heads, a.splits, a.M);
   cfg.blockDim = dim3((NREP + (RING ? 1 : 0)) * 32);
@@ -200,8 +208,7 @@ bool launch_cluster(const AttnDecodeArgs& a, cudaStream_t s, bool pdl, cudaError
   attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[1].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
   cfg.attrs = attr;
-  if (usable < 0) {
-    usable = 0;
+  if (usable == 0) {
     bool ok = CL <= 8 ||
               cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) ==
                   cudaSuccess;
@@ -209,9 +216,10 @@ bool launch_cluster(const AttnDecodeArgs& a, cudaStream_t s, bool pdl, cudaError
     cfg.numAttrs = 1;
     ok = ok && cudaOccupancyMaxActiveClusters(&n, kern, &cfg) == cudaSuccess;
     if (!ok) cudaGetLastError();  // a refused size is an answer, not an error to keep
-    usable = ok && n >= 1 ? 1 : 0;
+    usable = ok && n >= 1 ? 1 : 2;
+    if (slot) slot->store(usable, std::memory_order_relaxed);
   }
-  if (!usable) return false;
+  if (usable != 1) return false;
   cfg.numAttrs = 2;
   err = cudaLaunchKernelEx(&cfg, kern, a);
   return true;

@@ -168,10 +168,10 @@ __global__ void __launch_bounds__(kMW * 32, mma_min_ctas<RING>()) attn_decode_mm
   __syncwarp();
 
   // lane l holds the block id of this warp's page (32 * window + l)
-  int bt_lane = lane < mine ? bt[pg_first + warp + kMW * lane] : 0;
+  int bt_lane = lane < mine ? checked_block(a, bt[pg_first + warp + kMW * lane]) : 0;
   auto issue = [&](int i) {  // warp-uniform i
     if (i > 0 && (i & 31) == 0)
-      bt_lane = i + lane < mine ? bt[pg_first + warp + kMW * (i + lane)] : 0;
+      bt_lane = i + lane < mine ? checked_block(a, bt[pg_first + warp + kMW * (i + lane)]) : 0;
     const int blk = __shfl_sync(0xffffffffu, bt_lane, i & 31);
     if (lane == 0) {
       uint8_t* dst = wring + (i % RING) * kSlotBytes;
@@ -186,7 +186,7 @@ __global__ void __launch_bounds__(kMW * 32, mma_min_ctas<RING>()) attn_decode_mm
   };
   int issued = 0;
   for (; issued < RING && issued < mine; ++issued) issue(issued);
-  const int blk_pos = fresh && warp == 0 ? bt[pos / kPageTokens] : 0;
+  const int blk_pos = fresh && warp == 0 ? checked_block(a, bt[pos / kPageTokens]) : 0;
 
   const Act* cos_row = reinterpret_cast<const Act*>(a.cos) + static_cast<size_t>(pos) * (kHeadDim / 2);
   const Act* sin_row = reinterpret_cast<const Act*>(a.sin) + static_cast<size_t>(pos) * (kHeadDim / 2);

@@ -22,6 +22,19 @@
 
 namespace dialb200 {
 
+// A block id read from a caller's block table: when the pool size is known
+// (num_blocks > 0) an id outside [0, num_blocks) records kStatusBadArgs and
+// reads (and appends to) page 0 instead, so a bad table cannot reach memory
+// outside the pools.
+template <typename Args>
+__device__ __forceinline__ int checked_block(const Args& a, int blk) {
+  if (a.num_blocks > 0 && static_cast<unsigned>(blk) >= static_cast<unsigned>(a.num_blocks)) {
+    set_status(a.status, kStatusBadArgs);
+    return 0;
+  }
+  return blk;
+}
+
 constexpr int kHeadDim = 128;
 
 template <typename Act>
@@ -201,7 +214,7 @@ __device__ void attn_ring_producer(const AttnDecodeArgs& a, int m, int kvh, int 
     int issued = 0, bt_lane = 0;
     bool ok = true;
     for (int pg = 0; pg < npages && ok; ++pg) {
-      if ((pg & 31) == 0) bt_lane = pg + lane < npages ? bt[pg_first + pg + lane] : 0;
+      if ((pg & 31) == 0) bt_lane = pg + lane < npages ? checked_block(a, bt[pg_first + pg + lane]) : 0;
       const int blk = __shfl_sync(0xffffffffu, bt_lane, pg & 31);
       if (lane == 0) {
         const int slot = pg % RING;
@@ -363,12 +376,11 @@ __device__ void attn_item(const AttnDecodeArgs& a, int m, int kvh, int split, in
 
   // Issue every load that does not depend on another one first: the block
   // id of the span's first page, q (and the new k/v), norm weights, cos/sin.
-  const int blk_first = (RING == 0 && active) ? bt[tok0 / kPageTokens] : 0;
+  const int blk_first = (RING == 0 && active) ? checked_block(a, bt[tok0 / kPageTokens]) : 0;
   // the other block ids of the span's first 32 pages (register form)
   const int bt_lane0 =
-      (RING == 0 && active && lane < npg) ? bt[pg_first + lane]
-          : 0;
-  const int blk_pos = do_kv ? bt[pos / kPageTokens] : 0;
+      (RING == 0 && active && lane < npg) ? checked_block(a, bt[pg_first + lane]) : 0;
+  const int blk_pos = do_kv ? checked_block(a, bt[pos / kPageTokens]) : 0;
   float q[4], kn[4] = {0.f, 0.f, 0.f, 0.f}, vn[4] = {0.f, 0.f, 0.f, 0.f};
   if (!early) {
     load4_cg(qkv + h * kHeadDim + lane * 4, q);
@@ -460,7 +472,7 @@ __device__ void attn_item(const AttnDecodeArgs& a, int m, int kvh, int split, in
   if constexpr (TSG == 0) {
     for (int b0 = tok0, pg = 0; b0 < tok1; b0 += kPageTokens, ++pg) {
       if (RING == 0 && (pg & 31) == 0 && pg > 0)
-        bt_lane = pg + lane < npg ? bt[pg_first + pg + lane] : 0;
+        bt_lane = pg + lane < npg ? checked_block(a, bt[pg_first + pg + lane]) : 0;
       if constexpr (RING > 0) {
         // the page's K/V rows (lane: dims 4*lane.. of every token) from the ring
         const int slot = pg % RING;
@@ -567,7 +579,7 @@ __device__ void attn_item(const AttnDecodeArgs& a, int m, int kvh, int split, in
     float mh = -INFINITY, lh = 0.f;
     for (int pg0 = 0; pg0 < npg; pg0 += TSG) {
       if (pg0 > 0) {
-        if ((pg0 & 31) == 0) bt_lane = pg0 + lane < npg ? bt[pg_first + pg0 + lane] : 0;
+        if ((pg0 & 31) == 0) bt_lane = pg0 + lane < npg ? checked_block(a, bt[pg_first + pg0 + lane]) : 0;
         load_group(pg0, bt_lane);
       }
 #pragma unroll

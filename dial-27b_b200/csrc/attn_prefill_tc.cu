@@ -245,7 +245,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int pg = 0; pg < kKB / kPageTokens; ++pg) {
           const int page = min(j * (kKB / kPageTokens) + pg, a.sh.max_blocks - 1);
-          rows[pg] = (a.block_table[page] * KVH + kvh) * kPageTokens;
+          rows[pg] = (checked_block(a, a.block_table[page]) * KVH + kvh) * kPageTokens;
         }
         if (j >= 2 && !mbar_wait(&kfree[b], static_cast<uint32_t>(j / 2 - 1) & 1u, a.status,
                                  kStatusAttnTc))

@@ -1106,7 +1106,9 @@ int dial_b200_attention_decode(const dial_b200_attn_shape* sh, const void* qkv, 
     }
     a.status = device_status_word();
     a.page_ring = 1;
-    a.tok_split = 1;
+    // token split as the engine: on by default, the cluster-merge variant for
+    // steps of up to 4 rows with DIAL_B200_ATTN_TOKSPLIT=2, off with 0
+    a.tok_split = g_tuning().attn_tok_split;
     DIAL_CHECK(sh->num_blocks >= 0, "num_blocks %d is negative", sh->num_blocks);
     a.num_blocks = sh->num_blocks;
     DIAL_CUDA(attn_decode_launch(a, sh->act, static_cast<cudaStream_t>(stream), false));

@@ -85,6 +85,50 @@ def test_attention_decode_tensor_core_form_matches_cuda_core_form(cuda):
     assert np.mean(d <= ulp(np.maximum(np.abs(cc), 1e-3), "bf16")) >= 0.99
 
 
+@pytest.mark.parametrize("dtype", ["bf16", "f16"])
+@pytest.mark.parametrize("splits", [8, 16])
+def test_attention_decode_cluster_token_split(cuda, monkeypatch, dtype, splits):
+    """The opt-in token split inside the cluster-merge form
+    (DIAL_B200_ATTN_TOKSPLIT=2: steps of up to 4 rows, groups of 4 query
+    heads, splits a multiple of the cluster) against the oracle, the appended
+    V, and a repeat call bit for bit."""
+    import dial_b200
+
+    monkeypatch.setenv("DIAL_B200_ATTN_TOKSPLIT", "2")
+    case = PagedCase(32, 8, [0, 200, 777, 1023], seed=40 + splits, dtype=dtype)
+    (a, b), dev, _ = run(case, cuda, splits, calls=2)
+    assert dial_b200.device_status() == 0
+    ref, _, vref = case.oracle()
+    assert_attn_close(a, ref, dtype)
+    np.testing.assert_array_equal(a, b)
+    _, v = case.new_kv(dev["k_pages"], dev["v_pages"])
+    np.testing.assert_array_equal(v, vref)
+
+
+@pytest.mark.parametrize("rows", [2, 8])
+def test_attention_decode_block_id_outside_pool(cuda, rows):
+    """With the pool size given, a block id outside [0, num_blocks) in the
+    caller's table records the bad-argument device status and reads page 0
+    instead (the page-ring form for 2 rows, the tensor-core form for 8); the
+    status clears."""
+    import dial_b200
+    import torch
+    from dial_b200 import attention as A
+
+    dial_b200.device_status(clear=True)
+    case = PagedCase(32, 8, [100, 300, 5, 64, 200, 17, 900, 40][:rows], seed=70 + rows)
+    nb = case.rows * case.max_blocks
+    sh = A.make_shape(case.QH, case.KVH, case.max_blocks, case.max_pos, case.eps, num_blocks=nb)
+    dev = case.device(cuda)
+    dev["block_table"][0, 3] = nb + 5  # a page row 0 reads (position 100)
+    dev["block_table"][1, 0] = -1
+    scratch = torch.zeros(max(A.scratch_bytes(sh, case.rows, 4), 16), dtype=torch.uint8, device=cuda)
+    A.attention_decode(sh, splits=4, scratch=scratch, **dev)
+    torch.cuda.synchronize()
+    assert dial_b200.device_status(clear=True) == 0x104  # bad arguments
+    assert dial_b200.device_status() == 0
+
+
 def test_attention_decode_repeat_calls_agree(cuda):
     """Scratch counters reset themselves: a second call (which re-appends the
     same K/V) reproduces the first bit for bit."""
