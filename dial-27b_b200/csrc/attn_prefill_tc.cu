@@ -138,11 +138,6 @@ __device__ __forceinline__ uint32_t max_bf16x2(uint32_t a, uint32_t b) {
   asm("max.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
   return r;
 }
-__device__ __forceinline__ float ex2_approx(float x) {
-  float r;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
-  return r;
-}
 
 __device__ __forceinline__ void st16_async(uint32_t taddr, const uint32_t* v) {
   asm volatile(
@@ -342,7 +337,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float scale = AT::round(1.0f / sqrtf(static_cast<float>(kHeadDim)));
     const uint32_t scale2 = pack_bf16x2(scale, scale);
     constexpr uint32_t kBf16NegInf = 0xFF80u;
-    constexpr float kLog2e = 1.4426950408889634f;
     const uint32_t lane_off = static_cast<uint32_t>(32 * quarter) << 16;
     float* xch = reinterpret_cast<float*>(smem + OFF_XCH);  // [parity][half][row]
     auto pair_sync = [&]() { named_bar_sync(1 + quarter, 64); };
@@ -404,15 +398,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       // exponentials through the hardware exp2: its relative error (about
       // 1e-6 here) is far below the bf16 rounding P receives
       const float alpha = (m_run == -INFINITY) ? 0.f : __expf(m_run - m_new);
-      // p = 2^(s log2 e - m log2 e); a fully masked row (m = -inf) gets p = 0
-      const float mb = (m_new == -INFINITY) ? 0.f : m_new * kLog2e;
+      // p = exp(s - m) and the row sum in key order, as the f32 form computed
+      // them (the packed scores change no value); a fully masked row
+      // (m = -inf) gets p = 0
+      const bool dead = m_new == -INFINITY;
       float psum = 0.f;
       uint32_t pp[KH / 2];
 #pragma unroll
       for (int i = 0; i < KH / 2; ++i) {
-        const float p0 = ex2_approx(fmaf(__uint_as_float(sp[i] << 16), kLog2e, -mb));
-        const float p1 = ex2_approx(fmaf(__uint_as_float(sp[i] & 0xFFFF0000u), kLog2e, -mb));
-        psum += p0 + p1;
+        const float p0 = dead ? 0.f : __expf(__uint_as_float(sp[i] << 16) - m_new);
+        const float p1 = dead ? 0.f : __expf(__uint_as_float(sp[i] & 0xFFFF0000u) - m_new);
+        psum += p0;
+        psum += p1;
         pp[i] = pack_bf16x2(p0, p1);
       }
       l_run = l_run * alpha + psum;
