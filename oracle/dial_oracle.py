@@ -20,6 +20,8 @@ relative to the reference project root, lisa301/DIAL-27B):
 * SwiGLU MLP ...................... dial-core/src/models/qwen3_vl/text.rs:816-820
 * pre-norm residual block ......... dial-core/src/models/qwen3_vl/text.rs:1636-1688
 * head + greedy argmax ............ dial-core/src/models/qwen3_vl/qwen3_vl.rs:138-143,2459-2498
+* Gated-DeltaNet mixer ............ dial-core/src/models/qwen3_8/text.rs:233-481
+* Qwen3.8 gated full attention .... dial-core/src/models/qwen3_8/text.rs:14-39,82-226
 
 Ops whose arithmetic lives in the third-party ``candle`` 0.11.0 crates
 (RMSNorm, RoPE, softmax, SiLU, matmul) are NOT pinned by any reference test.
@@ -817,3 +819,64 @@ def gdn_mixer(mixed, z, b, a, conv_w, dt_bias, a_log, norm_w, hk: int, hv: int, 
     zz = np.asarray(z, np.float32).reshape(S, hv, dv)
     out = gdn_gated_rms_norm(core, zz, norm_w, eps, act).reshape(S, hv * dv)
     return out, GdnState(conv_state, rec)
+
+
+# ---------------------------------------------------------------------------
+# f4: the Qwen3.8 full-attention layers (qwen3_8/text.rs:82-226)
+# ---------------------------------------------------------------------------
+
+
+def rope_partial(x, cos, sin, rotary_dim: int, act: str = "bf16") -> np.ndarray:
+    """rotate_partial (qwen3_8/text.rs:83-110): the half-split rotation on the
+    first ``rotary_dim`` dims of x [..., T, D] with tables [T, rotary_dim/2];
+    the remaining dims pass through unchanged."""
+    x = np.asarray(x, dtype=np.float32)
+    d = x.shape[-1]
+    rot = rope(x[..., :rotary_dim], cos, sin, act)
+    if rotary_dim == d:
+        return rot
+    return np.concatenate([rot, x[..., rotary_dim:]], axis=-1)
+
+
+@dataclass
+class FullAttnState:
+    """Per-session KV of one full-attention layer (llama3/cache.rs:117-160):
+    k, v [kv_heads, L, head_dim] in the activation dtype."""
+    k: np.ndarray
+    v: np.ndarray
+
+
+def gated_full_attention(q_gate, k, v, q_norm_w, k_norm_w, heads: int, kv_heads: int,
+                         head_dim: int, rotary_dim: int, cos, sin, eps: float, index_pos: int,
+                         state: FullAttnState | None, act: str = "bf16", attn_f32: bool = False):
+    """FullAttention::forward (qwen3_8/text.rs:146-226) between its input
+    projections and o_proj, for one session.
+
+    q_gate [S, heads * 2 * head_dim] holds [q | gate] per head (text.rs:155-166:
+    head h is columns [2 h d, 2 h d + d) for q and the next d for its gate);
+    k, v [S, kv_heads * head_dim]; cos / sin the tables' rows from index_pos
+    ([S, rotary_dim / 2]).  q and k take the zero-centred RMSNorm per head
+    (text.rs:26-38), the partial RoPE, the session's cache, grouped causal
+    attention in the activation dtype (f32 with ``attn_f32``) with the softmax
+    in f32, and the output is multiplied by sigmoid(gate) (text.rs:223).
+    Returns (out [S, heads * head_dim], the new FullAttnState)."""
+    S = np.asarray(q_gate).shape[0]
+    qg = np.asarray(q_gate, np.float32).reshape(S, heads, 2 * head_dim)
+    q = qg[:, :, :head_dim]
+    gate = qg[:, :, head_dim:].reshape(S, heads * head_dim)
+    q = zero_centered_rms_norm(q, q_norm_w, eps, act).transpose(1, 0, 2)  # [heads, S, d]
+    kk = zero_centered_rms_norm(np.asarray(k, np.float32).reshape(S, kv_heads, head_dim),
+                                k_norm_w, eps, act).transpose(1, 0, 2)
+    vv = act_round(np.asarray(v, np.float32).reshape(S, kv_heads, head_dim).transpose(1, 0, 2),
+                   act)
+    q = rope_partial(q, cos, sin, rotary_dim, act)
+    kk = rope_partial(kk, cos, sin, rotary_dim, act)
+    if state is not None and index_pos > 0:  # index_pos 0 starts the session over
+        kk = np.concatenate([state.k, kk], axis=1)
+        vv = np.concatenate([state.v, vv], axis=1)
+    cdt = "f32" if attn_f32 else act
+    out = attention(act_round(q, cdt), act_round(kk, cdt), act_round(vv, cdt), causal=True,
+                    act=cdt)
+    out = act_round(out, act).transpose(1, 0, 2).reshape(S, heads * head_dim)
+    out = act_round(out * sigmoid_act(gate, act), act)
+    return out, FullAttnState(kk, vv)
