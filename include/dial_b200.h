@@ -118,7 +118,10 @@ typedef struct {
   int32_t num_blocks; /* pages in each of k_pages / v_pages; with more than 4
                          rows a positive value selects the tensor-core form
                          (mma.sync over TMA-staged pages), 0 the CUDA-core
-                         forms; dial_b200_attention_decode_noalloc ignores it */
+                         forms.  When positive, a block id outside
+                         [0, num_blocks) records the bad-argument device
+                         status and page 0 is used instead.
+                         dial_b200_attention_decode_noalloc ignores it */
 } dial_b200_attn_shape;
 
 /* Bytes of scratch dial_b200_attention_decode needs for `rows` rows and
